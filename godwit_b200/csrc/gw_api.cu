@@ -1,0 +1,940 @@
+// gw_api.cu — the C-ABI declared in include/godwit_cuda.h.
+//
+// Host-side replacement for the reference's ExpertRunner / Router / the MoE
+// half of TransformerLayer.forward, and for ExpertCache + ModelReader: the
+// expert bank is resident in HBM, so a forward call never waits on storage.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/godwit_cuda.h"
+#include "gw_internal.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+gw_status fail(gw_status code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+gw_status cuda_fail(cudaError_t e, const char* what) {
+    return fail(e == cudaErrorMemoryAllocation ? GW_E_OOM : GW_E_CUDA, "%s: %s", what,
+                cudaGetErrorString(e));
+}
+
+#define GW_CUDA(call)                                        \
+    do {                                                     \
+        cudaError_t _e = (call);                             \
+        if (_e != cudaSuccess) return cuda_fail(_e, #call);  \
+    } while (0)
+
+// Device buffer that grows on demand and is released with its owner.
+struct DevBuf {
+    void* p = nullptr;
+    size_t n = 0;
+    cudaError_t ensure(size_t bytes) {
+        if (bytes <= n) return cudaSuccess;
+        if (p) cudaFree(p);
+        p = nullptr;
+        n = 0;
+        cudaError_t e = cudaMalloc(&p, bytes);
+        if (e == cudaSuccess) n = bytes;
+        return e;
+    }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        n = 0;
+    }
+};
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+}  // namespace
+
+struct gw_ctx {
+    int device = 0;
+    cudaStream_t own = nullptr;
+    cudaStream_t cur = nullptr;
+    std::recursive_mutex mu;
+    DevBuf work;        // MoE scratch (MoeWork)
+    DevBuf staging;     // inputs/outputs of the synchronous API
+    DevBuf gemv_x;      // f16 x + xmul for GEMV calls
+    int work_tcap = 0, work_H = 0, work_F = 0, work_E = 0, work_k = 0;
+    gw::MoeWork w{};
+    int64_t launches = 0;
+    // profiling (gw_profile_enable): event pairs per timed launch
+    bool prof = false;
+    struct Timed { int kind; cudaEvent_t a, b; int64_t units; };
+    std::vector<Timed> timed;
+    DevBuf nlog;              // nactive per profiled layer
+    int nlog_used = 0;
+    gw_profile acc{};
+};
+
+struct gw_bank {
+    gw_ctx* ctx = nullptr;
+    gw_bank_desc d{};
+    int e_local = 0;
+    std::vector<uint8_t*> layer_mem;  // [L] each E_local * stride bytes
+    uint16_t* router_w = nullptr;     // [L][E][H]
+    uint16_t* router_b = nullptr;     // [L][E]
+    int64_t bytes = 0;
+};
+
+namespace {
+
+struct CtxLock {
+    std::lock_guard<std::recursive_mutex> g;
+    explicit CtxLock(gw_ctx* c) : g(c->mu) {}
+};
+
+gw_status set_device(gw_ctx* c) {
+    GW_CUDA(cudaSetDevice(c->device));
+    return GW_OK;
+}
+
+gw::MoeDims dims_of(const gw_bank* b) {
+    gw::MoeDims m;
+    m.H = b->d.hidden;
+    m.F = b->d.intermediate;
+    m.E = b->d.experts;
+    m.k = b->d.top_k;
+    m.act = b->d.activation;
+    m.limit = b->d.limit;
+    m.alpha = b->d.alpha;
+    m.shard_rank = b->d.shard_rank;
+    m.shard_count = b->d.shard_count;
+    return m;
+}
+
+gw::LayerView layer_of(const gw_bank* b, int layer) {
+    gw::LayerView v;
+    v.base = b->layer_mem[layer];
+    v.stride = b->d.expert_stride;
+    for (int i = 0; i < 6; ++i) v.off[i] = b->d.section_offset[i];
+    v.router_w = b->router_w + (int64_t)layer * b->d.experts * b->d.hidden;
+    v.router_b = b->d.has_router_bias ? b->router_b + (int64_t)layer * b->d.experts : nullptr;
+    return v;
+}
+
+// Carves the MoE scratch for T tokens out of one allocation.
+gw_status ensure_work(gw_ctx* c, const gw_bank* b, int T) {
+    const int H = b->d.hidden, F = b->d.intermediate, E = b->d.experts, k = b->d.top_k;
+    if (c->w.x16 && T <= c->work_tcap && H <= c->work_H && F <= c->work_F && E <= c->work_E &&
+        k <= c->work_k)
+        return GW_OK;
+    const int tcap = std::max(T, std::max(c->work_tcap, 1));
+    const int Hc = std::max(H, c->work_H), Fc = std::max(F, c->work_F);
+    const int Ec = std::max(E, c->work_E), kc = std::max(k, c->work_k);
+    size_t off = 0;
+    auto take = [&](size_t bytes) { size_t o = off; off += align256(bytes); return o; };
+    const size_t o_x16 = take((size_t)tcap * Hc * 2);
+    const size_t o_xmul = take((size_t)tcap * 4);
+    const size_t o_xr = take((size_t)tcap * Hc * 2);
+    const size_t o_logits = take((size_t)tcap * Ec * 4);
+    const size_t o_experts = take((size_t)tcap * kc * 4);
+    const size_t o_weights = take((size_t)tcap * kc * 4);
+    const size_t o_counts = take((size_t)Ec * 4);
+    const size_t o_active = take((size_t)Ec * 4);
+    const size_t o_nactive = take(4);
+    const size_t o_lists = take((size_t)Ec * tcap * 4);
+    const size_t o_act = take((size_t)tcap * kc * Fc * 2);
+    const size_t o_ybuf = take((size_t)tcap * kc * Hc * 4);
+    const size_t o_done = take(4);
+    cudaError_t e = c->work.ensure(off);
+    if (e != cudaSuccess) return cuda_fail(e, "workspace allocation");
+    char* base = static_cast<char*>(c->work.p);
+    GW_CUDA(cudaMemsetAsync(base + o_done, 0, 4, c->cur));
+    GW_CUDA(cudaMemsetAsync(base + o_nactive, 0, 4, c->cur));
+    gw::MoeWork& w = c->w;
+    w.tcap = tcap;
+    w.x16 = reinterpret_cast<__half*>(base + o_x16);
+    w.xmul = reinterpret_cast<float*>(base + o_xmul);
+    w.xr = base + o_xr;
+    w.logits = reinterpret_cast<float*>(base + o_logits);
+    w.experts = reinterpret_cast<int32_t*>(base + o_experts);
+    w.weights = reinterpret_cast<float*>(base + o_weights);
+    w.counts = reinterpret_cast<int32_t*>(base + o_counts);
+    w.active = reinterpret_cast<int32_t*>(base + o_active);
+    w.nactive = reinterpret_cast<int32_t*>(base + o_nactive);
+    w.lists = reinterpret_cast<int32_t*>(base + o_lists);
+    w.act = reinterpret_cast<__half*>(base + o_act);
+    w.ybuf = reinterpret_cast<float*>(base + o_ybuf);
+    w.done = reinterpret_cast<unsigned*>(base + o_done);
+    c->work_tcap = tcap;
+    c->work_H = Hc;
+    c->work_F = Fc;
+    c->work_E = Ec;
+    c->work_k = kc;
+    return GW_OK;
+}
+
+gw_status count(gw_ctx* c, int n) {
+    if (n < 0) return cuda_fail(cudaGetLastError(), "kernel launch");
+    c->launches += n;
+    return GW_OK;
+}
+
+gw_status check_bank(gw_bank* b, int layer) {
+    if (!b || !b->ctx) return fail(GW_E_ARG, "null bank");
+    if (layer < 0 || layer >= b->d.layers)
+        return fail(GW_E_ARG, "layer %d out of range [0, %d)", layer, b->d.layers);
+    return GW_OK;
+}
+
+gw_status check_dtype(int x_dtype) {
+    if (x_dtype != GW_DTYPE_F16 && x_dtype != GW_DTYPE_BF16)
+        return fail(GW_E_ARG, "x_dtype %d is neither GW_DTYPE_F16 nor GW_DTYPE_BF16", x_dtype);
+    return GW_OK;
+}
+
+// Router + grouping (or grouping of a supplied routing), experts, combine —
+// the device half of one MoE layer.  x_dev is [T][H] in x_dtype, or the fp32
+// stream when x_dtype == kF32 (then rounded to round_dtype).
+gw_status moe_layer_device(gw_ctx* c, gw_bank* b, int layer, const void* x_dev, int x_dtype,
+                           int round_dtype, int T, const int32_t* experts_in,
+                           const float* weights_in, float* out, int accumulate) {
+    const gw::MoeDims d = dims_of(b);
+    const gw::LayerView L = layer_of(b, layer);
+    gw_status st = ensure_work(c, b, T);
+    if (st) return st;
+    gw::MoeWork& w = c->w;
+    const bool from_stream = (x_dtype == gw::kF32);
+    st = count(c, gw::launch_prep(x_dev, x_dtype, from_stream ? round_dtype : x_dtype, T, d.H,
+                                  from_stream ? w.xr : nullptr, w.x16, w.xmul, c->cur));
+    if (st) return st;
+    if (experts_in) {
+        st = count(c, gw::launch_group(d, experts_in, weights_in, T, w, c->cur));
+    } else {
+        const void* xr = from_stream ? w.xr : x_dev;
+        st = count(c, gw::launch_router(L, d, xr, from_stream ? round_dtype : x_dtype, T, w, c->cur));
+    }
+    if (st) return st;
+    cudaEvent_t e0 = nullptr, e1 = nullptr, e2 = nullptr;
+    if (c->prof) {
+        GW_CUDA(cudaEventCreate(&e0));
+        GW_CUDA(cudaEventCreate(&e1));
+        GW_CUDA(cudaEventCreate(&e2));
+        GW_CUDA(cudaEventRecord(e0, c->cur));
+    }
+    st = count(c, gw::launch_gateup(L, d, T, w, c->cur));
+    if (st) return st;
+    if (c->prof) GW_CUDA(cudaEventRecord(e1, c->cur));
+    st = count(c, gw::launch_down(L, d, T, w, c->cur));
+    if (st) return st;
+    if (c->prof) {
+        GW_CUDA(cudaEventRecord(e2, c->cur));
+        c->timed.push_back({0, e0, e1, 0});
+        c->timed.push_back({1, e1, e2, 0});
+        const size_t need = (size_t)(c->nlog_used + 1) * 4;
+        if (need > c->nlog.n) {
+            // grow by copying the recorded prefix
+            DevBuf bigger;
+            cudaError_t e = bigger.ensure(std::max<size_t>(need * 2, 4096));
+            if (e != cudaSuccess) return cuda_fail(e, "profile log allocation");
+            if (c->nlog_used)
+                GW_CUDA(cudaMemcpyAsync(bigger.p, c->nlog.p, (size_t)c->nlog_used * 4,
+                                        cudaMemcpyDeviceToDevice, c->cur));
+            GW_CUDA(cudaStreamSynchronize(c->cur));
+            c->nlog.release();
+            c->nlog = bigger;
+        }
+        GW_CUDA(cudaMemcpyAsync(static_cast<int32_t*>(c->nlog.p) + c->nlog_used, w.nactive, 4,
+                                cudaMemcpyDeviceToDevice, c->cur));
+        c->nlog_used += 1;
+    }
+    return count(c, gw::launch_combine(d, T, w, out, accumulate, c->cur));
+}
+
+}  // namespace
+
+// Staging area for the synchronous calls: carves consecutive device regions.
+namespace {
+size_t dtype_size(int) { return 2; }
+
+struct Stage {
+    gw_ctx* c;
+    size_t off = 0;
+    std::vector<std::pair<size_t, size_t>> regions;
+    explicit Stage(gw_ctx* cc) : c(cc) {}
+    size_t add(size_t bytes) {
+        const size_t o = off;
+        off += align256(bytes);
+        return o;
+    }
+    cudaError_t alloc() { return c->staging.ensure(std::max<size_t>(off, 256)); }
+    template <class T>
+    T* at(size_t o) { return reinterpret_cast<T*>(static_cast<char*>(c->staging.p) + o); }
+};
+}  // namespace
+
+// Destroys the recorded events (consecutive kernels share one) once each.
+static void drop_timed(gw_ctx* c) {
+    std::vector<cudaEvent_t> evs;
+    for (auto& t : c->timed) { evs.push_back(t.a); evs.push_back(t.b); }
+    std::sort(evs.begin(), evs.end());
+    evs.erase(std::unique(evs.begin(), evs.end()), evs.end());
+    for (auto e : evs) cudaEventDestroy(e);
+    c->timed.clear();
+}
+
+extern "C" {
+
+const char* gw_last_error(void) { return g_last_error.c_str(); }
+
+int32_t gw_version(void) { return 100; }
+
+gw_status gw_init(int32_t device, gw_ctx** out) {
+    if (!out) return fail(GW_E_ARG, "null output pointer");
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+    if (device < 0 || device >= n) return fail(GW_E_ARG, "device %d out of range [0, %d)", device, n);
+    GW_CUDA(cudaSetDevice(device));
+    cudaDeviceProp prop;
+    GW_CUDA(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10)
+        return fail(GW_E_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a",
+                    device, prop.major, prop.minor);
+    if (gw::configure_kernels() != 0) return cuda_fail(cudaGetLastError(), "kernel attributes");
+    gw_ctx* c = new gw_ctx();
+    c->device = device;
+    e = cudaStreamCreateWithFlags(&c->own, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        delete c;
+        return cuda_fail(e, "cudaStreamCreate");
+    }
+    c->cur = c->own;
+    *out = c;
+    g_last_error.clear();
+    return GW_OK;
+}
+
+gw_status gw_shutdown(gw_ctx* c) {
+    if (!c) return fail(GW_E_ARG, "null context");
+    {
+        CtxLock lk(c);
+        cudaSetDevice(c->device);
+        cudaStreamSynchronize(c->cur);
+        drop_timed(c);
+        c->nlog.release();
+        c->work.release();
+        c->staging.release();
+        c->gemv_x.release();
+        cudaStreamDestroy(c->own);
+    }
+    delete c;
+    return GW_OK;
+}
+
+gw_status gw_ctx_set_stream(gw_ctx* c, void* stream) {
+    if (!c) return fail(GW_E_ARG, "null context");
+    CtxLock lk(c);
+    c->cur = stream ? static_cast<cudaStream_t>(stream) : c->own;
+    return GW_OK;
+}
+
+gw_status gw_sync(gw_ctx* c) {
+    if (!c) return fail(GW_E_ARG, "null context");
+    CtxLock lk(c);
+    GW_CUDA(cudaSetDevice(c->device));
+    GW_CUDA(cudaStreamSynchronize(c->cur));
+    return GW_OK;
+}
+
+gw_status gw_profile_enable(gw_ctx* c, int32_t enable) {
+    if (!c) return fail(GW_E_ARG, "null context");
+    CtxLock lk(c);
+    GW_CUDA(cudaSetDevice(c->device));
+    GW_CUDA(cudaStreamSynchronize(c->cur));
+    drop_timed(c);
+    c->nlog_used = 0;
+    c->acc = gw_profile{};
+    c->prof = enable != 0;
+    return GW_OK;
+}
+
+gw_status gw_profile_read(gw_ctx* c, gw_profile* out) {
+    if (!c || !out) return fail(GW_E_ARG, "null argument");
+    CtxLock lk(c);
+    GW_CUDA(cudaSetDevice(c->device));
+    GW_CUDA(cudaStreamSynchronize(c->cur));
+    for (auto& t : c->timed) {
+        float ms = 0.f;
+        GW_CUDA(cudaEventElapsedTime(&ms, t.a, t.b));
+        if (t.kind == 0) { c->acc.gateup_launches++; c->acc.gateup_ms += ms; }
+        else if (t.kind == 1) { c->acc.down_launches++; c->acc.down_ms += ms; }
+        else { c->acc.gemv_launches++; c->acc.gemv_ms += ms; c->acc.gemv_matrices += t.units; }
+    }
+    drop_timed(c);
+    if (c->nlog_used) {
+        std::vector<int32_t> h(c->nlog_used);
+        GW_CUDA(cudaMemcpy(h.data(), c->nlog.p, h.size() * 4, cudaMemcpyDeviceToHost));
+        for (int32_t v : h) c->acc.expert_passes += v;
+        c->nlog_used = 0;
+    }
+    *out = c->acc;
+    return GW_OK;
+}
+
+gw_status gw_last_launch_count(gw_ctx* c, int64_t* out) {
+    if (!c || !out) return fail(GW_E_ARG, "null argument");
+    *out = c->launches;
+    return GW_OK;
+}
+
+gw_status gw_layout_default(int32_t hidden, int32_t intermediate, int32_t experts,
+                            int32_t layers, int32_t top_k, int32_t activation,
+                            gw_bank_desc* out) {
+    if (!out) return fail(GW_E_ARG, "null output");
+    if (hidden <= 0 || intermediate <= 0 || hidden % 32 || intermediate % 32)
+        return fail(GW_E_ARG, "hidden (%d) and intermediate (%d) must be positive multiples of 32",
+                    hidden, intermediate);
+    std::memset(out, 0, sizeof *out);
+    out->hidden = hidden;
+    out->intermediate = intermediate;
+    out->experts = experts;
+    out->layers = layers;
+    out->top_k = top_k;
+    out->activation = activation;
+    out->limit = 7.0f;
+    out->alpha = 1.702f;
+    out->has_router_bias = activation == GW_ACT_GPTOSS_CLAMPED ? 1 : 0;
+    out->shard_rank = 0;
+    out->shard_count = 1;
+    // ExpertLayout.init (Install/InstallLayout.swift:56-91): six sections, each
+    // starting on a 16 KiB page, stride rounded up to a page.
+    const int64_t page = 16384;
+    const int64_t gu_rows = 2LL * intermediate, dn_rows = hidden;
+    const int64_t sizes[6] = {
+        gu_rows * (hidden / 32) * 16, gu_rows * (hidden / 32),
+        dn_rows * (intermediate / 32) * 16, dn_rows * (intermediate / 32),
+        gu_rows * 2, dn_rows * 2};
+    int64_t cursor = 0;
+    for (int i = 0; i < 6; ++i) {
+        cursor = (cursor + page - 1) / page * page;
+        out->section_offset[i] = cursor;
+        out->section_length[i] = sizes[i];
+        cursor += sizes[i];
+    }
+    out->expert_stride = (cursor + page - 1) / page * page;
+    return GW_OK;
+}
+
+gw_status gw_bank_create(gw_ctx* c, const gw_bank_desc* d, gw_bank** out) {
+    if (!c || !d || !out) return fail(GW_E_ARG, "null argument");
+    if (d->hidden <= 0 || d->hidden % 32 || d->intermediate <= 0 || d->intermediate % 32)
+        return fail(GW_E_ARG, "hidden and intermediate must be positive multiples of 32");
+    if (d->experts <= 0 || d->experts > gw::kMaxExperts)
+        return fail(GW_E_ARG, "experts %d outside [1, %d]", d->experts, gw::kMaxExperts);
+    if (d->top_k <= 0 || d->top_k > gw::kMaxTopK || d->top_k > d->experts)
+        return fail(GW_E_ARG, "top_k %d outside [1, min(%d, experts)]", d->top_k, gw::kMaxTopK);
+    if (d->layers <= 0) return fail(GW_E_ARG, "layers must be positive");
+    if (d->activation != GW_ACT_GPTOSS_CLAMPED && d->activation != GW_ACT_SILU)
+        return fail(GW_E_ARG, "unknown activation %d", d->activation);
+    if (d->shard_count <= 0 || d->shard_rank < 0 || d->shard_rank >= d->shard_count)
+        return fail(GW_E_ARG, "bad shard %d of %d", d->shard_rank, d->shard_count);
+    const int64_t H = d->hidden, F = d->intermediate;
+    const int64_t need[6] = {2 * F * (H / 32) * 16, 2 * F * (H / 32), H * (F / 32) * 16,
+                             H * (F / 32), 2 * F * 2, H * 2};
+    for (int i = 0; i < 6; ++i) {
+        if (d->section_length[i] < need[i])
+            return fail(GW_E_ARG, "section %d holds %lld bytes, needs %lld", i,
+                        (long long)d->section_length[i], (long long)need[i]);
+        if (d->section_offset[i] < 0 || d->section_offset[i] + need[i] > d->expert_stride)
+            return fail(GW_E_ARG, "section %d does not fit in the %lld-byte stride", i,
+                        (long long)d->expert_stride);
+        if (d->section_offset[i] % 16)
+            return fail(GW_E_ARG, "section %d offset %lld is not 16-byte aligned", i,
+                        (long long)d->section_offset[i]);
+    }
+    if (d->expert_stride % 16) return fail(GW_E_ARG, "expert stride must be a multiple of 16");
+    CtxLock lk(c);
+    gw_status st = set_device(c);
+    if (st) return st;
+    gw_bank* b = new gw_bank();
+    b->ctx = c;
+    b->d = *d;
+    b->e_local = (d->experts - d->shard_rank + d->shard_count - 1) / d->shard_count;
+    const size_t per_layer = (size_t)b->e_local * d->expert_stride;
+    b->layer_mem.assign(d->layers, nullptr);
+    for (int l = 0; l < d->layers; ++l) {
+        cudaError_t e = cudaMalloc(&b->layer_mem[l], std::max<size_t>(per_layer, 256));
+        if (e != cudaSuccess) {
+            gw_bank_destroy(b);
+            return cuda_fail(e, "bank layer allocation");
+        }
+        b->bytes += per_layer;
+    }
+    const size_t rw = (size_t)d->layers * d->experts * d->hidden * 2;
+    const size_t rb = (size_t)d->layers * d->experts * 2;
+    cudaError_t e = cudaMalloc(&b->router_w, rw);
+    if (e == cudaSuccess) e = cudaMalloc(&b->router_b, rb);
+    if (e != cudaSuccess) {
+        gw_bank_destroy(b);
+        return cuda_fail(e, "router allocation");
+    }
+    e = cudaMemsetAsync(b->router_b, 0, rb, c->cur);
+    if (e == cudaSuccess) e = cudaMemsetAsync(b->router_w, 0, rw, c->cur);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->cur);
+    if (e != cudaSuccess) {
+        gw_bank_destroy(b);
+        return cuda_fail(e, "router initialisation");
+    }
+    b->bytes += rw + rb;
+    *out = b;
+    return GW_OK;
+}
+
+gw_status gw_bank_destroy(gw_bank* b) {
+    if (!b) return fail(GW_E_ARG, "null bank");
+    if (b->ctx) {
+        CtxLock lk(b->ctx);
+        cudaSetDevice(b->ctx->device);
+        cudaStreamSynchronize(b->ctx->cur);
+        for (uint8_t* p : b->layer_mem)
+            if (p) cudaFree(p);
+        if (b->router_w) cudaFree(b->router_w);
+        if (b->router_b) cudaFree(b->router_b);
+    }
+    delete b;
+    return GW_OK;
+}
+
+static gw_status expert_ptr(gw_bank* b, int layer, int expert, uint8_t** out) {
+    gw_status st = check_bank(b, layer);
+    if (st) return st;
+    if (expert < 0 || expert >= b->d.experts)
+        return fail(GW_E_ARG, "expert %d out of range [0, %d)", expert, b->d.experts);
+    if (expert % b->d.shard_count != b->d.shard_rank)
+        return fail(GW_E_ARG, "expert %d is not resident on shard %d of %d", expert,
+                    b->d.shard_rank, b->d.shard_count);
+    *out = b->layer_mem[layer] + (int64_t)(expert / b->d.shard_count) * b->d.expert_stride;
+    return GW_OK;
+}
+
+gw_status gw_bank_upload_expert(gw_bank* b, int32_t layer, int32_t expert, const void* bytes,
+                                size_t len) {
+    uint8_t* dst;
+    gw_status st = expert_ptr(b, layer, expert, &dst);
+    if (st) return st;
+    if (!bytes) return fail(GW_E_ARG, "null stride bytes");
+    if ((int64_t)len != b->d.expert_stride)
+        return fail(GW_E_ARG, "stride is %zu bytes, the bank expects %lld", len,
+                    (long long)b->d.expert_stride);
+    CtxLock lk(b->ctx);
+    if ((st = set_device(b->ctx))) return st;
+    GW_CUDA(cudaMemcpyAsync(dst, bytes, len, cudaMemcpyHostToDevice, b->ctx->cur));
+    GW_CUDA(cudaStreamSynchronize(b->ctx->cur));
+    return GW_OK;
+}
+
+gw_status gw_bank_download_expert(gw_bank* b, int32_t layer, int32_t expert, void* bytes,
+                                  size_t len) {
+    uint8_t* src;
+    gw_status st = expert_ptr(b, layer, expert, &src);
+    if (st) return st;
+    if (!bytes || (int64_t)len != b->d.expert_stride)
+        return fail(GW_E_ARG, "destination must hold exactly one stride");
+    CtxLock lk(b->ctx);
+    if ((st = set_device(b->ctx))) return st;
+    GW_CUDA(cudaMemcpyAsync(bytes, src, len, cudaMemcpyDeviceToHost, b->ctx->cur));
+    GW_CUDA(cudaStreamSynchronize(b->ctx->cur));
+    return GW_OK;
+}
+
+gw_status gw_bank_upload_router(gw_bank* b, int32_t layer, const uint16_t* w, const uint16_t* bias) {
+    gw_status st = check_bank(b, layer);
+    if (st) return st;
+    if (!w) return fail(GW_E_ARG, "null router weight");
+    CtxLock lk(b->ctx);
+    if ((st = set_device(b->ctx))) return st;
+    const size_t nw = (size_t)b->d.experts * b->d.hidden;
+    GW_CUDA(cudaMemcpyAsync(b->router_w + layer * nw, w, nw * 2, cudaMemcpyHostToDevice, b->ctx->cur));
+    uint16_t* bd = b->router_b + (size_t)layer * b->d.experts;
+    if (bias)
+        GW_CUDA(cudaMemcpyAsync(bd, bias, b->d.experts * 2, cudaMemcpyHostToDevice, b->ctx->cur));
+    else
+        GW_CUDA(cudaMemsetAsync(bd, 0, b->d.experts * 2, b->ctx->cur));
+    GW_CUDA(cudaStreamSynchronize(b->ctx->cur));
+    return GW_OK;
+}
+
+gw_status gw_bank_fill_synthetic(gw_bank* b, uint64_t seed) {
+    if (!b || !b->ctx) return fail(GW_E_ARG, "null bank");
+    CtxLock lk(b->ctx);
+    gw_ctx* c = b->ctx;
+    gw_status st = set_device(c);
+    if (st) return st;
+    const int kinds[6] = {gw::kFillCodes, gw::kFillScales, gw::kFillCodes, gw::kFillScales,
+                          gw::kFillBf16Normal, gw::kFillBf16Normal};
+    for (int l = 0; l < b->d.layers; ++l) {
+        for (int e = b->d.shard_rank; e < b->d.experts; e += b->d.shard_count) {
+            uint8_t* ex = b->layer_mem[l] + (int64_t)(e / b->d.shard_count) * b->d.expert_stride;
+            for (int s = 0; s < 6; ++s) {
+                const uint64_t key = gw::mix64(seed ^ gw::mix64(((uint64_t)l << 40) |
+                                                                ((uint64_t)e << 8) | (uint64_t)s));
+                int kind = kinds[s];
+                if (s >= 4 && b->d.activation == GW_ACT_SILU) kind = gw::kFillZero;
+                if ((st = count(c, gw::launch_fill_bytes(ex + b->d.section_offset[s],
+                                                         b->d.section_length[s], key, kind, c->cur))))
+                    return st;
+            }
+        }
+        const uint64_t kw = gw::mix64(seed ^ gw::mix64(((uint64_t)l << 40) | (0xFFFFull << 8) | 6u));
+        const uint64_t kb = gw::mix64(seed ^ gw::mix64(((uint64_t)l << 40) | (0xFFFFull << 8) | 7u));
+        const size_t nw = (size_t)b->d.experts * b->d.hidden;
+        if ((st = count(c, gw::launch_fill_bytes(reinterpret_cast<uint8_t*>(b->router_w + l * nw),
+                                                 (int64_t)nw * 2, kw, gw::kFillBf16Normal, c->cur))))
+            return st;
+        if ((st = count(c, gw::launch_fill_bytes(
+                 reinterpret_cast<uint8_t*>(b->router_b + (size_t)l * b->d.experts),
+                 (int64_t)b->d.experts * 2, kb,
+                 b->d.has_router_bias ? gw::kFillBf16Normal : gw::kFillZero, c->cur))))
+            return st;
+    }
+    GW_CUDA(cudaStreamSynchronize(c->cur));
+    return GW_OK;
+}
+
+gw_status gw_bank_bytes(gw_bank* b, int64_t* out) {
+    if (!b || !out) return fail(GW_E_ARG, "null argument");
+    *out = b->bytes;
+    return GW_OK;
+}
+
+// ---- device-pointer API ---------------------------------------------------
+
+gw_status gw_moe_forward_async(gw_ctx* c, gw_bank* b, int32_t layer, const void* x_dev,
+                               int32_t x_dtype, int32_t T, float* out_dev, int32_t* experts_dev,
+                               float* weights_dev) {
+    if (!c || !x_dev || !out_dev) return fail(GW_E_ARG, "null argument");
+    gw_status st = check_bank(b, layer);
+    if (st || (st = check_dtype(x_dtype))) return st;
+    if (T <= 0) return fail(GW_E_ARG, "T must be positive");
+    CtxLock lk(c);
+    if ((st = set_device(c))) return st;
+    st = moe_layer_device(c, b, layer, x_dev, x_dtype, x_dtype, T, nullptr, nullptr, out_dev, 0);
+    if (st) return st;
+    const size_t nk = (size_t)T * b->d.top_k;
+    if (experts_dev)
+        GW_CUDA(cudaMemcpyAsync(experts_dev, c->w.experts, nk * 4, cudaMemcpyDeviceToDevice, c->cur));
+    if (weights_dev)
+        GW_CUDA(cudaMemcpyAsync(weights_dev, c->w.weights, nk * 4, cudaMemcpyDeviceToDevice, c->cur));
+    return GW_OK;
+}
+
+gw_status gw_moe_stack_forward_async(gw_ctx* c, gw_bank* b, const void* x_dev, int32_t x_dtype,
+                                     int32_t T, float* stream_dev) {
+    if (!c || !x_dev || !stream_dev) return fail(GW_E_ARG, "null argument");
+    gw_status st = check_bank(b, 0);
+    if (st || (st = check_dtype(x_dtype))) return st;
+    if (T <= 0) return fail(GW_E_ARG, "T must be positive");
+    CtxLock lk(c);
+    if ((st = set_device(c))) return st;
+    const int64_t n = (int64_t)T * b->d.hidden;
+    // stream = x widened to fp32; then stream += moe_l(round(stream)) per layer
+    if ((st = count(c, gw::launch_widen(x_dev, x_dtype, stream_dev, n, c->cur)))) return st;
+    for (int l = 0; l < b->d.layers; ++l) {
+        const void* src = (l == 0) ? x_dev : static_cast<const void*>(stream_dev);
+        const int src_dtype = (l == 0) ? x_dtype : gw::kF32;
+        st = moe_layer_device(c, b, l, src, src_dtype, x_dtype, T, nullptr, nullptr, stream_dev, 1);
+        if (st) return st;
+    }
+    return GW_OK;
+}
+
+gw_status gw_moe_apply_async(gw_ctx* c, gw_bank* b, int32_t layer, const void* x_dev,
+                             int32_t x_dtype, int32_t T, const int32_t* experts_dev,
+                             const float* weights_dev, float* out_dev, int32_t accumulate) {
+    if (!c || !x_dev || !out_dev || !experts_dev || !weights_dev) return fail(GW_E_ARG, "null argument");
+    gw_status st = check_bank(b, layer);
+    if (st || (st = check_dtype(x_dtype))) return st;
+    if (T <= 0) return fail(GW_E_ARG, "T must be positive");
+    CtxLock lk(c);
+    if ((st = set_device(c))) return st;
+    return moe_layer_device(c, b, layer, x_dev, x_dtype, x_dtype, T, experts_dev, weights_dev,
+                            out_dev, accumulate ? 1 : 0);
+}
+
+gw_status gw_residual_round_async(gw_ctx* c, float* stream_dev, const float* delta_dev,
+                                  void* x_out_dev, int32_t x_dtype, int64_t n) {
+    if (!c || !stream_dev) return fail(GW_E_ARG, "null argument");
+    gw_status st;
+    if (x_out_dev && (st = check_dtype(x_dtype))) return st;
+    CtxLock lk(c);
+    if ((st = set_device(c))) return st;
+    return count(c, gw::launch_residual_round(stream_dev, delta_dev, x_out_dev, x_dtype, n, c->cur));
+}
+
+// GEMV over `count` matrices whose x is already staged as f16 + multiplier.
+static gw_status gemv_device(gw_ctx* c, int32_t count_m, const uint8_t* packed, int64_t ps,
+                             const uint8_t* scales, int64_t ss, const uint16_t* bias, int64_t bs,
+                             const void* x, int64_t x_stride, int32_t x_dtype, float* y,
+                             int64_t ys, int32_t rows, int32_t cols) {
+    const int nx = x_stride == 0 ? 1 : count_m;
+    const size_t xbytes = align256((size_t)nx * cols * 2);
+    cudaError_t e = c->gemv_x.ensure(xbytes + align256((size_t)nx * 4));
+    if (e != cudaSuccess) return cuda_fail(e, "GEMV staging allocation");
+    __half* x16 = static_cast<__half*>(c->gemv_x.p);
+    float* xmul = reinterpret_cast<float*>(static_cast<char*>(c->gemv_x.p) + xbytes);
+    gw_status st;
+    if (x_stride != 0 && x_stride != cols) {
+        for (int m = 0; m < count_m; ++m) {
+            const char* xm = static_cast<const char*>(x) + (size_t)m * x_stride * 2;
+            if ((st = count(c, gw::launch_prep(xm, x_dtype, x_dtype, 1, cols, nullptr,
+                                               x16 + (size_t)m * cols, xmul + m, c->cur))))
+                return st;
+        }
+    } else if ((st = count(c, gw::launch_prep(x, x_dtype, x_dtype, nx, cols, nullptr, x16, xmul,
+                                              c->cur)))) {
+        return st;
+    }
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (c->prof) {
+        GW_CUDA(cudaEventCreate(&e0));
+        GW_CUDA(cudaEventCreate(&e1));
+        GW_CUDA(cudaEventRecord(e0, c->cur));
+    }
+    st = count(c, gw::launch_gemv_batched(count_m, packed, ps, scales, ss, bias, bs, x16,
+                                          x_stride == 0 ? 0 : cols, xmul, y, ys, rows, cols,
+                                          c->cur));
+    if (st) return st;
+    if (c->prof) {
+        GW_CUDA(cudaEventRecord(e1, c->cur));
+        c->timed.push_back({2, e0, e1, count_m});
+    }
+    return GW_OK;
+}
+
+gw_status gw_mxfp4_gemv_batched_async(gw_ctx* c, int32_t count_m, const uint8_t* packed,
+                                      int64_t packed_stride, const uint8_t* scales,
+                                      int64_t scale_stride, const uint16_t* bias,
+                                      int64_t bias_stride, const void* x, int64_t x_stride,
+                                      int32_t x_dtype, float* y, int64_t y_stride, int32_t rows,
+                                      int32_t cols) {
+    if (!c || !packed || !scales || !x || !y) return fail(GW_E_ARG, "null argument");
+    gw_status st = check_dtype(x_dtype);
+    if (st) return st;
+    if (count_m <= 0 || rows <= 0 || cols <= 0 || cols % 32)
+        return fail(GW_E_ARG, "need count > 0, rows > 0 and cols a positive multiple of 32");
+    if (packed_stride % 16 || reinterpret_cast<uintptr_t>(packed) % 16)
+        return fail(GW_E_ARG, "packed matrices must start on 16-byte boundaries");
+    CtxLock lk(c);
+    if ((st = set_device(c))) return st;
+    return gemv_device(c, count_m, packed, packed_stride, scales, scale_stride, bias, bias_stride,
+                       x, x_stride, x_dtype, y, y_stride, rows, cols);
+}
+
+// ---- synchronous host-pointer API ------------------------------------------
+
+
+gw_status gw_mxfp4_gemv(gw_ctx* c, const uint8_t* packed, const uint8_t* scales,
+                        const uint16_t* bias, const void* x, int32_t x_dtype, float* y,
+                        int32_t rows, int32_t cols) {
+    if (!c || !packed || !scales || !x || !y) return fail(GW_E_ARG, "null argument");
+    gw_status st = check_dtype(x_dtype);
+    if (st) return st;
+    if (rows <= 0 || cols <= 0 || cols % 32)
+        return fail(GW_E_ARG, "rows must be positive and cols a positive multiple of 32 (got %d x %d)",
+                    rows, cols);
+    CtxLock lk(c);
+    if ((st = set_device(c))) return st;
+    Stage sg(c);
+    const size_t np = (size_t)rows * cols / 2, ns = (size_t)rows * cols / 32;
+    const size_t op = sg.add(np), os = sg.add(ns), ob = sg.add(bias ? rows * 2 : 0),
+                 ox = sg.add((size_t)cols * 2), oy = sg.add((size_t)rows * 4);
+    cudaError_t e = sg.alloc();
+    if (e != cudaSuccess) return cuda_fail(e, "staging allocation");
+    GW_CUDA(cudaMemcpyAsync(sg.at<uint8_t>(op), packed, np, cudaMemcpyHostToDevice, c->cur));
+    GW_CUDA(cudaMemcpyAsync(sg.at<uint8_t>(os), scales, ns, cudaMemcpyHostToDevice, c->cur));
+    if (bias) GW_CUDA(cudaMemcpyAsync(sg.at<uint8_t>(ob), bias, rows * 2, cudaMemcpyHostToDevice, c->cur));
+    GW_CUDA(cudaMemcpyAsync(sg.at<uint8_t>(ox), x, (size_t)cols * 2, cudaMemcpyHostToDevice, c->cur));
+    st = gemv_device(c, 1, sg.at<uint8_t>(op), 0, sg.at<uint8_t>(os), 0,
+                     bias ? sg.at<uint16_t>(ob) : nullptr, 0, sg.at<void>(ox), 0, x_dtype,
+                     sg.at<float>(oy), 0, rows, cols);
+    if (st) return st;
+    GW_CUDA(cudaMemcpyAsync(y, sg.at<float>(oy), (size_t)rows * 4, cudaMemcpyDeviceToHost, c->cur));
+    GW_CUDA(cudaStreamSynchronize(c->cur));
+    return GW_OK;
+}
+
+gw_status gw_mxfp4_dequant(gw_ctx* c, const uint8_t* packed, const uint8_t* scales, int32_t rows,
+                           int32_t cols, float* w_out) {
+    if (!c || !packed || !scales || !w_out) return fail(GW_E_ARG, "null argument");
+    if (rows <= 0 || cols <= 0 || cols % 32)
+        return fail(GW_E_ARG, "rows must be positive and cols a positive multiple of 32");
+    CtxLock lk(c);
+    gw_status st = set_device(c);
+    if (st) return st;
+    Stage sg(c);
+    const size_t np = (size_t)rows * cols / 2, ns = (size_t)rows * cols / 32,
+                 nw = (size_t)rows * cols * 4;
+    const size_t op = sg.add(np), os = sg.add(ns), ow = sg.add(nw);
+    cudaError_t e = sg.alloc();
+    if (e != cudaSuccess) return cuda_fail(e, "staging allocation");
+    GW_CUDA(cudaMemcpyAsync(sg.at<uint8_t>(op), packed, np, cudaMemcpyHostToDevice, c->cur));
+    GW_CUDA(cudaMemcpyAsync(sg.at<uint8_t>(os), scales, ns, cudaMemcpyHostToDevice, c->cur));
+    if ((st = count(c, gw::launch_dequant(sg.at<uint8_t>(op), sg.at<uint8_t>(os), rows, cols,
+                                          sg.at<float>(ow), c->cur))))
+        return st;
+    GW_CUDA(cudaMemcpyAsync(w_out, sg.at<float>(ow), nw, cudaMemcpyDeviceToHost, c->cur));
+    GW_CUDA(cudaStreamSynchronize(c->cur));
+    return GW_OK;
+}
+
+
+gw_status gw_router_logits(gw_ctx* c, gw_bank* b, int32_t layer, const void* x, int32_t x_dtype,
+                           int32_t T, float* logits) {
+    if (!c || !x || !logits) return fail(GW_E_ARG, "null argument");
+    gw_status st = check_bank(b, layer);
+    if (st || (st = check_dtype(x_dtype))) return st;
+    if (T <= 0) return fail(GW_E_ARG, "T must be positive");
+    CtxLock lk(c);
+    if ((st = set_device(c))) return st;
+    if ((st = ensure_work(c, b, T))) return st;
+    const size_t nx = (size_t)T * b->d.hidden * dtype_size(x_dtype);
+    Stage sg(c);
+    const size_t ox = sg.add(nx);
+    cudaError_t e = sg.alloc();
+    if (e != cudaSuccess) return cuda_fail(e, "staging allocation");
+    GW_CUDA(cudaMemcpyAsync(sg.at<void>(ox), x, nx, cudaMemcpyHostToDevice, c->cur));
+    const gw::MoeDims d = dims_of(b);
+    if ((st = count(c, gw::launch_router(layer_of(b, layer), d, sg.at<void>(ox), x_dtype, T, c->w,
+                                         c->cur))))
+        return st;
+    GW_CUDA(cudaMemcpyAsync(logits, c->w.logits, (size_t)T * d.E * 4, cudaMemcpyDeviceToHost, c->cur));
+    GW_CUDA(cudaStreamSynchronize(c->cur));
+    return GW_OK;
+}
+
+gw_status gw_route(gw_ctx* c, gw_bank* b, int32_t layer, const void* x, int32_t x_dtype, int32_t T,
+                   int32_t* experts_out, float* weights_out) {
+    if (!c || !x || !experts_out || !weights_out) return fail(GW_E_ARG, "null argument");
+    gw_status st = check_bank(b, layer);
+    if (st || (st = check_dtype(x_dtype))) return st;
+    if (T <= 0) return fail(GW_E_ARG, "T must be positive");
+    CtxLock lk(c);
+    if ((st = set_device(c))) return st;
+    if ((st = ensure_work(c, b, T))) return st;
+    const size_t nx = (size_t)T * b->d.hidden * dtype_size(x_dtype);
+    Stage sg(c);
+    const size_t ox = sg.add(nx);
+    cudaError_t e = sg.alloc();
+    if (e != cudaSuccess) return cuda_fail(e, "staging allocation");
+    GW_CUDA(cudaMemcpyAsync(sg.at<void>(ox), x, nx, cudaMemcpyHostToDevice, c->cur));
+    const gw::MoeDims d = dims_of(b);
+    if ((st = count(c, gw::launch_router(layer_of(b, layer), d, sg.at<void>(ox), x_dtype, T, c->w,
+                                         c->cur))))
+        return st;
+    const size_t nk = (size_t)T * d.k;
+    GW_CUDA(cudaMemcpyAsync(experts_out, c->w.experts, nk * 4, cudaMemcpyDeviceToHost, c->cur));
+    GW_CUDA(cudaMemcpyAsync(weights_out, c->w.weights, nk * 4, cudaMemcpyDeviceToHost, c->cur));
+    GW_CUDA(cudaStreamSynchronize(c->cur));
+    return GW_OK;
+}
+
+gw_status gw_moe_forward(gw_ctx* c, gw_bank* b, int32_t layer, const void* x, int32_t x_dtype,
+                         int32_t T, const int32_t* experts_in, const float* weights_in, float* out,
+                         int32_t* experts_out, float* weights_out) {
+    if (!c || !x || !out) return fail(GW_E_ARG, "null argument");
+    gw_status st = check_bank(b, layer);
+    if (st || (st = check_dtype(x_dtype))) return st;
+    if (T <= 0) return fail(GW_E_ARG, "T must be positive");
+    if ((experts_in == nullptr) != (weights_in == nullptr))
+        return fail(GW_E_ARG, "experts_in and weights_in must both be given or both be NULL");
+    const int k = b->d.top_k;
+    if (experts_in) {
+        for (int64_t i = 0; i < (int64_t)T * k; ++i)
+            if (experts_in[i] < 0 || experts_in[i] >= b->d.experts)
+                return fail(GW_E_ARG, "routing entry %lld names expert %d, outside [0, %d)",
+                            (long long)i, experts_in[i], b->d.experts);
+    }
+    CtxLock lk(c);
+    if ((st = set_device(c))) return st;
+    const size_t nx = (size_t)T * b->d.hidden * dtype_size(x_dtype), nk = (size_t)T * k,
+                 no = (size_t)T * b->d.hidden * 4;
+    Stage sg(c);
+    const size_t ox = sg.add(nx), oe = sg.add(nk * 4), ow = sg.add(nk * 4), oo = sg.add(no);
+    cudaError_t e = sg.alloc();
+    if (e != cudaSuccess) return cuda_fail(e, "staging allocation");
+    GW_CUDA(cudaMemcpyAsync(sg.at<void>(ox), x, nx, cudaMemcpyHostToDevice, c->cur));
+    if (experts_in) {
+        GW_CUDA(cudaMemcpyAsync(sg.at<int32_t>(oe), experts_in, nk * 4, cudaMemcpyHostToDevice, c->cur));
+        GW_CUDA(cudaMemcpyAsync(sg.at<float>(ow), weights_in, nk * 4, cudaMemcpyHostToDevice, c->cur));
+    }
+    st = moe_layer_device(c, b, layer, sg.at<void>(ox), x_dtype, x_dtype, T,
+                          experts_in ? sg.at<int32_t>(oe) : nullptr,
+                          experts_in ? sg.at<float>(ow) : nullptr, sg.at<float>(oo), 0);
+    if (st) return st;
+    GW_CUDA(cudaMemcpyAsync(out, sg.at<float>(oo), no, cudaMemcpyDeviceToHost, c->cur));
+    if (experts_out)
+        GW_CUDA(cudaMemcpyAsync(experts_out, c->w.experts, nk * 4, cudaMemcpyDeviceToHost, c->cur));
+    if (weights_out)
+        GW_CUDA(cudaMemcpyAsync(weights_out, c->w.weights, nk * 4, cudaMemcpyDeviceToHost, c->cur));
+    GW_CUDA(cudaStreamSynchronize(c->cur));
+    return GW_OK;
+}
+
+gw_status gw_expert_apply_batch(gw_ctx* c, gw_bank* b, int32_t layer, const void* x,
+                                int32_t x_dtype, int32_t n, const int32_t* experts,
+                                const float* weights, float* y) {
+    if (!c || !x || !y || (n > 0 && (!experts || !weights))) return fail(GW_E_ARG, "null argument");
+    gw_status st = check_bank(b, layer);
+    if (st || (st = check_dtype(x_dtype))) return st;
+    if (n < 0 || n > b->d.top_k)
+        return fail(GW_E_ARG, "expert count %d outside [0, top_k=%d]", n, b->d.top_k);
+    if (n == 0) {  // applyBatch returns zeros for an empty expert list
+        std::memset(y, 0, (size_t)b->d.hidden * 4);
+        return GW_OK;
+    }
+    // Pad the assignment to the bank's top-k with id -1 (skipped).
+    int32_t ex[gw::kMaxTopK];
+    float wt[gw::kMaxTopK];
+    for (int j = 0; j < b->d.top_k; ++j) {
+        ex[j] = j < n ? experts[j] : -1;
+        wt[j] = j < n ? weights[j] : 0.f;
+        if (j < n && (ex[j] < 0 || ex[j] >= b->d.experts))
+            return fail(GW_E_ARG, "expert %d out of range [0, %d)", ex[j], b->d.experts);
+        for (int i = 0; i < j && j < n; ++i)
+            if (ex[i] == ex[j]) return fail(GW_E_ARG, "expert %d listed twice", ex[j]);
+    }
+    CtxLock lk(c);
+    if ((st = set_device(c))) return st;
+    const size_t nx = (size_t)b->d.hidden * 2, nk = (size_t)b->d.top_k, no = (size_t)b->d.hidden * 4;
+    Stage sg(c);
+    const size_t ox = sg.add(nx), oe = sg.add(nk * 4), ow = sg.add(nk * 4), oo = sg.add(no);
+    cudaError_t e = sg.alloc();
+    if (e != cudaSuccess) return cuda_fail(e, "staging allocation");
+    GW_CUDA(cudaMemcpyAsync(sg.at<void>(ox), x, nx, cudaMemcpyHostToDevice, c->cur));
+    GW_CUDA(cudaMemcpyAsync(sg.at<int32_t>(oe), ex, nk * 4, cudaMemcpyHostToDevice, c->cur));
+    GW_CUDA(cudaMemcpyAsync(sg.at<float>(ow), wt, nk * 4, cudaMemcpyHostToDevice, c->cur));
+    st = moe_layer_device(c, b, layer, sg.at<void>(ox), x_dtype, x_dtype, 1, sg.at<int32_t>(oe),
+                          sg.at<float>(ow), sg.at<float>(oo), 0);
+    if (st) return st;
+    GW_CUDA(cudaMemcpyAsync(y, sg.at<float>(oo), no, cudaMemcpyDeviceToHost, c->cur));
+    GW_CUDA(cudaStreamSynchronize(c->cur));
+    return GW_OK;
+}
+
+gw_status gw_expert_apply(gw_ctx* c, gw_bank* b, int32_t layer, int32_t expert, const void* x,
+                          int32_t x_dtype, float* y) {
+    const float one = 1.0f;
+    return gw_expert_apply_batch(c, b, layer, x, x_dtype, 1, &expert, &one, y);
+}
+
+}  // extern "C"

@@ -1,0 +1,91 @@
+// gw_internal.h — launch-level interface between the C-ABI (gw_api.cu) and
+// the kernels (gw_kernels.cu).  Nothing here crosses the library boundary.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gw {
+
+constexpr int kMaxTopK = 16;
+constexpr int kMaxExperts = 256;
+constexpr int kTokTile = 8;       // tokens per MMA column block
+constexpr int kGemvWarps = 4;     // warps per GEMV CTA (one 16-row tile each)
+
+// Element types of activation inputs.  F32 is internal: the residual stream
+// that the stack forward rounds to the configured input type.
+enum Dtype : int { kF16 = 0, kBF16 = 1, kF32 = 2 };
+
+// One layer of the resident bank as the kernels see it.
+struct LayerView {
+    const uint8_t* base;       // local expert 0's stride
+    int64_t stride;            // bytes per expert stride
+    int64_t off[6];            // section offsets within a stride
+    const uint16_t* router_w;  // bf16 [E][H]
+    const uint16_t* router_b;  // bf16 [E] or nullptr
+};
+
+struct MoeDims {
+    int H, F, E, k, act;
+    float limit, alpha;
+    int shard_rank, shard_count;
+};
+
+// Scratch the MoE forward uses between kernels, sized for `tcap` tokens.
+struct MoeWork {
+    int tcap;
+    __half* x16;       // [tcap][H]   f16 expert input (bf16 inputs prescaled by 2^p)
+    float* xmul;       // [tcap]      2^-p, applied to the GEMV result
+    void* xr;          // [tcap][H]   router input in the compute dtype (stack mode)
+    float* logits;     // [tcap][E]
+    int32_t* experts;  // [tcap][k]
+    float* weights;    // [tcap][k]
+    int32_t* counts;   // [E]          tokens routed to each expert
+    int32_t* active;   // [E]          experts with at least one token (any order)
+    int32_t* nactive;  // [1]
+    int32_t* lists;    // [E][tcap]    slot ids (t*k + j) per expert
+    __half* act;       // [tcap*k][F]  activated gate_up output (f16, as the reference)
+    float* ybuf;       // [tcap*k][H]  routing-weighted down output per slot
+    unsigned* done;    // [1]          router completion counter (self-resetting)
+};
+
+// Host-side launchers; each returns the number of kernels it launched (or -1
+// on a launch error, left in cudaGetLastError()).
+int launch_prep(const void* src, int src_dtype, int round_dtype, int T, int H, void* xr_out,
+                __half* x16, float* xmul, cudaStream_t s);
+int launch_router(const LayerView& L, const MoeDims& d, const void* xr, int x_dtype, int T,
+                  const MoeWork& w, cudaStream_t s);
+int launch_group(const MoeDims& d, const int32_t* experts_in, const float* weights_in, int T,
+                 const MoeWork& w, cudaStream_t s);
+int launch_gateup(const LayerView& L, const MoeDims& d, int T, const MoeWork& w,
+                  cudaStream_t s);
+int launch_down(const LayerView& L, const MoeDims& d, int T, const MoeWork& w, cudaStream_t s);
+int launch_combine(const MoeDims& d, int T, const MoeWork& w, float* out, int accumulate,
+                   cudaStream_t s);
+int launch_gemv_batched(int count, const uint8_t* packed, int64_t packed_stride,
+                        const uint8_t* scales, int64_t scale_stride, const uint16_t* bias,
+                        int64_t bias_stride, const __half* x16, int64_t x_stride,
+                        const float* xmul, float* y, int64_t y_stride, int rows, int cols,
+                        cudaStream_t s);
+int launch_dequant(const uint8_t* packed, const uint8_t* scales, int rows, int cols, float* w,
+                   cudaStream_t s);
+int launch_fill_bytes(uint8_t* dst, int64_t n, uint64_t key, int kind, cudaStream_t s);
+int launch_residual_round(float* stream, const float* delta, void* x_out, int x_dtype,
+                          int64_t n, cudaStream_t s);
+int launch_widen(const void* x, int x_dtype, float* stream, int64_t n, cudaStream_t s);
+size_t gemv_smem_bytes(int cols);
+int configure_kernels();
+
+// Counter hash used by the synthetic bank generator (splitmix64 finaliser).
+__host__ __device__ inline uint64_t mix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+// Fill kinds for launch_fill_bytes.
+enum FillKind : int { kFillCodes = 0, kFillScales = 1, kFillBf16Normal = 2, kFillZero = 3 };
+
+}  // namespace gw

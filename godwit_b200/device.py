@@ -1,0 +1,70 @@
+"""Stream-ordered device-pointer API over torch tensors.
+
+PyTorch supplies device memory, the current stream and torch.distributed;
+every kernel that runs is this library's.  Tensors are passed as raw device
+pointers to the `_async` entry points of include/godwit_cuda.h on the
+current torch stream.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _abi
+from ._abi import GW_DTYPE_BF16, GW_DTYPE_F16, call
+from .runtime import Context, ExpertBank
+
+_TORCH_DTYPES = {torch.float16: GW_DTYPE_F16, torch.bfloat16: GW_DTYPE_BF16}
+
+
+def _p(t: torch.Tensor | None):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _TORCH_DTYPES[t.dtype]
+    except KeyError:
+        raise _abi.GodwitCUDAError(_abi.GW_E_ARG, f"unsupported activation dtype {t.dtype}") from None
+
+
+def bind_stream(ctx: Context, stream: torch.cuda.Stream | None = None) -> None:
+    s = stream or torch.cuda.current_stream(ctx.device)
+    ctx.set_stream(s.cuda_stream)
+
+
+def gemv_batched(ctx: Context, packed: torch.Tensor, scales: torch.Tensor, bias: torch.Tensor | None,
+                 x: torch.Tensor, y: torch.Tensor) -> None:
+    """packed [R, rows, cols/2] u8, scales [R, rows, cols/32] u8, bias [R, rows]
+    bf16 (as int16/uint16/bf16 storage) or None, x [R or 1, cols], y [R, rows] f32."""
+    R, rows, half = packed.shape
+    cols = half * 2
+    x_stride = 0 if x.shape[0] == 1 else x.stride(0)
+    call("gw_mxfp4_gemv_batched_async", ctx.handle, R, _p(packed), packed.stride(0), _p(scales),
+         scales.stride(0), _p(bias), 0 if bias is None else bias.stride(0), _p(x), x_stride,
+         dtype_code(x), _p(y), y.stride(0), rows, cols)
+
+
+def moe_forward(ctx: Context, bank: ExpertBank, layer: int, x: torch.Tensor, out: torch.Tensor,
+                experts: torch.Tensor | None = None, weights: torch.Tensor | None = None) -> None:
+    T = x.shape[0]
+    call("gw_moe_forward_async", ctx.handle, bank.handle, layer, _p(x), dtype_code(x), T, _p(out),
+         _p(experts), _p(weights))
+
+
+def moe_apply(ctx: Context, bank: ExpertBank, layer: int, x: torch.Tensor, experts: torch.Tensor,
+              weights: torch.Tensor, out: torch.Tensor, accumulate: bool = False) -> None:
+    call("gw_moe_apply_async", ctx.handle, bank.handle, layer, _p(x), dtype_code(x), x.shape[0],
+         _p(experts), _p(weights), _p(out), 1 if accumulate else 0)
+
+
+def moe_stack(ctx: Context, bank: ExpertBank, x: torch.Tensor, stream_out: torch.Tensor) -> None:
+    call("gw_moe_stack_forward_async", ctx.handle, bank.handle, _p(x), dtype_code(x), x.shape[0],
+         _p(stream_out))
+
+
+def residual_round(ctx: Context, stream: torch.Tensor, delta: torch.Tensor | None,
+                   x_out: torch.Tensor | None) -> None:
+    call("gw_residual_round_async", ctx.handle, _p(stream), _p(delta), _p(x_out),
+         GW_DTYPE_BF16 if x_out is None else dtype_code(x_out), stream.numel())

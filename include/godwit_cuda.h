@@ -1,0 +1,249 @@
+/*
+ * godwit_cuda.h — C-ABI of the B200 (sm_100a) MoE expert hot path.
+ *
+ * This is the boundary Godwit's Swift engine binds in place of its Metal
+ * expert kernels.  Every entry point takes plain pointers and sizes; nothing
+ * in these signatures is a CUDA, PyTorch or Swift type (streams travel as
+ * `void*`).  Each call returns a `gw_status`; on failure `gw_last_error()`
+ * returns a thread-local message describing it.
+ *
+ * Reference interfaces replaced (paths inside rayl15/Godwit):
+ *   - Router.logits / select / route        Sources/Godwit/Runtime/Router.swift:38-104
+ *   - ExpertRunner.apply                    Sources/Godwit/Runtime/ExpertRunner.swift:275-331
+ *   - ExpertRunner.applyBatch               Sources/Godwit/Runtime/ExpertRunner.swift:191-269
+ *   - ExpertRunner.applyAssignments + the MoE half of TransformerLayer.forward
+ *                                           Sources/Godwit/Runtime/ExpertRunner.swift:108-182,
+ *                                           Sources/Godwit/Runtime/TransformerLayer.swift:150-238
+ *   - ExpertCache / ModelReader.loadExpertStride (the slot cache becomes an
+ *     HBM-resident bank)                    Sources/Godwit/Runtime/ExpertCache.swift:180-274,
+ *                                           Sources/Godwit/Runtime/ModelReader.swift:73-76
+ *   - mxfp4_gemv (benchmark GEMV)           Sources/Godwit/Metal/Quant/dequant_gemv.metal:37-67
+ *   - MXFP4.decode (bit-exact dequant)      Sources/Godwit/Quant/MXFP4.swift:37-92
+ *
+ * Conventions:
+ *   - Synchronous calls (no `_async` suffix) take HOST pointers, copy inputs to
+ *     the device, run, copy results back and wait, mirroring the reference's
+ *     commit-and-wait `MetalContext.run` (Infrastructure/Metal/MetalContext.swift:149-155).
+ *   - `_async` calls take DEVICE pointers and are ordered on the context's
+ *     stream (see gw_ctx_set_stream); they do not synchronise.
+ *   - The library owns all device memory it allocates.  Host arrays are
+ *     borrowed for the duration of a call only.
+ *   - A gw_ctx is internally locked: calls on one context are serialised.
+ *   - Shape misuse that the reference catches with `precondition` is
+ *     reported as GW_E_ARG before any kernel launches.
+ */
+#ifndef GODWIT_CUDA_H
+#define GODWIT_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__) || defined(__clang__)
+#define GW_API __attribute__((visibility("default")))
+#else
+#define GW_API
+#endif
+
+typedef int32_t gw_status;
+
+#define GW_OK             0
+#define GW_E_ARG         (-1)  /* invalid argument (shape, index, null pointer) */
+#define GW_E_CUDA        (-2)  /* CUDA runtime error                            */
+#define GW_E_OOM         (-3)  /* device allocation failed                      */
+#define GW_E_TIMEOUT     (-4)  /* a bounded device-side wait gave up            */
+#define GW_E_STATE       (-5)  /* object used in the wrong state                */
+#define GW_E_UNSUPPORTED (-6)  /* configuration this build does not implement   */
+
+/* Activation input element type. The reference feeds Float16; the B200
+ * configs feed bfloat16.  Both are accepted everywhere `x_dtype` appears. */
+#define GW_DTYPE_F16   0
+#define GW_DTYPE_BF16  1
+
+/* Expert activation, mirroring FeedForwardActivation
+ * (Sources/Godwit/Model/ArchitectureSpec.swift:15-39). */
+#define GW_ACT_GPTOSS_CLAMPED 0  /* (clamp(up,±L)+1)·min(gate,L)·σ(α·min(gate,L)) — expert.metal:82-102 */
+#define GW_ACT_SILU           1  /* silu(gate)·up                                  — expert.metal:380-393 */
+
+/* Expert stride sections, in storage order (Install/InstallLayout.swift:18-25). */
+#define GW_SEC_GATE_UP_BLOCKS 0
+#define GW_SEC_GATE_UP_SCALES 1
+#define GW_SEC_DOWN_BLOCKS    2
+#define GW_SEC_DOWN_SCALES    3
+#define GW_SEC_GATE_UP_BIAS   4
+#define GW_SEC_DOWN_BIAS      5
+#define GW_SEC_COUNT          6
+
+typedef struct gw_ctx  gw_ctx;
+typedef struct gw_bank gw_bank;
+
+/* Bank description: the model dimensions of ArchitectureSpec plus the expert
+ * stride and section spans of GodwitManifest.expertStride / expertSections
+ * (Install/GodwitManifest.swift:47-51). */
+typedef struct gw_bank_desc {
+    int32_t hidden;            /* H: 2880 GPT-OSS, 2048 Qwen3                 */
+    int32_t intermediate;      /* F: 2880 GPT-OSS, 768 Qwen3                  */
+    int32_t experts;           /* E: routed experts per layer                 */
+    int32_t layers;            /* L: MoE layers held by the bank              */
+    int32_t top_k;             /* experts per token                           */
+    int32_t activation;        /* GW_ACT_*                                    */
+    float   limit;             /* swiglu_limit (7.0), GPT-OSS only            */
+    float   alpha;             /* sigmoid steepness (1.702), GPT-OSS only     */
+    int32_t has_router_bias;   /* 0: router bias treated as zeros             */
+    int32_t shard_rank;        /* expert e is resident iff e % shard_count == shard_rank */
+    int32_t shard_count;       /* 1 = the whole bank on this device           */
+    int32_t reserved0;
+    int64_t expert_stride;                  /* bytes per expert stride        */
+    int64_t section_offset[GW_SEC_COUNT];   /* byte offset within the stride  */
+    int64_t section_length[GW_SEC_COUNT];   /* byte length of the section     */
+} gw_bank_desc;
+
+/* ---- errors, version ---------------------------------------------------- */
+
+/* Thread-local description of the last failure on this thread ("" if none). */
+GW_API const char* gw_last_error(void);
+/* ABI version, major*10000 + minor*100 + patch. */
+GW_API int32_t gw_version(void);
+
+/* ---- context ------------------------------------------------------------ */
+
+/* Binds a context to CUDA device `device` (one process per GPU). */
+GW_API gw_status gw_init(int32_t device, gw_ctx** out);
+GW_API gw_status gw_shutdown(gw_ctx* ctx);
+/* Orders subsequent `_async` work on `cuda_stream` (a cudaStream_t; NULL =
+ * the context's own stream). */
+GW_API gw_status gw_ctx_set_stream(gw_ctx* ctx, void* cuda_stream);
+/* Waits for all work queued on the context's stream. */
+GW_API gw_status gw_sync(gw_ctx* ctx);
+
+/* ---- layout (ExpertLayout.init, Install/InstallLayout.swift:50-92) ------ */
+
+/* Fills `out` with the page-aligned stride and section spans the reference
+ * installer writes, plus the dimensions given. */
+GW_API gw_status gw_layout_default(int32_t hidden, int32_t intermediate, int32_t experts,
+                            int32_t layers, int32_t top_k, int32_t activation,
+                            gw_bank_desc* out);
+
+/* ---- HBM-resident expert bank ------------------------------------------- */
+
+GW_API gw_status gw_bank_create(gw_ctx* ctx, const gw_bank_desc* desc, gw_bank** out);
+GW_API gw_status gw_bank_destroy(gw_bank* bank);
+/* Copies one expert's stride — the bytes ModelReader.loadExpertStride returns
+ * (Runtime/ModelReader.swift:73-76) — into HBM.  `len` must equal the stride.
+ * Rejects experts not owned by this shard. */
+GW_API gw_status gw_bank_upload_expert(gw_bank* bank, int32_t layer, int32_t expert,
+                                const void* stride_bytes, size_t len);
+/* Router weight bf16 [E, H] and bias bf16 [E] (may be NULL: zeros), the
+ * tensors Router.logits binds (Runtime/Router.swift:38-66). */
+GW_API gw_status gw_bank_upload_router(gw_bank* bank, int32_t layer,
+                                const uint16_t* w_bf16, const uint16_t* b_bf16_or_null);
+/* Fills every resident expert and the router of every layer on the device
+ * with the seeded synthetic distribution (codes uniform 0..15, scales
+ * uniform 118..124, biases and router weights ~N(0, 0.02) in bf16).  The
+ * generator is a counter hash, reproducible on the host. */
+GW_API gw_status gw_bank_fill_synthetic(gw_bank* bank, uint64_t seed);
+/* Copies one resident expert's stride back to the host (`len` = stride). */
+GW_API gw_status gw_bank_download_expert(gw_bank* bank, int32_t layer, int32_t expert,
+                                  void* stride_bytes, size_t len);
+/* Bytes of HBM the bank holds. */
+GW_API gw_status gw_bank_bytes(gw_bank* bank, int64_t* out);
+
+/* ---- synchronous host-pointer API --------------------------------------- */
+
+/* Router.logits for T tokens: logits[T, E] (fp32). */
+GW_API gw_status gw_router_logits(gw_ctx* ctx, gw_bank* bank, int32_t layer,
+                           const void* x, int32_t x_dtype, int32_t T, float* logits);
+/* Router.route for T tokens: experts[T, k] (highest logit first, the
+ * selection-sort order of Router.select) and weights[T, k] (softmax over the
+ * k selected logits). */
+GW_API gw_status gw_route(gw_ctx* ctx, gw_bank* bank, int32_t layer,
+                   const void* x, int32_t x_dtype, int32_t T,
+                   int32_t* experts_out, float* weights_out);
+/* ExpertRunner.apply: one expert on one token, y[H] before routing weight. */
+GW_API gw_status gw_expert_apply(gw_ctx* ctx, gw_bank* bank, int32_t layer, int32_t expert,
+                          const void* x, int32_t x_dtype, float* y);
+/* ExpertRunner.applyBatch: y[H] = sum_i weights[i] * expert_i(x). */
+GW_API gw_status gw_expert_apply_batch(gw_ctx* ctx, gw_bank* bank, int32_t layer,
+                                const void* x, int32_t x_dtype, int32_t n,
+                                const int32_t* experts, const float* weights, float* y);
+/* MoE block for T tokens: out[T, H] = sum_k w[t,k] * expert_{e[t,k]}(x[t]).
+ * If `experts_in`/`weights_in` are NULL the router runs on the device first
+ * (and its decision is returned through `experts_out`/`weights_out` if those
+ * are non-NULL); otherwise the given routing [T, k] is applied, which is
+ * ExpertRunner.applyAssignments for the same assignment set. */
+GW_API gw_status gw_moe_forward(gw_ctx* ctx, gw_bank* bank, int32_t layer,
+                         const void* x, int32_t x_dtype, int32_t T,
+                         const int32_t* experts_in, const float* weights_in,
+                         float* out, int32_t* experts_out, float* weights_out);
+/* mxfp4_gemv / mxfp4_gemv_bias on raw reference-layout arrays:
+ * y[rows] = dequant(packed, scales) . x + bias.  cols % 32 == 0. */
+GW_API gw_status gw_mxfp4_gemv(gw_ctx* ctx, const uint8_t* packed, const uint8_t* scales,
+                        const uint16_t* bias_bf16_or_null, const void* x, int32_t x_dtype,
+                        float* y, int32_t rows, int32_t cols);
+/* MXFP4.decode on the device, fp32 out [rows, cols]; bit-exact with the
+ * reference's CPU decoder (0xFF scale -> NaN). */
+GW_API gw_status gw_mxfp4_dequant(gw_ctx* ctx, const uint8_t* packed, const uint8_t* scales,
+                           int32_t rows, int32_t cols, float* w_out);
+
+/* ---- stream-ordered device-pointer API ---------------------------------- */
+
+/* Batched GEMV over `count` independent matrices (device pointers, strides
+ * in elements of each array's type).  x_stride may be 0 to share one x. */
+GW_API gw_status gw_mxfp4_gemv_batched_async(gw_ctx* ctx, int32_t count,
+                                      const uint8_t* packed, int64_t packed_stride,
+                                      const uint8_t* scales, int64_t scale_stride,
+                                      const uint16_t* bias_or_null, int64_t bias_stride,
+                                      const void* x, int64_t x_stride, int32_t x_dtype,
+                                      float* y, int64_t y_stride,
+                                      int32_t rows, int32_t cols);
+/* One MoE layer on device memory: x_dev [T, H] (x_dtype), out_dev [T, H] fp32.
+ * experts_dev/weights_dev: optional [T, k] outputs of the routing decision. */
+GW_API gw_status gw_moe_forward_async(gw_ctx* ctx, gw_bank* bank, int32_t layer,
+                               const void* x_dev, int32_t x_dtype, int32_t T,
+                               float* out_dev, int32_t* experts_dev, float* weights_dev);
+/* The whole layer stack with residual chaining and identity norm:
+ * stream = x; for l: stream += moe_l(round_to_x_dtype(stream)).
+ * x_dev [T, H] (x_dtype) in, stream_dev [T, H] fp32 out. */
+GW_API gw_status gw_moe_stack_forward_async(gw_ctx* ctx, gw_bank* bank,
+                                     const void* x_dev, int32_t x_dtype, int32_t T,
+                                     float* stream_dev);
+/* Applies a given routing [T, k] (device arrays) to x_dev: out_dev (=, or +=
+ * when `accumulate` != 0) sum_k w * expert(x).  Expert ids this shard does
+ * not own, or outside [0, E), contribute nothing — the per-rank half of
+ * expert parallelism. */
+GW_API gw_status gw_moe_apply_async(gw_ctx* ctx, gw_bank* bank, int32_t layer,
+                             const void* x_dev, int32_t x_dtype, int32_t T,
+                             const int32_t* experts_dev, const float* weights_dev,
+                             float* out_dev, int32_t accumulate);
+/* stream_dev[i] += delta_dev[i] (delta may be NULL) and, if x_out_dev is not
+ * NULL, x_out_dev[i] = round(stream_dev[i]) in x_dtype; n elements.  The
+ * residual add of TransformerLayer.forward (Runtime/TransformerLayer.swift:232-238). */
+GW_API gw_status gw_residual_round_async(gw_ctx* ctx, float* stream_dev, const float* delta_dev,
+                                  void* x_out_dev, int32_t x_dtype, int64_t n);
+/* Kernel timing recorded with CUDA events on the context's stream around
+ * each expert GEMV launch while profiling is enabled. */
+typedef struct gw_profile {
+    int64_t gateup_launches;   /* gate_up GEMV + activation kernels           */
+    int64_t down_launches;     /* down GEMV + routing-weight kernels          */
+    int64_t gemv_launches;     /* plain batched GEMV kernels                  */
+    double  gateup_ms;         /* summed device time of those launches        */
+    double  down_ms;
+    double  gemv_ms;
+    int64_t expert_passes;     /* sum over profiled layers of experts streamed */
+    int64_t gemv_matrices;     /* matrices processed by the profiled GEMVs    */
+} gw_profile;
+/* Enables (1) or disables (0) kernel timing; enabling clears the counters. */
+GW_API gw_status gw_profile_enable(gw_ctx* ctx, int32_t enable);
+/* Waits for the stream, then reports the counters since profiling was enabled. */
+GW_API gw_status gw_profile_read(gw_ctx* ctx, gw_profile* out);
+/* Total number of this library's kernels launched through `ctx` so far. */
+GW_API gw_status gw_last_launch_count(gw_ctx* ctx, int64_t* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GODWIT_CUDA_H */

@@ -1,0 +1,372 @@
+/*
+ * mxfp4_oracle.c — CPU restatement of rayl15/Godwit's MoE expert hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the parity checker and the timed
+ * CPU baseline; it is never linked into, loaded by, or called from the
+ * product library (godwit_b200/libgodwit_cuda.so).  Only tests/, the smoke
+ * check in __graft_entry__.py and bench.py's CPU-baseline leg load it.
+ *
+ * Every function names the reference file:line whose arithmetic it restates
+ * (paths inside rayl15/Godwit).  The reference is Swift + Metal and cannot be
+ * compiled here, so this is a restatement in C with the same loop order and
+ * fp32 arithmetic, not a compiled copy.  It is pinned against the reference's
+ * own known-answer tests (Tests/GodwitTests/MXFP4Tests.swift,
+ * MXFP4EncodeTests.swift, DequantGEMVTests.swift) and against golden vectors
+ * produced by importing the reference's NumPy twin
+ * (Scripts/analysis/expert_reference.py) — see tests/golden/make_golden.py.
+ *
+ * Values of x are passed as float arrays holding exactly the f16 / bf16
+ * values the device sees; callers do the conversion.
+ */
+#include <math.h>
+#include <pthread.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define GWO_API __attribute__((visibility("default")))
+
+/* MXFP4.codebook — Sources/Godwit/Quant/MXFP4.swift:22-25 */
+static const float kCodebook[16] = {
+    0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f,
+    -0.0f, -0.5f, -1.0f, -1.5f, -2.0f, -3.0f, -4.0f, -6.0f,
+};
+
+/* MXFP4.thresholds — MXFP4.swift:106 (midpoints between magnitudes) */
+static const float kThresholds[7] = {0.25f, 0.75f, 1.25f, 1.75f, 2.5f, 3.5f, 5.0f};
+
+GWO_API float gwo_codebook(int code) { return kCodebook[code & 15]; }
+
+/* MXFP4.decodeScale — MXFP4.swift:37-40: NaN for 0xFF, else 2^(byte-127). */
+GWO_API float gwo_decode_scale(uint8_t byte) {
+    if (byte == 0xFF) return NAN;
+    return exp2f((float)((int)byte - 127));
+}
+
+/* MXFP4.decodeBlock / decode — MXFP4.swift:48-63, :69-92.
+ * Low nibble holds the even-indexed weight. */
+GWO_API void gwo_decode(const uint8_t* packed, const uint8_t* scales, int64_t block_count,
+                        float* out) {
+    for (int64_t b = 0; b < block_count; ++b) {
+        const float scale = gwo_decode_scale(scales[b]);
+        for (int i = 0; i < 16; ++i) {
+            const uint8_t byte = packed[b * 16 + i];
+            out[b * 32 + 2 * i] = kCodebook[byte & 0x0F] * scale;
+            out[b * 32 + 2 * i + 1] = kCodebook[byte >> 4] * scale;
+        }
+    }
+}
+
+/* MXFP4.scaleByte(forPeak:) — MXFP4.swift:118-123: ceil(log2(peak/6)). */
+GWO_API uint8_t gwo_scale_byte_for_peak(float peak) {
+    if (!(peak > 0.0f) || !isfinite(peak)) return 127;
+    const float exponent = ceilf(log2f(peak / 6.0f));
+    int v = (int)exponent + 127;
+    if (v == 255) v = 254;
+    if (v < 0) v = 0;
+    if (v > 255) v = 255;
+    return (uint8_t)v;
+}
+
+/* MXFP4.code(forMagnitude:) — MXFP4.swift:127-134. */
+GWO_API uint8_t gwo_code_for_magnitude(float value) {
+    uint8_t code = 0;
+    for (int i = 0; i < 7; ++i) {
+        if (value < kThresholds[i]) return code;
+        code += 1;
+    }
+    return code;
+}
+
+/* MXFP4.encodeBlock — MXFP4.swift:143-182; sign bit kept for values that
+ * round to zero (code 8 = -0). `count` <= 32, short blocks zero-padded. */
+static uint8_t encode_block(const float* w, int count, uint8_t* packed) {
+    float peak = 0.0f;
+    for (int i = 0; i < count; ++i)
+        if (isfinite(w[i])) peak = fmaxf(peak, fabsf(w[i]));
+    const uint8_t sb = gwo_scale_byte_for_peak(peak);
+    const float inverse = 1.0f / gwo_decode_scale(sb);
+    for (int j = 0; j < 16; ++j) {
+        uint8_t byte = 0;
+        for (int half = 0; half < 2; ++half) {
+            const int idx = 2 * j + half;
+            if (idx >= count) continue;
+            const float v = w[idx];
+            if (!isfinite(v)) continue;
+            uint8_t nib = gwo_code_for_magnitude(fabsf(v) * inverse);
+            if (signbit(v)) nib |= 0x08;
+            byte |= half == 0 ? nib : (uint8_t)(nib << 4);
+        }
+        packed[j] = byte;
+    }
+    return sb;
+}
+
+/* MXFP4.encode — MXFP4.swift:188-207.  Returns the block count. */
+GWO_API int64_t gwo_encode(const float* w, int64_t n, uint8_t* packed, uint8_t* scales) {
+    const int64_t blocks = (n + 31) / 32;
+    for (int64_t b = 0; b < blocks; ++b) {
+        const int64_t start = b * 32;
+        const int count = (int)((n - start) < 32 ? (n - start) : 32);
+        scales[b] = encode_block(w + start, count, packed + b * 16);
+    }
+    return blocks;
+}
+
+/* DequantGEMVBenchmark.referenceMXFP4 — Benchmark/DequantGEMVBenchmark.swift:100-120,
+ * same loop order: per block a 16-pair fp32 partial, then acc += partial*scale.
+ * Plus the bf16 bias of mxfp4_gemv_bias (Metal/MoE/expert.metal:46-77);
+ * `bias` may be NULL. */
+static void gemv_rows(const uint8_t* packed, const uint8_t* scales, const float* bias,
+                      const float* x, int64_t r0, int64_t r1, int64_t cols, float* y) {
+    const int64_t bpr = cols / 32;
+    for (int64_t row = r0; row < r1; ++row) {
+        float acc = 0.0f;
+        for (int64_t block = 0; block < bpr; ++block) {
+            const float scale = gwo_decode_scale(scales[row * bpr + block]);
+            const int64_t base = row * (cols / 2) + block * 16;
+            const int64_t col0 = block * 32;
+            float partial = 0.0f;
+            for (int i = 0; i < 16; ++i) {
+                const uint8_t byte = packed[base + i];
+                partial += kCodebook[byte & 0x0F] * x[col0 + i * 2];
+                partial += kCodebook[byte >> 4] * x[col0 + i * 2 + 1];
+            }
+            acc += partial * scale;
+        }
+        y[row] = bias ? acc + bias[row] : acc;
+    }
+}
+
+GWO_API void gwo_gemv(const uint8_t* packed, const uint8_t* scales, const float* bias,
+                      const float* x, int64_t rows, int64_t cols, float* y) {
+    gemv_rows(packed, scales, bias, x, 0, rows, cols, y);
+}
+
+/* Same GEMV with rows split over `threads` POSIX threads (the all-cores CPU
+ * baseline).  Results are identical to gwo_gemv: each row is one thread's. */
+typedef struct {
+    const uint8_t* packed; const uint8_t* scales; const float* bias; const float* x;
+    int64_t r0, r1, cols; float* y;
+} gemv_job;
+
+static void* gemv_worker(void* p) {
+    gemv_job* j = (gemv_job*)p;
+    gemv_rows(j->packed, j->scales, j->bias, j->x, j->r0, j->r1, j->cols, j->y);
+    return NULL;
+}
+
+GWO_API void gwo_gemv_mt(const uint8_t* packed, const uint8_t* scales, const float* bias,
+                         const float* x, int64_t rows, int64_t cols, float* y, int threads) {
+    if (threads <= 1) { gemv_rows(packed, scales, bias, x, 0, rows, cols, y); return; }
+    if (threads > 256) threads = 256;
+    pthread_t tid[256];
+    gemv_job jobs[256];
+    const int64_t per = (rows + threads - 1) / threads;
+    int started = 0;
+    for (int t = 0; t < threads; ++t) {
+        const int64_t r0 = t * per, r1 = (t + 1) * per < rows ? (t + 1) * per : rows;
+        if (r0 >= r1) break;
+        jobs[t] = (gemv_job){packed, scales, bias, x, r0, r1, cols, y};
+        if (pthread_create(&tid[t], NULL, gemv_worker, &jobs[t]) != 0) {
+            gemv_worker(&jobs[t]);
+            tid[t] = 0;
+        }
+        started = t + 1;
+    }
+    for (int t = 0; t < started; ++t)
+        if (tid[t]) pthread_join(tid[t], NULL);
+}
+
+static inline float bf16_to_f32(uint16_t v) {
+    uint32_t bits = (uint32_t)v << 16;
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+static inline float round_f16(float v) { return (float)(_Float16)v; }
+
+/* bf16_gemv_bias — Metal/MoE/router.metal:18-34: logits[e] = sum_c W[e,c]*x[c] + b[e],
+ * fp32 accumulation (sequential here). `b` may be NULL (zeros). */
+GWO_API void gwo_router_logits(const uint16_t* w, const uint16_t* b, const float* x,
+                               int64_t E, int64_t H, float* logits) {
+    for (int64_t e = 0; e < E; ++e) {
+        float acc = 0.0f;
+        for (int64_t c = 0; c < H; ++c) acc += bf16_to_f32(w[e * H + c]) * x[c];
+        logits[e] = acc + (b ? bf16_to_f32(b[e]) : 0.0f);
+    }
+}
+
+/* Router.select — Runtime/Router.swift:78-98: partial selection sort with a
+ * strict '>' and swaps (ties resolve by current array order), then softmax
+ * over the k selected logits only, max-subtracted. */
+GWO_API void gwo_router_select(const float* logits, int E, int k, int32_t* experts,
+                               float* weights) {
+    int order[4096];
+    for (int i = 0; i < E; ++i) order[i] = i;
+    for (int pos = 0; pos < k; ++pos) {
+        int best = pos;
+        for (int cand = pos + 1; cand < E; ++cand)
+            if (logits[order[cand]] > logits[order[best]]) best = cand;
+        const int tmp = order[pos];
+        order[pos] = order[best];
+        order[best] = tmp;
+    }
+    float peak = -INFINITY;
+    for (int j = 0; j < k; ++j) {
+        experts[j] = order[j];
+        if (j == 0 || logits[order[j]] > peak) peak = logits[order[j]];
+    }
+    float total = 0.0f;
+    for (int j = 0; j < k; ++j) {
+        weights[j] = expf(logits[order[j]] - peak);
+        total += weights[j];
+    }
+    for (int j = 0; j < k; ++j) weights[j] = weights[j] / total;
+}
+
+/* gptoss_expert_activation — Metal/MoE/expert.metal:82-102: interleaved
+ * gate/up, gate clamped above only, up clamped both ways, output rounded to
+ * half.  Returned as float holding the half value. */
+GWO_API void gwo_act_gptoss(const float* gate_up, int64_t F, float limit, float alpha,
+                            float* out) {
+    for (int64_t i = 0; i < F; ++i) {
+        float gate = gate_up[2 * i];
+        float up = gate_up[2 * i + 1];
+        gate = fminf(gate, limit);
+        up = fminf(fmaxf(up, -limit), limit);
+        const float glu = gate * (1.0f / (1.0f + expf(-alpha * gate)));
+        out[i] = round_f16((up + 1.0f) * glu);
+    }
+}
+
+/* expert_activation_swiglu — Metal/MoE/expert.metal:380-393. */
+GWO_API void gwo_act_silu(const float* gate_up, int64_t F, float* out) {
+    for (int64_t i = 0; i < F; ++i) {
+        const float gate = gate_up[2 * i];
+        const float up = gate_up[2 * i + 1];
+        const float silu = gate * (1.0f / (1.0f + expf(-gate)));
+        out[i] = round_f16(silu * up);
+    }
+}
+
+/* Section spans of one expert stride (GodwitManifest.expertSections). */
+typedef struct {
+    int64_t offset[6];
+} gwo_sections;
+
+/* ExpertRunner.apply — Runtime/ExpertRunner.swift:275-331: gate_up GEMV with
+ * bias -> activation -> down GEMV with bias.  `stride` is one expert's bytes
+ * in the installed layout; y[H]. `act` 0 = GPT-OSS clamped GLU, 1 = SiLU. */
+GWO_API void gwo_expert_apply(const uint8_t* stride, const int64_t* section_offset,
+                              int64_t H, int64_t F, int act, float limit, float alpha,
+                              const float* x, float* y) {
+    const uint8_t* gu_blocks = stride + section_offset[0];
+    const uint8_t* gu_scales = stride + section_offset[1];
+    const uint8_t* dn_blocks = stride + section_offset[2];
+    const uint8_t* dn_scales = stride + section_offset[3];
+    const uint16_t* gu_bias = (const uint16_t*)(stride + section_offset[4]);
+    const uint16_t* dn_bias = (const uint16_t*)(stride + section_offset[5]);
+    float* gub = (float*)malloc(sizeof(float) * 2 * F);
+    float* dnb = (float*)malloc(sizeof(float) * H);
+    float* gu = (float*)malloc(sizeof(float) * 2 * F);
+    float* a = (float*)malloc(sizeof(float) * F);
+    for (int64_t i = 0; i < 2 * F; ++i) gub[i] = bf16_to_f32(gu_bias[i]);
+    for (int64_t i = 0; i < H; ++i) dnb[i] = bf16_to_f32(dn_bias[i]);
+    gemv_rows(gu_blocks, gu_scales, gub, x, 0, 2 * F, H, gu);
+    if (act == 0) gwo_act_gptoss(gu, F, limit, alpha, a);
+    else gwo_act_silu(gu, F, a);
+    gemv_rows(dn_blocks, dn_scales, dnb, a, 0, H, F, y);
+    free(gub); free(dnb); free(gu); free(a);
+}
+
+/* The MoE half of TransformerLayer.forward — Runtime/TransformerLayer.swift:158-238
+ * with ExpertRunner.applyAssignments (ExpertRunner.swift:108-182) and
+ * expert_accumulate (expert.metal:107-116): route every token, then
+ * out[t] += w * expert(x[t]) in (token, rank) order.
+ *   strides:   pointer to expert 0 of this layer; expert e at strides + e*stride_bytes
+ *   router_w:  bf16 [E, H]; router_b: bf16 [E] or NULL
+ *   experts_in/weights_in: optional fixed routing [T, k] (NULL = route here)
+ *   experts_out/weights_out: routing decision [T, k] (may be NULL)
+ * x [T, H] floats holding the device's input values; out [T, H]. */
+GWO_API void gwo_moe_layer(const uint8_t* strides, int64_t stride_bytes,
+                           const int64_t* section_offset, int64_t H, int64_t F, int64_t E,
+                           int k, int act, float limit, float alpha,
+                           const uint16_t* router_w, const uint16_t* router_b,
+                           const float* x, int64_t T,
+                           const int32_t* experts_in, const float* weights_in,
+                           float* out, int32_t* experts_out, float* weights_out) {
+    float* logits = (float*)malloc(sizeof(float) * E);
+    float* y = (float*)malloc(sizeof(float) * H);
+    int32_t ex[64];
+    float wt[64];
+    for (int64_t t = 0; t < T; ++t) {
+        const float* xt = x + t * H;
+        if (experts_in) {
+            for (int j = 0; j < k; ++j) { ex[j] = experts_in[t * k + j]; wt[j] = weights_in[t * k + j]; }
+        } else {
+            gwo_router_logits(router_w, router_b, xt, E, H, logits);
+            gwo_router_select(logits, (int)E, k, ex, wt);
+        }
+        if (experts_out) for (int j = 0; j < k; ++j) experts_out[t * k + j] = ex[j];
+        if (weights_out) for (int j = 0; j < k; ++j) weights_out[t * k + j] = wt[j];
+        float* o = out + t * H;
+        for (int64_t i = 0; i < H; ++i) o[i] = 0.0f;
+        for (int j = 0; j < k; ++j) {
+            if (ex[j] < 0) continue;
+            gwo_expert_apply(strides + (int64_t)ex[j] * stride_bytes, section_offset, H, F,
+                             act, limit, alpha, xt, y);
+            for (int64_t i = 0; i < H; ++i) o[i] += y[i] * wt[j];
+        }
+    }
+    free(logits);
+    free(y);
+}
+
+/* Multi-threaded MoE layer over tokens (the all-cores CPU baseline of the
+ * layer configs); each token is one thread's work, so results equal
+ * gwo_moe_layer's. */
+typedef struct {
+    const uint8_t* strides; int64_t stride_bytes; const int64_t* so; int64_t H, F, E;
+    int k, act; float limit, alpha; const uint16_t* rw; const uint16_t* rb;
+    const float* x; int64_t t0, t1; float* out; int32_t* eo; float* wo;
+} moe_job;
+
+static void* moe_worker(void* p) {
+    moe_job* j = (moe_job*)p;
+    for (int64_t t = j->t0; t < j->t1; ++t)
+        gwo_moe_layer(j->strides, j->stride_bytes, j->so, j->H, j->F, j->E, j->k, j->act,
+                      j->limit, j->alpha, j->rw, j->rb, j->x + t * j->H, 1, NULL, NULL,
+                      j->out + t * j->H, j->eo ? j->eo + t * j->k : NULL,
+                      j->wo ? j->wo + t * j->k : NULL);
+    return NULL;
+}
+
+GWO_API void gwo_moe_layer_mt(const uint8_t* strides, int64_t stride_bytes,
+                              const int64_t* section_offset, int64_t H, int64_t F, int64_t E,
+                              int k, int act, float limit, float alpha,
+                              const uint16_t* router_w, const uint16_t* router_b,
+                              const float* x, int64_t T, float* out, int32_t* experts_out,
+                              float* weights_out, int threads) {
+    if (threads < 1) threads = 1;
+    if (threads > 256) threads = 256;
+    if (threads > T) threads = (int)T;
+    pthread_t tid[256];
+    moe_job jobs[256];
+    const int64_t per = (T + threads - 1) / threads;
+    int started = 0;
+    for (int t = 0; t < threads; ++t) {
+        const int64_t t0 = t * per, t1 = (t + 1) * per < T ? (t + 1) * per : T;
+        if (t0 >= t1) break;
+        jobs[t] = (moe_job){strides, stride_bytes, section_offset, H, F, E, k, act, limit, alpha,
+                            router_w, router_b, x, t0, t1, out, experts_out, weights_out};
+        if (pthread_create(&tid[t], NULL, moe_worker, &jobs[t]) != 0) {
+            moe_worker(&jobs[t]);
+            tid[t] = 0;
+        }
+        started = t + 1;
+    }
+    for (int t = 0; t < started; ++t)
+        if (tid[t]) pthread_join(tid[t], NULL);
+}

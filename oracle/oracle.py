@@ -1,0 +1,280 @@
+"""Python face of the CPU oracle — TEST INFRASTRUCTURE ONLY.
+
+Wraps oracle/liboracle.so (the C restatement in mxfp4_oracle.c) and adds an
+fp64 NumPy restatement of the MoE layer for the rel-L2 gate.  Only tests/,
+__graft_entry__.smoke() and bench.py's CPU-baseline leg import this module;
+the product library never calls it.
+
+Parity pinning: see tests/test_oracle_kats.py (the reference's own
+known-answer tests) and tests/golden/ (vectors produced by importing the
+reference's NumPy twin, Scripts/analysis/expert_reference.py).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB = os.path.join(HERE, "liboracle.so")
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB):
+            import subprocess
+            import sys
+            subprocess.run([sys.executable, os.path.join(os.path.dirname(HERE), "godwit_b200",
+                                                         "build.py")], check=True)
+        L = C.CDLL(LIB)
+        P, I64, F = C.c_void_p, C.c_int64, C.c_float
+        L.gwo_decode_scale.restype = F
+        L.gwo_decode_scale.argtypes = [C.c_uint8]
+        L.gwo_codebook.restype = F
+        L.gwo_codebook.argtypes = [C.c_int]
+        L.gwo_decode.argtypes = [P, P, I64, P]
+        L.gwo_scale_byte_for_peak.restype = C.c_uint8
+        L.gwo_scale_byte_for_peak.argtypes = [F]
+        L.gwo_code_for_magnitude.restype = C.c_uint8
+        L.gwo_code_for_magnitude.argtypes = [F]
+        L.gwo_encode.restype = I64
+        L.gwo_encode.argtypes = [P, I64, P, P]
+        L.gwo_gemv.argtypes = [P, P, P, P, I64, I64, P]
+        L.gwo_gemv_mt.argtypes = [P, P, P, P, I64, I64, P, C.c_int]
+        L.gwo_router_logits.argtypes = [P, P, P, I64, I64, P]
+        L.gwo_router_select.argtypes = [P, C.c_int, C.c_int, P, P]
+        L.gwo_act_gptoss.argtypes = [P, I64, F, F, P]
+        L.gwo_act_silu.argtypes = [P, I64, P]
+        L.gwo_expert_apply.argtypes = [P, P, I64, I64, C.c_int, F, F, P, P]
+        L.gwo_moe_layer.argtypes = [P, I64, P, I64, I64, I64, C.c_int, C.c_int, F, F, P, P, P,
+                                    I64, P, P, P, P, P]
+        L.gwo_moe_layer_mt.argtypes = [P, I64, P, I64, I64, I64, C.c_int, C.c_int, F, F, P, P,
+                                       P, I64, P, P, P, C.c_int]
+        _lib = L
+    return _lib
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+# ---- MXFP4 codec (MXFP4.swift) ---------------------------------------------
+
+def decode_scale(byte: int) -> float:
+    return lib().gwo_decode_scale(byte)
+
+
+def codebook() -> np.ndarray:
+    return np.array([lib().gwo_codebook(i) for i in range(16)], dtype=np.float32)
+
+
+def decode(packed: np.ndarray, scales: np.ndarray) -> np.ndarray:
+    packed = np.ascontiguousarray(packed, dtype=np.uint8)
+    scales = np.ascontiguousarray(scales, dtype=np.uint8)
+    nb = scales.size
+    out = np.empty(nb * 32, dtype=np.float32)
+    lib().gwo_decode(_p(packed), _p(scales), nb, _p(out))
+    return out
+
+
+def dequant(packed: np.ndarray, scales: np.ndarray) -> np.ndarray:
+    rows = packed.shape[0]
+    return decode(packed, scales).reshape(rows, -1)
+
+
+def scale_byte_for_peak(peak: float) -> int:
+    return lib().gwo_scale_byte_for_peak(peak)
+
+
+def code_for_magnitude(v: float) -> int:
+    return lib().gwo_code_for_magnitude(v)
+
+
+def encode(w: np.ndarray):
+    w = _f32(w).ravel()
+    nb = (w.size + 31) // 32
+    packed = np.zeros(nb * 16, dtype=np.uint8)
+    scales = np.zeros(nb, dtype=np.uint8)
+    lib().gwo_encode(_p(w), w.size, _p(packed), _p(scales))
+    return packed, scales
+
+
+# ---- GEMV / router / activation / expert / layer ----------------------------
+
+def gemv(packed, scales, x, bias=None, threads: int = 1) -> np.ndarray:
+    """referenceMXFP4 (+ bias): x and bias as float values."""
+    packed = np.ascontiguousarray(packed, dtype=np.uint8)
+    scales = np.ascontiguousarray(scales, dtype=np.uint8)
+    rows, cols = packed.shape[0], packed.shape[1] * 2
+    x = _f32(x)
+    b = None if bias is None else _f32(bias)
+    y = np.empty(rows, dtype=np.float32)
+    if threads > 1:
+        lib().gwo_gemv_mt(_p(packed), _p(scales), _p(b), _p(x), rows, cols, _p(y), threads)
+    else:
+        lib().gwo_gemv(_p(packed), _p(scales), _p(b), _p(x), rows, cols, _p(y))
+    return y
+
+
+def router_logits(w_bf16, b_bf16, x) -> np.ndarray:
+    w = np.ascontiguousarray(w_bf16, dtype=np.uint16)
+    E, H = w.shape
+    b = None if b_bf16 is None else np.ascontiguousarray(b_bf16, dtype=np.uint16)
+    out = np.empty(E, dtype=np.float32)
+    lib().gwo_router_logits(_p(w), _p(b), _p(_f32(x)), E, H, _p(out))
+    return out
+
+
+def router_select(logits, k: int):
+    lg = _f32(logits)
+    ex = np.empty(k, dtype=np.int32)
+    wt = np.empty(k, dtype=np.float32)
+    lib().gwo_router_select(_p(lg), lg.size, k, _p(ex), _p(wt))
+    return ex, wt
+
+
+def act_gptoss(gate_up, limit=7.0, alpha=1.702):
+    gu = _f32(gate_up)
+    out = np.empty(gu.size // 2, dtype=np.float32)
+    lib().gwo_act_gptoss(_p(gu), gu.size // 2, limit, alpha, _p(out))
+    return out
+
+
+def act_silu(gate_up):
+    gu = _f32(gate_up)
+    out = np.empty(gu.size // 2, dtype=np.float32)
+    lib().gwo_act_silu(_p(gu), gu.size // 2, _p(out))
+    return out
+
+
+def _offsets(spec) -> np.ndarray:
+    from godwit_b200._abi import SECTIONS
+    lay = spec.layout()
+    return np.array([lay.offsets[s] for s in SECTIONS], dtype=np.int64)
+
+
+def expert_apply(spec, stride: np.ndarray, x) -> np.ndarray:
+    so = _offsets(spec)
+    y = np.empty(spec.hidden, dtype=np.float32)
+    lib().gwo_expert_apply(_p(np.ascontiguousarray(stride, dtype=np.uint8)), _p(so), spec.hidden,
+                           spec.intermediate, spec.activation, spec.limit, spec.alpha,
+                           _p(_f32(x)), _p(y))
+    return y
+
+
+def moe_layer(spec, strides: np.ndarray, router_w, router_b, x, routing=None, threads: int = 1):
+    """strides: uint8 [E, stride] of one layer; x float [T, H].
+    Returns (out [T, H], experts [T, k], weights [T, k])."""
+    so = _offsets(spec)
+    strides = np.ascontiguousarray(strides, dtype=np.uint8)
+    x = _f32(x)
+    T = x.shape[0]
+    k = spec.top_k
+    out = np.empty((T, spec.hidden), dtype=np.float32)
+    ex = np.empty((T, k), dtype=np.int32)
+    wt = np.empty((T, k), dtype=np.float32)
+    rw = np.ascontiguousarray(router_w, dtype=np.uint16)
+    rb = None if router_b is None else np.ascontiguousarray(router_b, dtype=np.uint16)
+    if routing is None and threads > 1:
+        lib().gwo_moe_layer_mt(_p(strides), strides.shape[1], _p(so), spec.hidden,
+                               spec.intermediate, spec.experts, k, spec.activation, spec.limit,
+                               spec.alpha, _p(rw), _p(rb), _p(x), T, _p(out), _p(ex), _p(wt),
+                               threads)
+        return out, ex, wt
+    ein = win = None
+    if routing is not None:
+        ein = np.ascontiguousarray(routing[0], dtype=np.int32)
+        win = np.ascontiguousarray(routing[1], dtype=np.float32)
+    lib().gwo_moe_layer(_p(strides), strides.shape[1], _p(so), spec.hidden, spec.intermediate,
+                        spec.experts, k, spec.activation, spec.limit, spec.alpha, _p(rw), _p(rb),
+                        _p(x), T, _p(ein), _p(win), _p(out), _p(ex), _p(wt))
+    return out, ex, wt
+
+
+# ---- fp64 NumPy restatement (layer_reference.py:70-98, expert_reference.py:35-74) ----
+
+FP4 = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0,
+                -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0], dtype=np.float64)
+
+
+def dequant64(packed: np.ndarray, scales: np.ndarray) -> np.ndarray:
+    rows = packed.shape[0]
+    nb = scales.shape[1]
+    blocks = packed.reshape(rows, nb, 16)
+    out = np.empty((rows, nb, 32), dtype=np.float64)
+    out[:, :, 0::2] = FP4[blocks & 0x0F]
+    out[:, :, 1::2] = FP4[blocks >> 4]
+    out *= np.exp2(scales.astype(np.float64) - 127.0)[:, :, None]
+    return out.reshape(rows, nb * 32)
+
+
+def expert_sections(spec, stride: np.ndarray):
+    from godwit_b200.synth import bf16_bits_to_f32
+    lay = spec.layout()
+    H, F = spec.hidden, spec.intermediate
+
+    def sec(name):
+        o = lay.offsets[name]
+        return stride[o:o + lay.sizes[name]]
+
+    gu = dequant64(sec("gate_up_blocks").reshape(2 * F, H // 2), sec("gate_up_scales").reshape(2 * F, H // 32))
+    dn = dequant64(sec("down_blocks").reshape(H, F // 2), sec("down_scales").reshape(H, F // 32))
+    gb = bf16_bits_to_f32(sec("gate_up_bias").view(np.uint16)).astype(np.float64)
+    db = bf16_bits_to_f32(sec("down_bias").view(np.uint16)).astype(np.float64)
+    return gu, gb, dn, db
+
+
+def expert64(spec, stride: np.ndarray, x: np.ndarray, round_act: bool = True, cache=None) -> np.ndarray:
+    gu, gb, dn, db = cache if cache is not None else expert_sections(spec, stride)
+    g = gu @ np.asarray(x, np.float64) + gb
+    gate, up = g[0::2], g[1::2]
+    if spec.activation == 0:
+        gate = np.minimum(gate, spec.limit)
+        up = np.clip(up, -spec.limit, spec.limit)
+        a = (up + 1.0) * (gate / (1.0 + np.exp(-spec.alpha * gate)))
+    else:
+        a = (gate / (1.0 + np.exp(-gate))) * up
+    if round_act:  # the reference stores the activation as half (expert.metal:101)
+        a = a.astype(np.float16).astype(np.float64)
+    return dn @ a + db
+
+
+def moe_layer64(spec, strides: np.ndarray, x: np.ndarray, experts: np.ndarray,
+                weights: np.ndarray, round_act: bool = True) -> np.ndarray:
+    """fp64 layer for a given routing (selection is checked separately),
+    expert-major so each expert is dequantised once."""
+    T = x.shape[0]
+    x = np.asarray(x, np.float64)
+    out = np.zeros((T, spec.hidden), dtype=np.float64)
+    for e in np.unique(experts):
+        if e < 0:
+            continue
+        gu, gb, dn, db = expert_sections(spec, strides[int(e)])
+        tt, jj = np.nonzero(experts == e)
+        g = x[tt] @ gu.T + gb
+        gate, up = g[:, 0::2], g[:, 1::2]
+        if spec.activation == 0:
+            gate = np.minimum(gate, spec.limit)
+            up = np.clip(up, -spec.limit, spec.limit)
+            a = (up + 1.0) * (gate / (1.0 + np.exp(-spec.alpha * gate)))
+        else:
+            a = (gate / (1.0 + np.exp(-gate))) * up
+        if round_act:
+            a = a.astype(np.float16).astype(np.float64)
+        y = a @ dn.T + db
+        np.add.at(out, tt, y * np.asarray(weights, np.float64)[tt, jj][:, None])
+    return out
+
+
+def rel_l2(a, b) -> float:
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-300))
