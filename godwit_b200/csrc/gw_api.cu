@@ -859,10 +859,15 @@ gw_status gw_moe_forward(gw_ctx* c, gw_bank* b, int32_t layer, const void* x, in
         return fail(GW_E_ARG, "experts_in and weights_in must both be given or both be NULL");
     const int k = b->d.top_k;
     if (experts_in) {
-        for (int64_t i = 0; i < (int64_t)T * k; ++i)
+        for (int64_t i = 0; i < (int64_t)T * k; ++i) {
             if (experts_in[i] < 0 || experts_in[i] >= b->d.experts)
                 return fail(GW_E_ARG, "routing entry %lld names expert %d, outside [0, %d)",
                             (long long)i, experts_in[i], b->d.experts);
+            for (int64_t j = i - i % k; j < i; ++j)
+                if (experts_in[j] == experts_in[i])
+                    return fail(GW_E_ARG, "token %lld lists expert %d twice", (long long)(i / k),
+                                experts_in[i]);
+        }
     }
     CtxLock lk(c);
     if ((st = set_device(c))) return st;

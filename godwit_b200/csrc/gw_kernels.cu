@@ -156,6 +156,7 @@ __device__ void select_topk_warp(const float* __restrict__ logits, int E, int k,
 __device__ __forceinline__ void group_slot(const MoeDims& d, const MoeWork& w, int e, int slot) {
     if (e < 0 || e >= d.E || (e % d.shard_count) != d.shard_rank) return;
     const int pos = atomicAdd(w.counts + e, 1);
+    if (pos >= w.tcap) return;  // a malformed routing listing an expert twice for a token
     if (pos == 0) {
         const int a = atomicAdd(w.nactive, 1);
         w.active[a] = e;
@@ -289,7 +290,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) k_gateup(LayerView L, MoeDims
     const int a = blockIdx.x;
     if (a >= *w.nactive) return;
     const int e = w.active[a];
-    const int cnt = w.counts[e];
+    const int cnt = min(w.counts[e], w.tcap);
     const int* list = w.lists + (int64_t)e * w.tcap;
     const uint8_t* ex = L.base + (int64_t)(e / d.shard_count) * L.stride;
     const uint8_t* packed = ex + L.off[0];
@@ -343,7 +344,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) k_down(LayerView L, MoeDims d
     const int a = blockIdx.x;
     if (a >= *w.nactive) return;
     const int e = w.active[a];
-    const int cnt = w.counts[e];
+    const int cnt = min(w.counts[e], w.tcap);
     const int* list = w.lists + (int64_t)e * w.tcap;
     const uint8_t* ex = L.base + (int64_t)(e / d.shard_count) * L.stride;
     const uint8_t* packed = ex + L.off[2];
