@@ -113,44 +113,67 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # CPU reference leg (the oracle port of the reference's Swift CPU path)
 
-def cpu_reference_sample(spec, T_sample: int, threads: int, budget_s: float = 12.0):
-    """Times the oracle MoE layer on host cores for a bounded token sample of
-    layer 0 (weights generated on the host by the same counter hash as the
-    device bank).  Returns (tokens/s through the whole stack, sample text)."""
-    import numpy as np
+class CpuReference:
+    """The oracle MoE layer (C restatement of the reference's CPU path) on the
+    host cores, for a bounded token sample of layer 0.  The weights are made
+    on the host by the same counter hash as the device bank's, so the sample
+    computes the workload's own layer."""
 
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as O
-    from godwit_b200 import synth
+    def __init__(self, spec, threads: int, max_tokens: int = 2048):
+        import numpy as np
 
-    rng = np.random.default_rng(SEED)
-    x = synth.as_f32(synth.make_hidden(rng, T_sample, spec.hidden, "bf16"), "bf16")
-    rw, rb = synth.hash_router(spec, SEED, 0)
-    rb_arg = rb if spec.router_bias else None
-    needed = set()
-    for t in range(T_sample):
-        e, _ = O.router_select(O.router_logits(rw, rb_arg, x[t]), spec.top_k)
-        needed.update(int(v) for v in e)
-    lay = spec.layout()
-    strides = np.zeros((spec.experts, lay.stride), np.uint8)
-    for e in needed:
-        strides[e] = synth.hash_expert_stride(spec, SEED, 0, e)
-    # time growing token counts until the budget is used
-    n = min(T_sample, max(1, threads))
-    best = None
-    while True:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        from godwit_b200 import synth
+
+        self.O, self.spec, self.threads = O, spec, threads
+        rng = np.random.default_rng(SEED)
+        self.x = synth.as_f32(synth.make_hidden(rng, max_tokens, spec.hidden, "bf16"), "bf16")
+        self.rw, rb = synth.hash_router(spec, SEED, 0)
+        self.rb = rb if spec.router_bias else None
+        self.strides = np.zeros((spec.experts, spec.layout().stride), np.uint8)
+        self.ready = set()
+        self.n = max(1, min(threads, max_tokens))
+
+    def _need(self, n):
+        from godwit_b200 import synth
+        for t in range(n):
+            e, _ = self.O.router_select(self.O.router_logits(self.rw, self.rb, self.x[t]),
+                                        self.spec.top_k)
+            for v in e:
+                if int(v) not in self.ready:
+                    self.strides[int(v)] = synth.hash_expert_stride(self.spec, SEED, 0, int(v))
+                    self.ready.add(int(v))
+
+    def calibrate(self, budget_s: float):
+        """Grows the token count until one run takes about budget_s."""
+        while True:
+            self._need(self.n)
+            dt = self.run()
+            if dt * 2.0 > budget_s or self.n >= self.x.shape[0]:
+                return
+            self.n = min(self.x.shape[0], int(self.n * max(2.0, min(8.0, budget_s / max(dt, 1e-3) / 2))))
+
+    def run(self) -> float:
         t0 = time.perf_counter()
-        O.moe_layer(spec, strides, rw, rb_arg, x[:n], threads=threads)
-        dt = time.perf_counter() - t0
-        best = (n, dt)
-        if dt * 2.5 > budget_s or n >= T_sample:
-            break
-        n = min(T_sample, n * 2)
-    n, dt = best
-    token_layers_per_s = n / dt
-    return token_layers_per_s / spec.layers, (
-        f"{n} tokens x 1 layer (of {spec.layers}) of the workload, scaled to the stack; "
-        f"{dt:.2f} s on {threads} threads")
+        self.O.moe_layer(self.spec, self.strides, self.rw, self.rb, self.x[:self.n],
+                         threads=self.threads)
+        return time.perf_counter() - t0
+
+    def value(self, dt: float) -> float:
+        """Tokens/s through the whole stack (layer-tokens/s divided by the depth)."""
+        return self.n / dt / self.spec.layers
+
+    def sample(self, dt: float) -> str:
+        return (f"{self.n} tokens x layer 0 (of {self.spec.layers}) of the workload's bank, "
+                f"scaled to the stack; {dt:.2f} s on {self.threads} threads")
+
+
+def cpu_reference_sample(spec, threads: int, budget_s: float = 12.0):
+    ref = CpuReference(spec, threads)
+    ref.calibrate(budget_s)
+    dt = ref.run()
+    return ref.value(dt), ref.sample(dt)
 
 
 def cpu_gemv_sample(threads: int, budget_s: float = 10.0):
@@ -187,12 +210,15 @@ def run_reference(args, workload):
     preset, T, desc = WORKLOADS[workload]
     from godwit_b200.layout import PRESETS
     vals = []
+    ref = None if preset is None else CpuReference(PRESETS[preset], threads)
+    if ref is not None:
+        ref.calibrate(4.0)
     for i in range(args.warmup + args.steps):
-        if preset is None:
+        if ref is None:
             v, sample = cpu_gemv_sample(threads, budget_s=4.0)
         else:
-            v, sample = cpu_reference_sample(PRESETS[preset], max(T, threads), threads,
-                                             budget_s=4.0)
+            dt = ref.run()
+            v, sample = ref.value(dt), ref.sample(dt)
         if i >= args.warmup:
             vals.append(v)
     value = statistics.median(vals)
@@ -225,6 +251,8 @@ def main():
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="profiling only: hold and run this many layers instead of the model's")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -275,8 +303,10 @@ def run_decode(args):
     world, rank, local = _dist_setup(args)
     preset, T, desc = WORKLOADS[args.workload]
     spec = PRESETS[preset]
+    if args.layers:
+        spec = spec.with_(layers=args.layers)
     ctx = Context(local)
-    D.bind_stream(ctx)
+    cur = D.bind_stream(ctx)
     bank = ExpertBank(ctx, spec, shard_rank=rank, shard_count=world)
     t0 = time.time()
     bank.fill_synthetic(SEED)
@@ -303,7 +333,6 @@ def run_decode(args):
         step()
         out_host.copy_(stream_buf, non_blocking=True)
 
-    cur = torch.cuda.current_stream()
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -361,7 +390,8 @@ def run_decode(args):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "mxfp4 weights x bf16 activations, fp32 accumulate",
             "data": "synthetic (seeded random-init bank, hidden ~N(0,1))",
-            "config": {"workload": args.workload, "description": desc, "model_shape": spec.name,
+            "config": {"workload": args.workload, "description": desc if not args.layers else
+                       f"{desc} (profiling run: {spec.layers} layers)", "model_shape": spec.name,
                        "layers": spec.layers, "experts": spec.experts, "top_k": spec.top_k,
                        "hidden": spec.hidden, "intermediate": spec.intermediate, "tokens": T,
                        "parallelism": f"ep{world}" if world > 1 else "single",
@@ -377,12 +407,14 @@ def run_decode(args):
                          "alg_bytes_per_step": step_bytes_total,
                          "expert_passes_per_step": prof["expert_passes"] / prof_steps,
                          "expert_ms_per_step": expert_ms / prof_steps,
-                         "launches_timed": launches_prof},
+                         "launches_timed": launches_prof,
+                         "kernel_ms_per_step": {k: round(prof[k + "_ms"] / prof_steps, 4)
+                                                for k in ("router", "gateup", "down", "combine")}},
             "clocks": clocks,
         }
         if not args.no_cpu_baseline and world == 1:
             threads = os.cpu_count() or 1
-            v, sample = cpu_reference_sample(spec, max(T, threads), threads)
+            v, sample = cpu_reference_sample(spec, threads)
             line["cpu_baseline"] = {"value": v, "unit": unit, "cores": threads, "kind": "port",
                                     "sample": sample}
         print(json.dumps(line), flush=True)
@@ -404,7 +436,7 @@ def run_gemv(args):
 
     world, rank, local = _dist_setup(args)
     ctx = Context(local)
-    D.bind_stream(ctx)
+    cur = D.bind_stream(ctx)
     rows = cols = 2880
     alg = 4_429_440  # packed + scales + x + bias + y (config 0)
     l2 = torch.cuda.get_device_properties(local).L2_cache_size
@@ -423,7 +455,6 @@ def run_gemv(args):
     x = x_host.to("cuda")
     y = torch.empty(R, rows, dtype=torch.float32, device="cuda")
     y_host = torch.empty(R, rows, dtype=torch.float32).pin_memory()
-    cur = torch.cuda.current_stream()
 
     def step():
         D.gemv_batched(ctx, packed, scales, bias, x, y)

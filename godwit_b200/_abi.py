@@ -94,7 +94,9 @@ class Profile(C.Structure):
     _fields_ = [("gateup_launches", C.c_int64), ("down_launches", C.c_int64),
                 ("gemv_launches", C.c_int64), ("gateup_ms", C.c_double), ("down_ms", C.c_double),
                 ("gemv_ms", C.c_double), ("expert_passes", C.c_int64),
-                ("gemv_matrices", C.c_int64)]
+                ("gemv_matrices", C.c_int64), ("router_launches", C.c_int64),
+                ("combine_launches", C.c_int64), ("router_ms", C.c_double),
+                ("combine_ms", C.c_double)]
 
 
 SIGNATURES["gw_profile_enable"] = (ST, [P, I32])

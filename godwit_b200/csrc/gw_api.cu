@@ -72,7 +72,7 @@ struct gw_ctx {
     std::recursive_mutex mu;
     DevBuf work;        // MoE scratch (MoeWork)
     DevBuf staging;     // inputs/outputs of the synchronous API
-    DevBuf gemv_x;      // f16 x + xmul for GEMV calls
+    DevBuf gemv_x;      // f16 x + block scales of GEMV calls
     int work_tcap = 0, work_H = 0, work_F = 0, work_E = 0, work_k = 0;
     gw::MoeWork w{};
     int64_t launches = 0;
@@ -134,7 +134,7 @@ gw::LayerView layer_of(const gw_bank* b, int layer) {
 // Carves the MoE scratch for T tokens out of one allocation.
 gw_status ensure_work(gw_ctx* c, const gw_bank* b, int T) {
     const int H = b->d.hidden, F = b->d.intermediate, E = b->d.experts, k = b->d.top_k;
-    if (c->w.x16 && T <= c->work_tcap && H <= c->work_H && F <= c->work_F && E <= c->work_E &&
+    if (c->w.logits && T <= c->work_tcap && H <= c->work_H && F <= c->work_F && E <= c->work_E &&
         k <= c->work_k)
         return GW_OK;
     const int tcap = std::max(T, std::max(c->work_tcap, 1));
@@ -142,9 +142,9 @@ gw_status ensure_work(gw_ctx* c, const gw_bank* b, int T) {
     const int Ec = std::max(E, c->work_E), kc = std::max(k, c->work_k);
     size_t off = 0;
     auto take = [&](size_t bytes) { size_t o = off; off += align256(bytes); return o; };
+    const size_t o_xr = take((size_t)tcap * Hc * 2);
     const size_t o_x16 = take((size_t)tcap * Hc * 2);
     const size_t o_xmul = take((size_t)tcap * 4);
-    const size_t o_xr = take((size_t)tcap * Hc * 2);
     const size_t o_logits = take((size_t)tcap * Ec * 4);
     const size_t o_experts = take((size_t)tcap * kc * 4);
     const size_t o_weights = take((size_t)tcap * kc * 4);
@@ -154,17 +154,18 @@ gw_status ensure_work(gw_ctx* c, const gw_bank* b, int T) {
     const size_t o_lists = take((size_t)Ec * tcap * 4);
     const size_t o_act = take((size_t)tcap * kc * Fc * 2);
     const size_t o_ybuf = take((size_t)tcap * kc * Hc * 4);
-    const size_t o_done = take(4);
+    const size_t o_done = take((size_t)(tcap / 8 + 1) * 4);
     cudaError_t e = c->work.ensure(off);
     if (e != cudaSuccess) return cuda_fail(e, "workspace allocation");
     char* base = static_cast<char*>(c->work.p);
-    GW_CUDA(cudaMemsetAsync(base + o_done, 0, 4, c->cur));
+    GW_CUDA(cudaMemsetAsync(base + o_done, 0, (size_t)(tcap / 8 + 1) * 4, c->cur));
     GW_CUDA(cudaMemsetAsync(base + o_nactive, 0, 4, c->cur));
+    GW_CUDA(cudaMemsetAsync(base + o_counts, 0, (size_t)Ec * 4, c->cur));
     gw::MoeWork& w = c->w;
     w.tcap = tcap;
+    w.xr = base + o_xr;
     w.x16 = reinterpret_cast<__half*>(base + o_x16);
     w.xmul = reinterpret_cast<float*>(base + o_xmul);
-    w.xr = base + o_xr;
     w.logits = reinterpret_cast<float*>(base + o_logits);
     w.experts = reinterpret_cast<int32_t*>(base + o_experts);
     w.weights = reinterpret_cast<float*>(base + o_weights);
@@ -202,62 +203,72 @@ gw_status check_dtype(int x_dtype) {
     return GW_OK;
 }
 
+// Records an event pair around `launch` when profiling (kind: 0 gate_up,
+// 1 down, 2 gemv, 3 router/grouping, 4 combine).
+template <class F>
+gw_status timed_launch(gw_ctx* c, int kind, int64_t units, F&& launch) {
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (c->prof) {
+        GW_CUDA(cudaEventCreate(&e0));
+        GW_CUDA(cudaEventCreate(&e1));
+        GW_CUDA(cudaEventRecord(e0, c->cur));
+    }
+    gw_status st = count(c, launch());
+    if (st) return st;
+    if (c->prof) {
+        GW_CUDA(cudaEventRecord(e1, c->cur));
+        c->timed.push_back({kind, e0, e1, units});
+    }
+    return GW_OK;
+}
+
+// Appends this layer's number of active experts to the profile log.
+gw_status log_nactive(gw_ctx* c) {
+    const size_t need = (size_t)(c->nlog_used + 1) * 4;
+    if (need > c->nlog.n) {
+        DevBuf bigger;
+        cudaError_t e = bigger.ensure(std::max<size_t>(need * 2, 4096));
+        if (e != cudaSuccess) return cuda_fail(e, "profile log allocation");
+        if (c->nlog_used)
+            GW_CUDA(cudaMemcpyAsync(bigger.p, c->nlog.p, (size_t)c->nlog_used * 4,
+                                    cudaMemcpyDeviceToDevice, c->cur));
+        GW_CUDA(cudaStreamSynchronize(c->cur));
+        c->nlog.release();
+        c->nlog = bigger;
+    }
+    GW_CUDA(cudaMemcpyAsync(static_cast<int32_t*>(c->nlog.p) + c->nlog_used, c->w.nactive, 4,
+                            cudaMemcpyDeviceToDevice, c->cur));
+    c->nlog_used += 1;
+    return GW_OK;
+}
+
 // Router + grouping (or grouping of a supplied routing), experts, combine —
-// the device half of one MoE layer.  x_dev is [T][H] in x_dtype, or the fp32
-// stream when x_dtype == kF32 (then rounded to round_dtype).
+// the device half of one MoE layer.  x_dev is [T][H] in x_dtype (f16 or
+// bf16).  out (=, or += when accumulate) receives the weighted expert sum;
+// if x_next is given it receives round(out) in x_dtype.
 gw_status moe_layer_device(gw_ctx* c, gw_bank* b, int layer, const void* x_dev, int x_dtype,
-                           int round_dtype, int T, const int32_t* experts_in,
-                           const float* weights_in, float* out, int accumulate) {
+                           int T, const int32_t* experts_in, const float* weights_in, float* out,
+                           int accumulate, void* x_next) {
     const gw::MoeDims d = dims_of(b);
     const gw::LayerView L = layer_of(b, layer);
     gw_status st = ensure_work(c, b, T);
     if (st) return st;
     gw::MoeWork& w = c->w;
-    const bool from_stream = (x_dtype == gw::kF32);
-    st = count(c, gw::launch_prep(x_dev, x_dtype, from_stream ? round_dtype : x_dtype, T, d.H,
-                                  from_stream ? w.xr : nullptr, w.x16, w.xmul, c->cur));
-    if (st) return st;
     if (experts_in) {
-        st = count(c, gw::launch_group(d, experts_in, weights_in, T, w, c->cur));
-    } else {
-        const void* xr = from_stream ? w.xr : x_dev;
-        st = count(c, gw::launch_router(L, d, xr, from_stream ? round_dtype : x_dtype, T, w, c->cur));
+        st = count(c, gw::launch_xprep(x_dev, x_dtype, T, d.H, w.x16, w.xmul, c->cur));
+        if (st) return st;
+        st = timed_launch(c, 3, 0, [&] { return gw::launch_group(d, experts_in, weights_in, T, w, c->cur); });
     }
+    else
+        st = timed_launch(c, 3, 0, [&] { return gw::launch_router(L, d, x_dev, x_dtype, T, w, c->cur); });
     if (st) return st;
-    cudaEvent_t e0 = nullptr, e1 = nullptr, e2 = nullptr;
-    if (c->prof) {
-        GW_CUDA(cudaEventCreate(&e0));
-        GW_CUDA(cudaEventCreate(&e1));
-        GW_CUDA(cudaEventCreate(&e2));
-        GW_CUDA(cudaEventRecord(e0, c->cur));
-    }
-    st = count(c, gw::launch_gateup(L, d, T, w, c->cur));
-    if (st) return st;
-    if (c->prof) GW_CUDA(cudaEventRecord(e1, c->cur));
-    st = count(c, gw::launch_down(L, d, T, w, c->cur));
-    if (st) return st;
-    if (c->prof) {
-        GW_CUDA(cudaEventRecord(e2, c->cur));
-        c->timed.push_back({0, e0, e1, 0});
-        c->timed.push_back({1, e1, e2, 0});
-        const size_t need = (size_t)(c->nlog_used + 1) * 4;
-        if (need > c->nlog.n) {
-            // grow by copying the recorded prefix
-            DevBuf bigger;
-            cudaError_t e = bigger.ensure(std::max<size_t>(need * 2, 4096));
-            if (e != cudaSuccess) return cuda_fail(e, "profile log allocation");
-            if (c->nlog_used)
-                GW_CUDA(cudaMemcpyAsync(bigger.p, c->nlog.p, (size_t)c->nlog_used * 4,
-                                        cudaMemcpyDeviceToDevice, c->cur));
-            GW_CUDA(cudaStreamSynchronize(c->cur));
-            c->nlog.release();
-            c->nlog = bigger;
-        }
-        GW_CUDA(cudaMemcpyAsync(static_cast<int32_t*>(c->nlog.p) + c->nlog_used, w.nactive, 4,
-                                cudaMemcpyDeviceToDevice, c->cur));
-        c->nlog_used += 1;
-    }
-    return count(c, gw::launch_combine(d, T, w, out, accumulate, c->cur));
+    if ((st = timed_launch(c, 0, 0, [&] { return gw::launch_gateup(L, d, x_dev, x_dtype, T, w, c->cur); })))
+        return st;
+    if ((st = timed_launch(c, 1, 0, [&] { return gw::launch_down(L, d, T, w, c->cur); }))) return st;
+    if (c->prof && (st = log_nactive(c))) return st;
+    return timed_launch(c, 4, 0, [&] {
+        return gw::launch_combine(d, T, w, out, accumulate, x_next, x_dtype, c->cur);
+    });
 }
 
 }  // namespace
@@ -378,7 +389,9 @@ gw_status gw_profile_read(gw_ctx* c, gw_profile* out) {
         GW_CUDA(cudaEventElapsedTime(&ms, t.a, t.b));
         if (t.kind == 0) { c->acc.gateup_launches++; c->acc.gateup_ms += ms; }
         else if (t.kind == 1) { c->acc.down_launches++; c->acc.down_ms += ms; }
-        else { c->acc.gemv_launches++; c->acc.gemv_ms += ms; c->acc.gemv_matrices += t.units; }
+        else if (t.kind == 2) { c->acc.gemv_launches++; c->acc.gemv_ms += ms; c->acc.gemv_matrices += t.units; }
+        else if (t.kind == 3) { c->acc.router_launches++; c->acc.router_ms += ms; }
+        else { c->acc.combine_launches++; c->acc.combine_ms += ms; }
     }
     drop_timed(c);
     if (c->nlog_used) {
@@ -628,7 +641,7 @@ gw_status gw_moe_forward_async(gw_ctx* c, gw_bank* b, int32_t layer, const void*
     if (T <= 0) return fail(GW_E_ARG, "T must be positive");
     CtxLock lk(c);
     if ((st = set_device(c))) return st;
-    st = moe_layer_device(c, b, layer, x_dev, x_dtype, x_dtype, T, nullptr, nullptr, out_dev, 0);
+    st = moe_layer_device(c, b, layer, x_dev, x_dtype, T, nullptr, nullptr, out_dev, 0, nullptr);
     if (st) return st;
     const size_t nk = (size_t)T * b->d.top_k;
     if (experts_dev)
@@ -647,12 +660,15 @@ gw_status gw_moe_stack_forward_async(gw_ctx* c, gw_bank* b, const void* x_dev, i
     CtxLock lk(c);
     if ((st = set_device(c))) return st;
     const int64_t n = (int64_t)T * b->d.hidden;
-    // stream = x widened to fp32; then stream += moe_l(round(stream)) per layer
+    // stream = x widened to fp32; then stream += moe_l(round(stream)) per layer.
+    // Each layer's combine writes round(stream) into the workspace's x buffer,
+    // which is the next layer's input.
+    if ((st = ensure_work(c, b, T))) return st;
     if ((st = count(c, gw::launch_widen(x_dev, x_dtype, stream_dev, n, c->cur)))) return st;
     for (int l = 0; l < b->d.layers; ++l) {
-        const void* src = (l == 0) ? x_dev : static_cast<const void*>(stream_dev);
-        const int src_dtype = (l == 0) ? x_dtype : gw::kF32;
-        st = moe_layer_device(c, b, l, src, src_dtype, x_dtype, T, nullptr, nullptr, stream_dev, 1);
+        const void* src = (l == 0) ? x_dev : c->w.xr;
+        void* next = (l + 1 < b->d.layers) ? c->w.xr : nullptr;
+        st = moe_layer_device(c, b, l, src, x_dtype, T, nullptr, nullptr, stream_dev, 1, next);
         if (st) return st;
     }
     return GW_OK;
@@ -667,8 +683,8 @@ gw_status gw_moe_apply_async(gw_ctx* c, gw_bank* b, int32_t layer, const void* x
     if (T <= 0) return fail(GW_E_ARG, "T must be positive");
     CtxLock lk(c);
     if ((st = set_device(c))) return st;
-    return moe_layer_device(c, b, layer, x_dev, x_dtype, x_dtype, T, experts_dev, weights_dev,
-                            out_dev, accumulate ? 1 : 0);
+    return moe_layer_device(c, b, layer, x_dev, x_dtype, T, experts_dev, weights_dev, out_dev,
+                            accumulate ? 1 : 0, nullptr);
 }
 
 gw_status gw_residual_round_async(gw_ctx* c, float* stream_dev, const float* delta_dev,
@@ -681,7 +697,7 @@ gw_status gw_residual_round_async(gw_ctx* c, float* stream_dev, const float* del
     return count(c, gw::launch_residual_round(stream_dev, delta_dev, x_out_dev, x_dtype, n, c->cur));
 }
 
-// GEMV over `count` matrices whose x is already staged as f16 + multiplier.
+// GEMV over `count` matrices (device pointers).
 static gw_status gemv_device(gw_ctx* c, int32_t count_m, const uint8_t* packed, int64_t ps,
                              const uint8_t* scales, int64_t ss, const uint16_t* bias, int64_t bs,
                              const void* x, int64_t x_stride, int32_t x_dtype, float* y,
@@ -692,33 +708,10 @@ static gw_status gemv_device(gw_ctx* c, int32_t count_m, const uint8_t* packed, 
     if (e != cudaSuccess) return cuda_fail(e, "GEMV staging allocation");
     __half* x16 = static_cast<__half*>(c->gemv_x.p);
     float* xmul = reinterpret_cast<float*>(static_cast<char*>(c->gemv_x.p) + xbytes);
-    gw_status st;
-    if (x_stride != 0 && x_stride != cols) {
-        for (int m = 0; m < count_m; ++m) {
-            const char* xm = static_cast<const char*>(x) + (size_t)m * x_stride * 2;
-            if ((st = count(c, gw::launch_prep(xm, x_dtype, x_dtype, 1, cols, nullptr,
-                                               x16 + (size_t)m * cols, xmul + m, c->cur))))
-                return st;
-        }
-    } else if ((st = count(c, gw::launch_prep(x, x_dtype, x_dtype, nx, cols, nullptr, x16, xmul,
-                                              c->cur)))) {
-        return st;
-    }
-    cudaEvent_t e0 = nullptr, e1 = nullptr;
-    if (c->prof) {
-        GW_CUDA(cudaEventCreate(&e0));
-        GW_CUDA(cudaEventCreate(&e1));
-        GW_CUDA(cudaEventRecord(e0, c->cur));
-    }
-    st = count(c, gw::launch_gemv_batched(count_m, packed, ps, scales, ss, bias, bs, x16,
-                                          x_stride == 0 ? 0 : cols, xmul, y, ys, rows, cols,
-                                          c->cur));
-    if (st) return st;
-    if (c->prof) {
-        GW_CUDA(cudaEventRecord(e1, c->cur));
-        c->timed.push_back({2, e0, e1, count_m});
-    }
-    return GW_OK;
+    return timed_launch(c, 2, count_m, [&] {
+        return gw::launch_gemv_batched(count_m, packed, ps, scales, ss, bias, bs, x, x_stride,
+                                       x_dtype, x16, xmul, y, ys, rows, cols, c->cur);
+    });
 }
 
 gw_status gw_mxfp4_gemv_batched_async(gw_ctx* c, int32_t count_m, const uint8_t* packed,
@@ -817,6 +810,8 @@ gw_status gw_router_logits(gw_ctx* c, gw_bank* b, int32_t layer, const void* x, 
     if ((st = count(c, gw::launch_router(layer_of(b, layer), d, sg.at<void>(ox), x_dtype, T, c->w,
                                          c->cur))))
         return st;
+    GW_CUDA(cudaMemsetAsync(c->w.counts, 0, (size_t)d.E * 4, c->cur));
+    GW_CUDA(cudaMemsetAsync(c->w.nactive, 0, 4, c->cur));
     GW_CUDA(cudaMemcpyAsync(logits, c->w.logits, (size_t)T * d.E * 4, cudaMemcpyDeviceToHost, c->cur));
     GW_CUDA(cudaStreamSynchronize(c->cur));
     return GW_OK;
@@ -841,6 +836,8 @@ gw_status gw_route(gw_ctx* c, gw_bank* b, int32_t layer, const void* x, int32_t 
     if ((st = count(c, gw::launch_router(layer_of(b, layer), d, sg.at<void>(ox), x_dtype, T, c->w,
                                          c->cur))))
         return st;
+    GW_CUDA(cudaMemsetAsync(c->w.counts, 0, (size_t)d.E * 4, c->cur));
+    GW_CUDA(cudaMemsetAsync(c->w.nactive, 0, 4, c->cur));
     const size_t nk = (size_t)T * d.k;
     GW_CUDA(cudaMemcpyAsync(experts_out, c->w.experts, nk * 4, cudaMemcpyDeviceToHost, c->cur));
     GW_CUDA(cudaMemcpyAsync(weights_out, c->w.weights, nk * 4, cudaMemcpyDeviceToHost, c->cur));
@@ -882,9 +879,9 @@ gw_status gw_moe_forward(gw_ctx* c, gw_bank* b, int32_t layer, const void* x, in
         GW_CUDA(cudaMemcpyAsync(sg.at<int32_t>(oe), experts_in, nk * 4, cudaMemcpyHostToDevice, c->cur));
         GW_CUDA(cudaMemcpyAsync(sg.at<float>(ow), weights_in, nk * 4, cudaMemcpyHostToDevice, c->cur));
     }
-    st = moe_layer_device(c, b, layer, sg.at<void>(ox), x_dtype, x_dtype, T,
+    st = moe_layer_device(c, b, layer, sg.at<void>(ox), x_dtype, T,
                           experts_in ? sg.at<int32_t>(oe) : nullptr,
-                          experts_in ? sg.at<float>(ow) : nullptr, sg.at<float>(oo), 0);
+                          experts_in ? sg.at<float>(ow) : nullptr, sg.at<float>(oo), 0, nullptr);
     if (st) return st;
     GW_CUDA(cudaMemcpyAsync(out, sg.at<float>(oo), no, cudaMemcpyDeviceToHost, c->cur));
     if (experts_out)
@@ -928,8 +925,8 @@ gw_status gw_expert_apply_batch(gw_ctx* c, gw_bank* b, int32_t layer, const void
     GW_CUDA(cudaMemcpyAsync(sg.at<void>(ox), x, nx, cudaMemcpyHostToDevice, c->cur));
     GW_CUDA(cudaMemcpyAsync(sg.at<int32_t>(oe), ex, nk * 4, cudaMemcpyHostToDevice, c->cur));
     GW_CUDA(cudaMemcpyAsync(sg.at<float>(ow), wt, nk * 4, cudaMemcpyHostToDevice, c->cur));
-    st = moe_layer_device(c, b, layer, sg.at<void>(ox), x_dtype, x_dtype, 1, sg.at<int32_t>(oe),
-                          sg.at<float>(ow), sg.at<float>(oo), 0);
+    st = moe_layer_device(c, b, layer, sg.at<void>(ox), x_dtype, 1, sg.at<int32_t>(oe),
+                          sg.at<float>(ow), sg.at<float>(oo), 0, nullptr);
     if (st) return st;
     GW_CUDA(cudaMemcpyAsync(y, sg.at<float>(oo), no, cudaMemcpyDeviceToHost, c->cur));
     GW_CUDA(cudaStreamSynchronize(c->cur));

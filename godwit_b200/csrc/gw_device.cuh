@@ -87,74 +87,184 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
-// One warp's 16-row x 8-column (tokens) MXFP4 tile over the full K.
+// ---------------------------------------------------------------------------
+// Block-diagonal MXFP4 tile: one warp, 16 weight rows (rowA / rowB halves),
+// blocks [blk0, blk1), 1..8 tokens.
 //
-// Fragment mapping (m16n8k16, g = lane/4, t = lane%4):
-//   A rows: MMA row g    <- weight row rowA, MMA row g+8 <- weight row rowB.
-//   K: for each 32-column block the thread owns packed word t (columns
-//      8t..8t+7 of the block); byte 0/1 feed the first k16 step's low/high
-//      k-pairs, bytes 2/3 the second's.  B is loaded with the same column
-//      permutation: x[token g][block*32 + 8t .. 8t+7] as one 16-byte smem load.
-//   C: c0 = (rowA, token 2t), c1 = (rowA, token 2t+1),
-//      c2 = (rowB, token 2t), c3 = (rowB, token 2t+1).
-// `xs` is the token block in shared memory, row stride `xs_stride` halves.
-template <int kUnroll>
-__device__ __forceinline__ void mxfp4_tile(const uint8_t* __restrict__ packed,
-                                           const uint8_t* __restrict__ scales, int cols,
-                                           int rowA, int rowB, const __half* xs, int xs_stride,
-                                           float (&acc)[4]) {
+// Each thread streams WHOLE 16-byte blocks with 128-bit loads: in round r of
+// an 8-block group, thread t of a quad owns block base + 4r + t of rows rowA
+// and rowB, so a warp load covers 64 contiguous bytes of 8 rows (full
+// sectors).  The four threads of an MMA quad therefore feed four different
+// blocks (four different scales) into one m16n8k16 MMA, so each block's
+// partial is kept apart by the B operand: the B fragment of thread (g, t)
+// holds x[token][that thread's block] only when column g belongs to
+// (block t, token) and zeros otherwise (a shared zero block).  D[row][col]
+// then accumulates exactly one (block, token) partial per column, which is
+// scaled by its E8M0 scale (and the x block scale) into fp32 accumulators —
+// the reference's "acc += partial * scale" — before the MMA accumulator
+// restarts from zero.
+//
+//   kTok = 1: columns = the 8 blocks of the group (one token).
+//   kTok = 2: columns = 4 blocks x 2 tokens; kSets token pairs share each
+//             converted weight fragment (their MMAs use separate
+//             accumulators), so 2*kSets tokens cost one weight conversion.
+//
+// Shared x layout: xs[token][block][40 halves] (32 values + 8 pad, which
+// keeps the four active threads' 16-byte loads on distinct banks); the block
+// at index `zero_blk` of token row 0 is all zeros.  The results are in the
+// units of the staged x (the caller applies the token's x scale).
+constexpr int kXBlockHalves = 40;
+
+template <int kTok, int kSets>
+__device__ __forceinline__ void mxfp4_tile_diag(const uint8_t* __restrict__ packed,
+                                                const uint8_t* __restrict__ scales, int cols,
+                                                int rowA, int rowB, const __half* xs,
+                                                int xs_stride, int ntok,
+                                                int blk0, int blk1,
+                                                float (&accA)[kTok * kSets],
+                                                float (&accB)[kTok * kSets]) {
+    static_assert((kTok == 1 && kSets == 1) || kTok == 2, "1 token, or token pairs");
     const int lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
-    const int nblk = cols >> 5;
-    const uint32_t* pA = reinterpret_cast<const uint32_t*>(packed + (size_t)rowA * (cols >> 1)) + t;
-    const uint32_t* pB = reinterpret_cast<const uint32_t*>(packed + (size_t)rowB * (cols >> 1)) + t;
-    const uint8_t* sA = scales + (size_t)rowA * nblk;
-    const uint8_t* sB = scales + (size_t)rowB * nblk;
-    const __half* xr = xs + g * xs_stride + 8 * t;
-    const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+    const int nblk = blk1;
+    const int row_blocks = cols >> 5;
+    const int zero_blk = row_blocks;  // the zero block
+    const size_t rb = (size_t)(cols >> 1);
+    const uint4* pA = reinterpret_cast<const uint4*>(packed + (size_t)rowA * rb);
+    const uint4* pB = reinterpret_cast<const uint4*>(packed + (size_t)rowB * rb);
+    const uint8_t* sA = scales + (size_t)rowA * row_blocks;
+    const uint8_t* sB = scales + (size_t)rowB * row_blocks;
+#pragma unroll
+    for (int j = 0; j < kTok * kSets; ++j) { accA[j] = 0.f; accB[j] = 0.f; }
 
-    int b = 0;
-    for (; b + kUnroll <= nblk; b += kUnroll) {
-        uint32_t wa[kUnroll], wb[kUnroll], ea[kUnroll], eb[kUnroll];
+    uint4 wa[2], wb[2];
+    auto load = [&](int base) {
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-            wa[u] = ldg_u32(pA + 4 * (b + u));
-            wb[u] = ldg_u32(pB + 4 * (b + u));
-            ea[u] = ldg_u8(sA + b + u);
-            eb[u] = ldg_u8(sB + b + u);
+        for (int r = 0; r < 2; ++r) {
+            const int blk = base + 4 * r + t;
+            if (blk < nblk) { wa[r] = __ldg(pA + blk); wb[r] = __ldg(pB + blk); }
+            else { wa[r] = make_uint4(0, 0, 0, 0); wb[r] = make_uint4(0, 0, 0, 0); }
         }
+    };
+    // x source of this thread's B fragment for (round r, set s): the token
+    // row and block when column g is (this thread's block, token), else the
+    // zero block.
+    auto xsrc = [&](int r, int s, int base) -> const uint4* {
+        const int blk = base + 4 * r + t;
+        int tok = -1;
+        if (kTok == 1) tok = (g == 4 * r + t) ? 0 : -1;
+        else tok = (g >> 1) == t ? 2 * s + (g & 1) : -1;
+        const bool live = tok >= 0 && tok < ntok && blk < nblk;
+        return reinterpret_cast<const uint4*>(live ? xs + tok * xs_stride + blk * kXBlockHalves
+                                                   : xs + zero_blk * kXBlockHalves);
+    };
+    load(blk0);
+    for (int base = blk0; base < nblk; base += 8) {
+        uint4 ca[2], cb[2];
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-            const uint4 xv = *reinterpret_cast<const uint4*>(xr + 32 * (b + u));
-            uint32_t a0, a1, a2, a3, q0, q1, q2, q3;
-            e2m1x8_to_f16x8(wa[u], a0, a1, a2, a3);
-            e2m1x8_to_f16x8(wb[u], q0, q1, q2, q3);
-            float d[4];
-            mma16816(d, a0, q0, a1, q1, xv.x, xv.y, zero);
-            mma16816(d, a2, q2, a3, q3, xv.z, xv.w, d);
-            const float fa = gemv_scale(ea[u]), fb = gemv_scale(eb[u]);
-            acc[0] = fmaf(d[0], fa, acc[0]);
-            acc[1] = fmaf(d[1], fa, acc[1]);
-            acc[2] = fmaf(d[2], fb, acc[2]);
-            acc[3] = fmaf(d[3], fb, acc[3]);
+        for (int r = 0; r < 2; ++r) { ca[r] = wa[r]; cb[r] = wb[r]; }
+        if (base + 8 < nblk) load(base + 8);  // next group's loads in flight
+        float d[kSets][4];
+#pragma unroll
+        for (int s = 0; s < kSets; ++s) d[s][0] = d[s][1] = d[s][2] = d[s][3] = 0.f;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const uint4* xp[kSets];
+#pragma unroll
+            for (int s = 0; s < kSets; ++s) xp[s] = xsrc(r, s, base);
+            const uint32_t wA[4] = {ca[r].x, ca[r].y, ca[r].z, ca[r].w};
+            const uint32_t wB[4] = {cb[r].x, cb[r].y, cb[r].z, cb[r].w};
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+                uint32_t a0, a1, a2, a3, q0, q1, q2, q3;
+                e2m1x8_to_f16x8(wA[w], a0, a1, a2, a3);
+                e2m1x8_to_f16x8(wB[w], q0, q1, q2, q3);
+#pragma unroll
+                for (int s = 0; s < kSets; ++s) {
+                    const uint4 xv = xp[s][w];
+                    // step 2w: bytes 0,1 of word w; step 2w+1: bytes 2,3
+                    mma16816(d[s], a0, q0, a1, q1, xv.x, xv.y, d[s]);
+                    mma16816(d[s], a2, q2, a3, q3, xv.z, xv.w, d[s]);
+                }
+            }
+            if constexpr (kTok == 2) {
+                // flush this round: column 2t+q = (block base+4r+t, token 2s+q)
+                const int blk = base + 4 * r + t;
+                const bool ok = blk < nblk;
+                const float fa = ok ? gemv_scale(ldg_u8(sA + blk)) : 0.f;
+                const float fb = ok ? gemv_scale(ldg_u8(sB + blk)) : 0.f;
+#pragma unroll
+                for (int s = 0; s < kSets; ++s) {
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        const int tok = 2 * s + q;
+                        accA[tok] = fmaf(d[s][q], fa, accA[tok]);
+                        accB[tok] = fmaf(d[s][2 + q], fb, accB[tok]);
+                    }
+                    d[s][0] = d[s][1] = d[s][2] = d[s][3] = 0.f;
+                }
+            }
+        }
+        if constexpr (kTok == 1) {
+            // flush the group: column 2t+q = block base+2t+q
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const int blk = base + 2 * t + q;
+                const bool ok = blk < nblk;
+                const float fa = ok ? gemv_scale(ldg_u8(sA + blk)) : 0.f;
+                const float fb = ok ? gemv_scale(ldg_u8(sB + blk)) : 0.f;
+                accA[0] = fmaf(d[0][q], fa, accA[0]);
+                accB[0] = fmaf(d[0][2 + q], fb, accB[0]);
+            }
         }
     }
-    for (; b < nblk; ++b) {
-        const uint32_t wa = ldg_u32(pA + 4 * b), wb = ldg_u32(pB + 4 * b);
-        const uint32_t ea = ldg_u8(sA + b), eb = ldg_u8(sB + b);
-        const uint4 xv = *reinterpret_cast<const uint4*>(xr + 32 * b);
-        uint32_t a0, a1, a2, a3, q0, q1, q2, q3;
-        e2m1x8_to_f16x8(wa, a0, a1, a2, a3);
-        e2m1x8_to_f16x8(wb, q0, q1, q2, q3);
-        float d[4];
-        mma16816(d, a0, q0, a1, q1, xv.x, xv.y, zero);
-        mma16816(d, a2, q2, a3, q3, xv.z, xv.w, d);
-        const float fa = gemv_scale(ea), fb = gemv_scale(eb);
-        acc[0] = fmaf(d[0], fa, acc[0]);
-        acc[1] = fmaf(d[1], fa, acc[1]);
-        acc[2] = fmaf(d[2], fb, acc[2]);
-        acc[3] = fmaf(d[3], fb, acc[3]);
+    // sum the quad's columns
+#pragma unroll
+    for (int j = 0; j < kTok * kSets; ++j) {
+        accA[j] += __shfl_xor_sync(0xffffffffu, accA[j], 1);
+        accA[j] += __shfl_xor_sync(0xffffffffu, accA[j], 2);
+        accB[j] += __shfl_xor_sync(0xffffffffu, accB[j], 1);
+        accB[j] += __shfl_xor_sync(0xffffffffu, accB[j], 2);
     }
 }
+
+// 2^p as an fp32 bit pattern, |p| <= 126.
+__device__ __forceinline__ float pow2f(int p) { return __uint_as_float((uint32_t)(127 + p) << 23); }
+
+// Shift p that brings a row maximum m into [2^15, 2^16): every bf16 value
+// within 2^-24 of the row maximum then converts to f16 exactly after
+// multiplying by 2^p, and the GEMV result is multiplied by 2^-p.  0 for zero
+// or non-finite m.
+__device__ __forceinline__ int row_exponent_shift(float m) {
+    const uint32_t e = (__float_as_uint(m) >> 23) & 0xffu;  // biased exponent of m
+    if (m == 0.f || e == 0xffu) return 0;
+    const int ex = (e == 0 ? -126 : (int)e - 126);          // m < 2^ex
+    const int p = 16 - ex;
+    return p < -120 ? -120 : (p > 120 ? 120 : p);
+}
+
+// Stages n f16 rows (row_ids into src [*][cols]) into the padded block
+// layout of mxfp4_tile_diag.
+__device__ __forceinline__ void stage_x16(__half* xs, int xs_stride, const __half* src,
+                                          const int* row_ids, int n, int cols) {
+    const int chunks = cols >> 3;  // 16-byte chunks per row; 4 per block
+    for (int i = threadIdx.x; i < n * chunks; i += blockDim.x) {
+        const int r = i / chunks, c = i - r * chunks;
+        const uint4 v = *reinterpret_cast<const uint4*>(src + (int64_t)row_ids[r] * cols + 8 * c);
+        *reinterpret_cast<uint4*>(xs + r * xs_stride + (c >> 2) * kXBlockHalves + 8 * (c & 3)) = v;
+    }
+}
+
+// Zeroes the shared zero block (block index cols/32 of token row 0's
+// layout; the row stride leaves room for it, see diag_stride).
+__device__ __forceinline__ void zero_block_init(__half* xs, int cols) {
+    if (threadIdx.x < kXBlockHalves / 8)
+        *reinterpret_cast<uint4*>(xs + (cols >> 5) * kXBlockHalves + 8 * threadIdx.x) =
+            make_uint4(0u, 0u, 0u, 0u);
+}
+
+// Row stride of the staged x: the row's blocks plus one (the zero block
+// lives in that slot of row 0).
+__device__ __forceinline__ int diag_stride(int cols) { return ((cols >> 5) + 1) * kXBlockHalves; }
 
 }  // namespace gw

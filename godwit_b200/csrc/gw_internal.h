@@ -10,7 +10,8 @@ namespace gw {
 
 constexpr int kMaxTopK = 16;
 constexpr int kMaxExperts = 256;
-constexpr int kTokTile = 8;       // tokens per MMA column block
+constexpr int kTokTile = 8;       // tokens per router CTA
+constexpr int kChunk = 4;         // tokens per weight pass of an expert GEMV tile
 constexpr int kGemvWarps = 4;     // warps per GEMV CTA (one 16-row tile each)
 
 // Element types of activation inputs.  F32 is internal: the residual stream
@@ -35,9 +36,9 @@ struct MoeDims {
 // Scratch the MoE forward uses between kernels, sized for `tcap` tokens.
 struct MoeWork {
     int tcap;
-    __half* x16;       // [tcap][H]   f16 expert input (bf16 inputs prescaled by 2^p)
-    float* xmul;       // [tcap]      2^-p, applied to the GEMV result
-    void* xr;          // [tcap][H]   router input in the compute dtype (stack mode)
+    void* xr;          // [tcap][H]   next layer's input in the compute dtype (stack mode)
+    __half* x16;       // [tcap][H]   expert input as f16 (bf16 rows scaled by 1/xmul)
+    float* xmul;       // [tcap]       power-of-two scale undoing each row's conversion shift
     float* logits;     // [tcap][E]
     int32_t* experts;  // [tcap][k]
     float* weights;    // [tcap][k]
@@ -47,34 +48,34 @@ struct MoeWork {
     int32_t* lists;    // [E][tcap]    slot ids (t*k + j) per expert
     __half* act;       // [tcap*k][F]  activated gate_up output (f16, as the reference)
     float* ybuf;       // [tcap*k][H]  routing-weighted down output per slot
-    unsigned* done;    // [1]          router completion counter (self-resetting)
+    unsigned* done;    // [tcap/8+1]   router completion counter per token chunk (self-resetting)
 };
 
 // Host-side launchers; each returns the number of kernels it launched (or -1
 // on a launch error, left in cudaGetLastError()).
-int launch_prep(const void* src, int src_dtype, int round_dtype, int T, int H, void* xr_out,
-                __half* x16, float* xmul, cudaStream_t s);
-int launch_router(const LayerView& L, const MoeDims& d, const void* xr, int x_dtype, int T,
+int launch_router(const LayerView& L, const MoeDims& d, const void* x, int x_dtype, int T,
                   const MoeWork& w, cudaStream_t s);
 int launch_group(const MoeDims& d, const int32_t* experts_in, const float* weights_in, int T,
                  const MoeWork& w, cudaStream_t s);
-int launch_gateup(const LayerView& L, const MoeDims& d, int T, const MoeWork& w,
-                  cudaStream_t s);
+int launch_gateup(const LayerView& L, const MoeDims& d, const void* x, int x_dtype, int T,
+                  const MoeWork& w, cudaStream_t s);
 int launch_down(const LayerView& L, const MoeDims& d, int T, const MoeWork& w, cudaStream_t s);
 int launch_combine(const MoeDims& d, int T, const MoeWork& w, float* out, int accumulate,
-                   cudaStream_t s);
+                   void* x_next, int x_dtype, cudaStream_t s);
 int launch_gemv_batched(int count, const uint8_t* packed, int64_t packed_stride,
                         const uint8_t* scales, int64_t scale_stride, const uint16_t* bias,
-                        int64_t bias_stride, const __half* x16, int64_t x_stride,
-                        const float* xmul, float* y, int64_t y_stride, int rows, int cols,
+                        int64_t bias_stride, const void* x, int64_t x_stride, int x_dtype,
+                        __half* x16, float* xmul, float* y, int64_t y_stride, int rows, int cols,
                         cudaStream_t s);
 int launch_dequant(const uint8_t* packed, const uint8_t* scales, int rows, int cols, float* w,
                    cudaStream_t s);
 int launch_fill_bytes(uint8_t* dst, int64_t n, uint64_t key, int kind, cudaStream_t s);
 int launch_residual_round(float* stream, const float* delta, void* x_out, int x_dtype,
                           int64_t n, cudaStream_t s);
+int launch_xprep(const void* x, int x_dtype, int T, int H, __half* x16, float* xmul,
+                 cudaStream_t s);
 int launch_widen(const void* x, int x_dtype, float* stream, int64_t n, cudaStream_t s);
-size_t gemv_smem_bytes(int cols);
+size_t gemv_smem_bytes(int cols, int max_tok);
 int configure_kernels();
 
 // Counter hash used by the synthetic bank generator (splitmix64 finaliser).

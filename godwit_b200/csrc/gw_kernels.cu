@@ -1,8 +1,5 @@
 // gw_kernels.cu — sm_100a kernels of the MoE expert hot path.
 //
-//   k_prep          activation staging: router input in the compute dtype and
-//                   the f16 expert input (bf16 rows prescaled by a power of two
-//                   so every bf16 value converts to f16 exactly)
 //   k_router        bf16 router GEMV + bias (Metal/MoE/router.metal:18-34); the
 //                   last CTA to finish runs the top-k selection and softmax of
 //                   Router.select (Runtime/Router.swift:78-98) for every token
@@ -13,13 +10,18 @@
 //                   (expert.metal:46-102, :380-393), one expert per CTA row
 //   k_down          grouped MXFP4 down GEMV + bias, scaled by the routing weight
 //                   (expert.metal:107-116 folded into the epilogue)
-//   k_combine       per-token sum of its k expert contributions in rank order
+//   k_combine       per-token sum of its k expert contributions in rank order,
+//                   optionally added to the residual stream, which is then
+//                   rounded into the next layer's input
 //   k_gemv          batched plain MXFP4 GEMV (dequant_gemv.metal:37-67)
 //   k_dequant       bit-exact MXFP4 decode (Quant/MXFP4.swift:48-92)
 //   k_fill          seeded synthetic bank bytes
 //   k_residual      stream += delta and the rounded next-layer input
+//   k_widen         stream = x
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+
+#include <algorithm>
 
 #include "gw_device.cuh"
 #include "gw_internal.h"
@@ -34,61 +36,10 @@ __device__ __forceinline__ float load_act(const void* p, int dtype, int64_t i) {
     return reinterpret_cast<const float*>(p)[i];
 }
 
-__device__ __forceinline__ float round_to(float v, int dtype) {
-    if (dtype == kF16) return __half2float(__float2half_rn(v));
-    if (dtype == kBF16) return __bfloat162float(__float2bfloat16_rn(v));
-    return v;
-}
-
 __device__ __forceinline__ void store_act(void* p, int dtype, int64_t i, float v) {
     if (dtype == kF16) reinterpret_cast<__half*>(p)[i] = __float2half_rn(v);
     else if (dtype == kBF16) reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
     else reinterpret_cast<float*>(p)[i] = v;
-}
-
-// ---------------------------------------------------------------------------
-// k_prep: one CTA per token.
-//   src_dtype == round_dtype: the input is already in the compute dtype.
-//   src_dtype == kF32: the residual stream, rounded to round_dtype first (and
-//   written to xr_out for the router).
-// f16 values pass through unscaled.  bf16 values are multiplied by 2^p, p
-// chosen from the row's largest magnitude so that it lands in [2^15, 2^16);
-// every bf16 value within 2^-24 of the row maximum is then an exact f16, and
-// the GEMV multiplies its fp32 result by xmul = 2^-p.
-__global__ void k_prep(const void* __restrict__ src, int src_dtype, int round_dtype, int H,
-                       void* __restrict__ xr_out, __half* __restrict__ x16,
-                       float* __restrict__ xmul) {
-    const int t = blockIdx.x;
-    __shared__ float red[32];
-    float m = 0.f;
-    for (int h = threadIdx.x; h < H; h += blockDim.x) {
-        const float v = round_to(load_act(src, src_dtype, (int64_t)t * H + h), round_dtype);
-        m = fmaxf(m, fabsf(v));
-    }
-    m = warp_max(m);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
-        v = warp_max(v);
-        if (threadIdx.x == 0) red[0] = v;
-    }
-    __syncthreads();
-    m = red[0];
-    int p = 0;
-    if (round_dtype == kBF16 && m > 0.f && isfinite(m)) {
-        int ex;
-        frexpf(m, &ex);  // m < 2^ex
-        p = 16 - ex;
-        p = p < -120 ? -120 : (p > 120 ? 120 : p);
-    }
-    for (int h = threadIdx.x; h < H; h += blockDim.x) {
-        const int64_t i = (int64_t)t * H + h;
-        const float v = round_to(load_act(src, src_dtype, i), round_dtype);
-        if (xr_out) store_act(xr_out, round_dtype, i, v);
-        x16[i] = __float2half_rn(ldexpf(v, p));
-    }
-    if (threadIdx.x == 0) xmul[t] = ldexpf(1.f, -p);
 }
 
 // ---------------------------------------------------------------------------
@@ -165,70 +116,127 @@ __device__ __forceinline__ void group_slot(const MoeDims& d, const MoeWork& w, i
 }
 
 // ---------------------------------------------------------------------------
+// Converts one 32-value block of token row t to f16 with the row's shift p
+// (x16 = x * 2^p; see row_exponent_shift).  One warp, lane = value.
+__device__ __forceinline__ void prep_block(const void* x, int x_dtype, int H, int t, int blk, int p,
+                                           __half* x16) {
+    const int64_t i = (int64_t)t * H + blk * 32 + (threadIdx.x & 31);
+    if (x_dtype == kF16) x16[i] = reinterpret_cast<const __half*>(x)[i];
+    else x16[i] = __float2half_rn(bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(x)[i]) * pow2f(p));
+}
+
 // k_router: grid (ceil(E/4), ceil(T/8)), 4 warps; warp w scores expert
-// 4*blockIdx.x + w against up to 8 tokens.  Each CTA then counts itself done;
-// the last one selects the top-k of every token and groups the slots.
+// 4*blockIdx.x + w against the CTA's (up to) 8 tokens, and the CTA converts
+// its share of those tokens' x blocks for the expert GEMVs.  Each CTA then
+// counts itself done on its token chunk's counter; the last CTA of a chunk
+// selects the top-k of the chunk's tokens and adds their slots to the expert
+// lists (whose counts the previous combine left at zero).
 __global__ void __launch_bounds__(128) k_router(LayerView L, MoeDims d, const void* __restrict__ xr,
                                                 int x_dtype, int T, MoeWork w) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int e = blockIdx.x * 4 + warp;
     const int t0 = blockIdx.y * kTokTile;
     const int t1 = min(T, t0 + kTokTile);
-    if (e < d.E) {
-        const uint4* wrow = reinterpret_cast<const uint4*>(L.router_w + (int64_t)e * d.H);
-        const int nchunk = d.H >> 3;
-        const float bias = L.router_b ? bf16_bits_to_f32(L.router_b[e]) : 0.f;
-        for (int t = t0; t < t1; ++t) {
-            const uint4* xrow = reinterpret_cast<const uint4*>(
-                reinterpret_cast<const char*>(xr) + ((int64_t)t * d.H) * (x_dtype == kF32 ? 4 : 2));
-            float acc = 0.f;
-            for (int c = lane; c < nchunk; c += 32) {
-                const uint4 wv = __ldg(wrow + c);
-                const uint4 xv = __ldg(xrow + c);
-                const uint32_t wr[4] = {wv.x, wv.y, wv.z, wv.w};
-                const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
+    // every warp streams the chunk's x rows (for its expert's dot products,
+    // or only for the row maxima when the CTA has fewer than 4 experts left)
+    const bool has_e = e < d.E;
+    const uint4* wrow = reinterpret_cast<const uint4*>(L.router_w + (int64_t)(has_e ? e : 0) * d.H);
+    const int nchunk = d.H >> 3;
+    float acc[kTokTile], mx[kTokTile];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const float w0 = __uint_as_float(wr[q] << 16);
-                    const float w1 = __uint_as_float(wr[q] & 0xffff0000u);
-                    float x0, x1;
-                    if (x_dtype == kBF16) {
-                        x0 = __uint_as_float(xx[q] << 16);
-                        x1 = __uint_as_float(xx[q] & 0xffff0000u);
-                    } else {
-                        const __half2 h = *reinterpret_cast<const __half2*>(&xx[q]);
-                        x0 = __low2float(h);
-                        x1 = __high2float(h);
-                    }
-                    acc = fmaf(w0, x0, acc);
-                    acc = fmaf(w1, x1, acc);
+    for (int q = 0; q < kTokTile; ++q) acc[q] = mx[q] = 0.f;
+    for (int c = lane; c < nchunk; c += 32) {
+        const uint4 wv = has_e ? __ldg(wrow + c) : make_uint4(0u, 0u, 0u, 0u);
+        const uint32_t wr[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+        for (int q = 0; q < kTokTile; ++q) {
+            if (t0 + q >= t1) break;
+            const uint4 xv = __ldg(reinterpret_cast<const uint4*>(
+                                       static_cast<const char*>(xr) + (int64_t)(t0 + q) * d.H * 2) + c);
+            const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                float x0, x1;
+                if (x_dtype == kBF16) {
+                    x0 = __uint_as_float(xx[u] << 16);
+                    x1 = __uint_as_float(xx[u] & 0xffff0000u);
+                } else {
+                    const __half2 h = *reinterpret_cast<const __half2*>(&xx[u]);
+                    x0 = __low2float(h);
+                    x1 = __high2float(h);
                 }
+                mx[q] = fmaxf(mx[q], fmaxf(fabsf(x0), fabsf(x1)));
+                acc[q] = fmaf(__uint_as_float(wr[u] << 16), x0, acc[q]);
+                acc[q] = fmaf(__uint_as_float(wr[u] & 0xffff0000u), x1, acc[q]);
             }
-            acc = warp_sum(acc);
-            if (lane == 0) w.logits[(int64_t)t * d.E + e] = acc + bias;
         }
     }
+    __shared__ int shift[kTokTile];
+    {
+        const float bias = (has_e && L.router_b) ? bf16_bits_to_f32(L.router_b[e]) : 0.f;
+#pragma unroll
+        for (int q = 0; q < kTokTile; ++q) {
+            if (t0 + q >= t1) break;
+            const float v = warp_sum(acc[q]);
+            const float m = warp_max(mx[q]);
+            if (lane == 0 && has_e) w.logits[(int64_t)(t0 + q) * d.E + e] = v + bias;
+            if (lane == 0 && warp == 0) {
+                const int p = x_dtype == kBF16 ? row_exponent_shift(m) : 0;
+                shift[q] = p;
+                if (blockIdx.x == 0) w.xmul[t0 + q] = pow2f(-p);
+            }
+        }
+    }
+    __syncthreads();
+    // this CTA's share of the chunk's x blocks
+    const int nblk = d.H >> 5;
+    for (int task = blockIdx.x * 4 + warp; task < (t1 - t0) * nblk; task += gridDim.x * 4)
+        prep_block(xr, x_dtype, d.H, t0 + task / nblk, task % nblk, shift[task / nblk], w.x16);
 
     __shared__ int last;
     __shared__ int ord[4][kMaxExperts];
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
-        const unsigned total = gridDim.x * gridDim.y;
-        const unsigned prev = atomicAdd(w.done, 1u);
-        last = (prev == total - 1);
+        const unsigned prev = atomicAdd(w.done + blockIdx.y, 1u);
+        last = (prev == gridDim.x - 1);
     }
     __syncthreads();
     if (!last) return;
     __threadfence();
-    for (int i = threadIdx.x; i < d.E; i += blockDim.x) w.counts[i] = 0;
-    if (threadIdx.x == 0) { *w.nactive = 0; *w.done = 0u; }
-    __syncthreads();
-    for (int t = warp; t < T; t += 4) {
+    if (threadIdx.x == 0) w.done[blockIdx.y] = 0u;
+    for (int t = t0 + warp; t < t1; t += 4) {
         select_topk_warp(w.logits + (int64_t)t * d.E, d.E, d.k, ord[warp],
                          w.experts + (int64_t)t * d.k, w.weights + (int64_t)t * d.k);
         if (lane < d.k) group_slot(d, w, __ldcg(w.experts + (int64_t)t * d.k + lane), t * d.k + lane);
     }
+}
+
+// k_xprep: x row -> f16 with the row's shift (see row_exponent_shift);
+// grid (rows), one CTA per row, row m at x + m * x_stride elements.
+__global__ void k_xprep(const void* __restrict__ x, int64_t x_stride, int x_dtype, int cols,
+                        __half* __restrict__ x16, float* __restrict__ xmul) {
+    const int m = blockIdx.x;
+    const void* xm = static_cast<const char*>(x) + (size_t)m * x_stride * 2;
+    __shared__ float red[32];
+    __shared__ int shift;
+    float mval = 0.f;
+    if (x_dtype == kBF16)
+        for (int i = threadIdx.x; i < cols; i += blockDim.x)
+            mval = fmaxf(mval, fabsf(bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(xm)[i])));
+    mval = warp_max(mval);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mval;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float v = 0.f;
+        for (int i = 0; i < (int)(blockDim.x >> 5); ++i) v = fmaxf(v, red[i]);
+        shift = x_dtype == kBF16 ? row_exponent_shift(v) : 0;
+        xmul[m] = pow2f(-shift);
+    }
+    __syncthreads();
+    const int nblk = cols >> 5;
+    for (int blk = threadIdx.x >> 5; blk < nblk; blk += blockDim.x >> 5)
+        prep_block(xm, x_dtype, cols, 0, blk, shift, x16 + (size_t)m * cols);
 }
 
 // k_group: one CTA; a caller-supplied routing [T][k] (copied into the
@@ -248,22 +256,80 @@ __global__ void __launch_bounds__(256) k_group(MoeDims d, const int32_t* __restr
 }
 
 // ---------------------------------------------------------------------------
-// Grouped expert GEMVs.  grid (min(E, T*k), ceil(tiles / 4)), 4 warps: CTA
-// (a, y) takes the a-th active expert and its 16-row tiles 4y..4y+3, and
-// walks that expert's token list in blocks of 8 tokens staged in shared
-// memory (row stride cols + 32 halves keeps the 16-byte fragment loads
-// conflict-free).  Weight bytes are read once per 8 tokens.
+// Grouped expert GEMVs.  grid (min(E, T*k), ceil(tiles / tiles_per_cta)),
+// 4 warps: CTA (a, y) takes the a-th active expert; each of its warps owns one
+// 16-row tile and a 1/ksplit share of the K blocks (ksplit = 1, 2 or 4 warps
+// per tile, chosen by the host so that few-expert launches still fill the
+// GPU).  As soon as the expert is known every warp queues its weight tile for
+// L2; the expert's tokens are then walked in pairs staged in shared memory,
+// so the tile streams from HBM once and any further pass (an expert chosen by
+// 3+ tokens) hits L2.
 
-__device__ __forceinline__ int xs_stride_for(int cols) { return cols + 32; }
+// Block range of split `sp` out of `ksplit` (multiples of the 8-block group).
+__device__ __forceinline__ void split_range(int nblk, int ksplit, int sp, int& b0, int& b1) {
+    const int groups = (nblk + 7) >> 3;
+    const int per = (groups + ksplit - 1) / ksplit;
+    b0 = min(nblk, sp * per * 8);
+    b1 = min(nblk, (sp + 1) * per * 8);
+}
 
-__device__ __forceinline__ void stage_tokens(__half* xs, int xs_stride, const __half* src_rows,
-                                             const int* row_ids, int n, int cols) {
-    const int chunks = cols >> 3;  // 16-byte chunks per row
-    for (int i = threadIdx.x; i < kTokTile * chunks; i += blockDim.x) {
-        const int r = i / chunks, c = i - r * chunks;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (r < n) v = *reinterpret_cast<const uint4*>(src_rows + (int64_t)row_ids[r] * cols + 8 * c);
-        *reinterpret_cast<uint4*>(xs + r * xs_stride + 8 * c) = v;
+// Runs one token chunk (n = 1..kChunk) of a tile split over `ksplit` warps
+// and calls emit(token, rowA total, rowB total) once per (row pair, token)
+// on the split-0 warp.  Every thread of the CTA must call this (it
+// synchronises when ksplit > 1).
+template <class Emit>
+__device__ __forceinline__ void run_tile(int n, bool valid, const uint8_t* packed,
+                                         const uint8_t* scales, int cols, int rowA, int rowB,
+                                         const __half* xs, int ksplit, Emit&& emit) {
+    __shared__ float red[kGemvWarps][8][2 * kChunk];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int sp = warp % ksplit;
+    int b0, b1;
+    split_range(cols >> 5, ksplit, sp, b0, b1);
+    float a[kChunk], b[kChunk];
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) a[j] = b[j] = 0.f;
+    if (valid) {
+        const int st = diag_stride(cols);
+        if (n == 1) {
+            float a1[1], bb1[1];
+            mxfp4_tile_diag<1, 1>(packed, scales, cols, rowA, rowB, xs, st, 1, b0, b1, a1, bb1);
+            a[0] = a1[0];
+            b[0] = bb1[0];
+        } else if (n == 2) {
+            float a2[2], bb2[2];
+            mxfp4_tile_diag<2, 1>(packed, scales, cols, rowA, rowB, xs, st, 2, b0, b1, a2, bb2);
+            a[0] = a2[0]; a[1] = a2[1];
+            b[0] = bb2[0]; b[1] = bb2[1];
+        } else {
+            mxfp4_tile_diag<2, 2>(packed, scales, cols, rowA, rowB, xs, st, n, b0, b1, a, b);
+        }
+    }
+    if (ksplit > 1) {
+        if (t == 0) {
+#pragma unroll
+            for (int j = 0; j < kChunk; ++j) {
+                red[warp][g][j] = a[j];
+                red[warp][g][kChunk + j] = b[j];
+            }
+        }
+        __syncthreads();
+        if (sp == 0 && t == 0) {
+            for (int q = 1; q < ksplit; ++q) {
+#pragma unroll
+                for (int j = 0; j < kChunk; ++j) {
+                    a[j] += red[warp + q][g][j];
+                    b[j] += red[warp + q][g][kChunk + j];
+                }
+            }
+        }
+        __syncthreads();
+    }
+    if (valid && sp == 0 && t == 0) {
+#pragma unroll
+        for (int j = 0; j < kChunk; ++j)
+            if (j < n) emit(j, a[j], b[j]);
     }
 }
 
@@ -280,118 +346,118 @@ __device__ __forceinline__ float activate(float gate, float up, float limit, flo
     }
 }
 
+
 template <int kAct>
-__global__ void __launch_bounds__(kGemvWarps * 32) k_gateup(LayerView L, MoeDims d, int T, MoeWork w) {
+__global__ void __launch_bounds__(kGemvWarps * 32, 5) k_gateup(LayerView L, MoeDims d, const void* x,
+                                                              int x_dtype, int T, MoeWork w,
+                                                              int ksplit) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     __half* xs = reinterpret_cast<__half*>(smem_raw);
-    __shared__ int rows[kTokTile];
-    __shared__ int slots[kTokTile];
-    __shared__ float xm[kTokTile];
+    __shared__ int rows[kChunk];
+    __shared__ int slots[kChunk];
+    __shared__ float xm[kChunk];
     const int a = blockIdx.x;
     if (a >= *w.nactive) return;
     const int e = w.active[a];
-    const int cnt = min(w.counts[e], w.tcap);
-    const int* list = w.lists + (int64_t)e * w.tcap;
     const uint8_t* ex = L.base + (int64_t)(e / d.shard_count) * L.stride;
     const uint8_t* packed = ex + L.off[0];
     const uint8_t* scales = ex + L.off[1];
     const uint16_t* bias = reinterpret_cast<const uint16_t*>(ex + L.off[4]);
     const int H = d.H, F = d.F;
-    const int xs_stride = xs_stride_for(H);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int g = lane >> 2, t = lane & 3;
-    const int tile = blockIdx.y * kGemvWarps + warp;
+    const int g = lane >> 2;
+    const int tile = blockIdx.y * (kGemvWarps / ksplit) + warp / ksplit;
     const int ntiles = F >> 3;  // 8 output features (16 interleaved rows) per tile
+    const bool valid = tile < ntiles;
     const int f = tile * 8 + g;
-    const int rowA = 2 * f, rowB = rowA + 1;
+    const int rowA = valid ? 2 * f : 0, rowB = rowA + 1;
+    zero_block_init(xs, H);
+    const int cnt = min(w.counts[e], w.tcap);
+    const int* list = w.lists + (int64_t)e * w.tcap;
     float bA = 0.f, bB = 0.f;
-    if (tile < ntiles) { bA = bf16_bits_to_f32(bias[rowA]); bB = bf16_bits_to_f32(bias[rowB]); }
+    if (valid) { bA = bf16_bits_to_f32(bias[rowA]); bB = bf16_bits_to_f32(bias[rowB]); }
 
-    for (int c0 = 0; c0 < cnt; c0 += kTokTile) {
-        const int n = min(kTokTile, cnt - c0);
+    for (int c0 = 0; c0 < cnt;) {
+        const int n = min(kChunk, cnt - c0);
         __syncthreads();
-        if (threadIdx.x < kTokTile) {
+        if (threadIdx.x < kChunk) {
             const int s = threadIdx.x < n ? list[c0 + threadIdx.x] : 0;
             slots[threadIdx.x] = s;
             rows[threadIdx.x] = s / d.k;
             xm[threadIdx.x] = threadIdx.x < n ? w.xmul[s / d.k] : 0.f;
         }
         __syncthreads();
-        stage_tokens(xs, xs_stride, w.x16, rows, n, H);
+        stage_x16(xs, diag_stride(H), w.x16, rows, n, H);
         __syncthreads();
-        if (tile < ntiles) {
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
-            mxfp4_tile<6>(packed, scales, H, rowA, rowB, xs, xs_stride, acc);
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                const int col = 2 * t + q;
-                if (col < n) {
-                    const float gate = acc[q] * xm[col] + bA;
-                    const float up = acc[2 + q] * xm[col] + bB;
-                    const float v = activate<kAct>(gate, up, d.limit, d.alpha);
-                    w.act[(int64_t)slots[col] * F + f] = __float2half_rn(v);
-                }
-            }
-        }
+        run_tile(n, valid, packed, scales, H, rowA, rowB, xs, ksplit,
+                 [&](int col, float ga, float ub) {
+                     const float v = activate<kAct>(ga * xm[col] + bA, ub * xm[col] + bB, d.limit, d.alpha);
+                     w.act[(int64_t)slots[col] * F + f] = __float2half_rn(v);
+                 });
+        c0 += n;
     }
 }
 
-__global__ void __launch_bounds__(kGemvWarps * 32) k_down(LayerView L, MoeDims d, int T, MoeWork w) {
+__global__ void __launch_bounds__(kGemvWarps * 32, 5) k_down(LayerView L, MoeDims d, int T, MoeWork w,
+                                                            int ksplit) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     __half* xs = reinterpret_cast<__half*>(smem_raw);
-    __shared__ int slots[kTokTile];
-    __shared__ float wt[kTokTile];
+    __shared__ int slots[kChunk];
+    __shared__ float wt[kChunk];
     const int a = blockIdx.x;
     if (a >= *w.nactive) return;
     const int e = w.active[a];
-    const int cnt = min(w.counts[e], w.tcap);
-    const int* list = w.lists + (int64_t)e * w.tcap;
     const uint8_t* ex = L.base + (int64_t)(e / d.shard_count) * L.stride;
     const uint8_t* packed = ex + L.off[2];
     const uint8_t* scales = ex + L.off[3];
     const uint16_t* bias = reinterpret_cast<const uint16_t*>(ex + L.off[5]);
     const int H = d.H, F = d.F;
-    const int xs_stride = xs_stride_for(F);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int g = lane >> 2, t = lane & 3;
-    const int tile = blockIdx.y * kGemvWarps + warp;
+    const int g = lane >> 2;
+    const int tile = blockIdx.y * (kGemvWarps / ksplit) + warp / ksplit;
     const int ntiles = H >> 4;
-    const int rowA = tile * 16 + g, rowB = rowA + 8;
+    const bool valid = tile < ntiles;
+    const int rowA = valid ? tile * 16 + g : 0, rowB = rowA + 8;
+    zero_block_init(xs, F);
+    const int cnt = min(w.counts[e], w.tcap);
+    const int* list = w.lists + (int64_t)e * w.tcap;
     float bA = 0.f, bB = 0.f;
-    if (tile < ntiles) { bA = bf16_bits_to_f32(bias[rowA]); bB = bf16_bits_to_f32(bias[rowB]); }
+    if (valid) { bA = bf16_bits_to_f32(bias[rowA]); bB = bf16_bits_to_f32(bias[rowB]); }
 
-    for (int c0 = 0; c0 < cnt; c0 += kTokTile) {
-        const int n = min(kTokTile, cnt - c0);
+    for (int c0 = 0; c0 < cnt;) {
+        const int n = min(kChunk, cnt - c0);
         __syncthreads();
-        if (threadIdx.x < kTokTile) {
+        if (threadIdx.x < kChunk) {
             const int s = threadIdx.x < n ? list[c0 + threadIdx.x] : 0;
             slots[threadIdx.x] = s;
             wt[threadIdx.x] = threadIdx.x < n ? w.weights[s] : 0.f;
         }
         __syncthreads();
-        stage_tokens(xs, xs_stride, w.act, slots, n, F);
+        stage_x16(xs, diag_stride(F), w.act, slots, n, F);
         __syncthreads();
-        if (tile < ntiles) {
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
-            mxfp4_tile<6>(packed, scales, F, rowA, rowB, xs, xs_stride, acc);
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                const int col = 2 * t + q;
-                if (col < n) {
-                    float* y = w.ybuf + (int64_t)slots[col] * H;
-                    y[rowA] = (acc[q] + bA) * wt[col];
-                    y[rowB] = (acc[2 + q] + bB) * wt[col];
-                }
-            }
-        }
+        run_tile(n, valid, packed, scales, F, rowA, rowB, xs, ksplit,
+                 [&](int col, float ya, float yb) {
+                     float* y = w.ybuf + (int64_t)slots[col] * H;
+                     y[rowA] = (ya + bA) * wt[col];
+                     y[rowB] = (yb + bB) * wt[col];
+                 });
+        c0 += n;
     }
 }
 
-// k_combine: out[t][h] (=|+=) sum over ranks j of ybuf[t*k+j][h], skipping
-// slots whose expert this shard does not own.  grid (ceil(H/4/256), T).
-__global__ void k_combine(MoeDims d, MoeWork w, float* __restrict__ out, int accumulate) {
+// k_combine: s = sum over ranks j of ybuf[t*k+j] (skipping slots whose expert
+// this shard does not own); out (=|+=) s; if x_next, x_next = round(out) in
+// x_dtype.  grid (ceil(H/4/256), T).
+__global__ void k_combine(MoeDims d, MoeWork w, float* __restrict__ out, int accumulate,
+                          void* __restrict__ x_next, int x_dtype) {
     const int t = blockIdx.y;
     const int h4 = blockIdx.x * blockDim.x + threadIdx.x;
+    // the expert lists have been consumed: leave the counts at zero for the
+    // next router launch
+    if (blockIdx.x == 0 && blockIdx.y == 0) {
+        for (int i = threadIdx.x; i < d.E; i += blockDim.x) w.counts[i] = 0;
+        if (threadIdx.x == 0) *w.nactive = 0;
+    }
     if (h4 * 4 >= d.H) return;
     float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int j = 0; j < d.k; ++j) {
@@ -402,53 +468,53 @@ __global__ void k_combine(MoeDims d, MoeWork w, float* __restrict__ out, int acc
     }
     float4* o = reinterpret_cast<float4*>(out + (int64_t)t * d.H) + h4;
     if (accumulate) {
-        float4 p = *o;
-        p.x += s.x; p.y += s.y; p.z += s.z; p.w += s.w;
-        *o = p;
-    } else {
-        *o = s;
+        const float4 p = *o;
+        s.x += p.x; s.y += p.y; s.z += p.z; s.w += p.w;
+    }
+    *o = s;
+    if (x_next) {
+        const int64_t i = (int64_t)t * d.H + 4 * h4;
+        store_act(x_next, x_dtype, i, s.x);
+        store_act(x_next, x_dtype, i + 1, s.y);
+        store_act(x_next, x_dtype, i + 2, s.z);
+        store_act(x_next, x_dtype, i + 3, s.w);
     }
 }
 
 // ---------------------------------------------------------------------------
-// k_gemv: batched plain GEMV, y = dequant(W) x * xmul + bias.
-// grid (count, ceil(rows/16/4)), 4 warps, one 16-row tile per warp.
-__global__ void __launch_bounds__(kGemvWarps * 32) k_gemv(
+// k_gemv: batched plain GEMV, y = dequant(W) x + bias.  grid (count,
+// ceil(rows/16/4)), 4 warps, one 16-row tile per warp, the block-diagonal
+// single-token tile; x (f16 or bf16) is staged with per-block scales.
+__global__ void __launch_bounds__(kGemvWarps * 32, 6) k_gemv(
     const uint8_t* __restrict__ packed, int64_t packed_stride, const uint8_t* __restrict__ scales,
     int64_t scale_stride, const uint16_t* __restrict__ bias, int64_t bias_stride,
-    const __half* __restrict__ x16, int64_t x_stride, const float* __restrict__ xmul,
+    const __half* __restrict__ x16, const float* __restrict__ xmul, int x_stride,
     float* __restrict__ y, int64_t y_stride, int rows, int cols) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     __half* xs = reinterpret_cast<__half*>(smem_raw);
     const int m = blockIdx.x;
-    const int xs_stride = xs_stride_for(cols);
-    const int row_id = (x_stride == 0) ? 0 : m;
-    const int chunks = cols >> 3;
-    const __half* xsrc = x16 + (int64_t)row_id * cols;
-    for (int i = threadIdx.x; i < kTokTile * chunks; i += blockDim.x) {
-        const int r = i / chunks, c = i - r * chunks;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (r == 0) v = *reinterpret_cast<const uint4*>(xsrc + 8 * c);
-        *reinterpret_cast<uint4*>(xs + r * xs_stride + 8 * c) = v;
-    }
-    __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
     const int tile = blockIdx.y * kGemvWarps + warp;
-    if (tile * 16 >= rows) return;
-    int rowA = tile * 16 + g, rowB = rowA + 8;
+    const int rowA = tile * 16 + g, rowB = rowA + 8;
     const bool okA = rowA < rows, okB = rowB < rows;
     // Rows past the end read a valid row (row 0) and are not stored.
     const int rA = okA ? rowA : 0, rB = okB ? rowB : 0;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    mxfp4_tile<6>(packed + m * packed_stride, scales + m * scale_stride, cols, rA, rB, xs,
-                  xs_stride, acc);
+    const uint8_t* pm = packed + m * packed_stride;
+    const int xrow = x_stride == 0 ? 0 : m;
+    zero_block_init(xs, cols);
+    stage_x16(xs, diag_stride(cols), x16, &xrow, 1, cols);
+    __syncthreads();
+    if (tile * 16 >= rows) return;
+    float a[1], b[1];
+    mxfp4_tile_diag<1, 1>(pm, scales + m * scale_stride, cols, rA, rB, xs, diag_stride(cols), 1, 0,
+                          cols >> 5, a, b);
     if (t == 0) {
-        const float mul = xmul[row_id];
         const uint16_t* bm = bias ? bias + m * bias_stride : nullptr;
+        const float mul = xmul[xrow];
         float* ym = y + m * y_stride;
-        if (okA) ym[rowA] = acc[0] * mul + (bm ? bf16_bits_to_f32(bm[rowA]) : 0.f);
-        if (okB) ym[rowB] = acc[2] * mul + (bm ? bf16_bits_to_f32(bm[rowB]) : 0.f);
+        if (okA) ym[rowA] = a[0] * mul + (bm ? bf16_bits_to_f32(bm[rowA]) : 0.f);
+        if (okB) ym[rowB] = b[0] * mul + (bm ? bf16_bits_to_f32(bm[rowB]) : 0.f);
     }
 }
 
@@ -469,23 +535,26 @@ __global__ void k_dequant(const uint8_t* __restrict__ packed, const uint8_t* __r
 // k_fill: synthetic bank bytes from the counter hash (see mix64).
 __global__ void k_fill(uint8_t* __restrict__ dst, int64_t n, uint64_t key, int kind) {
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-        if (kind == kFillCodes) {
-            dst[i] = (uint8_t)(mix64(key + (uint64_t)(i >> 3)) >> (8 * (i & 7)));
-        } else if (kind == kFillScales) {
-            dst[i] = (uint8_t)(118 + mix64(key + (uint64_t)i) % 7);
-        } else if (kind == kFillZero) {
-            dst[i] = 0;
-        } else if ((i & 1) == 0) {  // bf16 ~N(0, 0.02), one value per 2 bytes
-            const uint64_t j = (uint64_t)(i >> 1);
-            const double u1 = ((double)(mix64(key + 2 * j) >> 11) + 0.5) * (1.0 / 9007199254740992.0);
-            const double u2 = (double)(mix64(key + 2 * j + 1) >> 11) * (1.0 / 9007199254740992.0);
+    const int64_t first = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (kind == kFillBf16Normal) {  // bf16 ~N(0, 0.02), one value per 2 bytes
+        uint16_t* out = reinterpret_cast<uint16_t*>(dst);
+        for (int64_t j = first; j < n / 2; j += stride) {
+            const uint64_t u = (uint64_t)j;
+            const double u1 = ((double)(mix64(key + 2 * u) >> 11) + 0.5) * (1.0 / 9007199254740992.0);
+            const double u2 = (double)(mix64(key + 2 * u + 1) >> 11) * (1.0 / 9007199254740992.0);
             const double z = sqrt(-2.0 * log(u1)) * cos(6.283185307179586 * u2) * 0.02;
-            const __nv_bfloat16 b = __double2bfloat16(z);
-            const uint16_t bits = *reinterpret_cast<const uint16_t*>(&b);
-            dst[i] = (uint8_t)(bits & 0xff);
-            if (i + 1 < n) dst[i + 1] = (uint8_t)(bits >> 8);
+            // double -> fp32 (nearest) -> bf16 (nearest even), mirrored on the host
+            out[j] = __bfloat16_as_ushort(__float2bfloat16_rn((float)z));
         }
+        return;
+    }
+    for (int64_t i = first; i < n; i += stride) {
+        if (kind == kFillCodes)
+            dst[i] = (uint8_t)(mix64(key + (uint64_t)(i >> 3)) >> (8 * (i & 7)));
+        else if (kind == kFillScales)
+            dst[i] = (uint8_t)(118 + mix64(key + (uint64_t)i) % 7);
+        else
+            dst[i] = 0;
     }
 }
 
@@ -510,12 +579,25 @@ __global__ void k_widen(const void* __restrict__ x, int x_dtype, float* __restri
 
 inline int ok_or_fail() { return cudaPeekAtLastError() == cudaSuccess ? 1 : -1; }
 
+// Warps per tile: split K when the expert work alone cannot fill the GPU
+// (batch-1 decode runs only top_k experts per layer).
+int pick_ksplit(int tiles_total) {
+    const int target = 148 * 32;  // warps in flight
+    if (tiles_total >= target) return 1;
+    if (tiles_total * 2 >= target) return 2;
+    return 4;
+}
+
 }  // namespace
 
-size_t gemv_smem_bytes(int cols) { return (size_t)kTokTile * (cols + 32) * sizeof(__half); }
+// Dynamic shared bytes of the expert kernels for `cols`-wide inputs.
+size_t gemv_smem_bytes(int cols, int max_tok) {
+    const size_t diag = (size_t)(cols / 32 + 1) * kXBlockHalves * sizeof(__half);
+    return (size_t)std::min(std::max(max_tok, 1), kChunk) * diag;
+}
 
 int configure_kernels() {
-    const int max_smem = 200 * 1024;
+    const int max_smem = 64 * 1024;
     if (cudaFuncSetAttribute(k_gateup<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem) != cudaSuccess) return -1;
     if (cudaFuncSetAttribute(k_gateup<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem) != cudaSuccess) return -1;
     if (cudaFuncSetAttribute(k_down, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem) != cudaSuccess) return -1;
@@ -523,17 +605,10 @@ int configure_kernels() {
     return 0;
 }
 
-int launch_prep(const void* src, int src_dtype, int round_dtype, int T, int H, void* xr_out,
-                __half* x16, float* xmul, cudaStream_t s) {
-    if (T <= 0) return 0;
-    k_prep<<<T, 256, 0, s>>>(src, src_dtype, round_dtype, H, xr_out, x16, xmul);
-    return ok_or_fail();
-}
-
-int launch_router(const LayerView& L, const MoeDims& d, const void* xr, int x_dtype, int T,
+int launch_router(const LayerView& L, const MoeDims& d, const void* x, int x_dtype, int T,
                   const MoeWork& w, cudaStream_t s) {
     dim3 grid((d.E + 3) / 4, (T + kTokTile - 1) / kTokTile);
-    k_router<<<grid, 128, 0, s>>>(L, d, xr, x_dtype, T, w);
+    k_router<<<grid, 128, 0, s>>>(L, d, x, x_dtype, T, w);
     return ok_or_fail();
 }
 
@@ -543,44 +618,58 @@ int launch_group(const MoeDims& d, const int32_t* experts_in, const float* weigh
     return ok_or_fail();
 }
 
-int launch_gateup(const LayerView& L, const MoeDims& d, int T, const MoeWork& w,
-                  cudaStream_t s) {
+int launch_gateup(const LayerView& L, const MoeDims& d, const void* x, int x_dtype, int T,
+                  const MoeWork& w, cudaStream_t s) {
     const int maxa = min(d.E, T * d.k);
     const int tiles = d.F / 8;
-    dim3 grid(maxa, (tiles + kGemvWarps - 1) / kGemvWarps);
+    const int ks = pick_ksplit(tiles * maxa);
+    const int per = kGemvWarps / ks;
+    dim3 grid(maxa, (tiles + per - 1) / per);
+    const size_t sm = gemv_smem_bytes(d.H, T);
     if (d.act == 0)
-        k_gateup<0><<<grid, kGemvWarps * 32, gemv_smem_bytes(d.H), s>>>(L, d, T, w);
+        k_gateup<0><<<grid, kGemvWarps * 32, sm, s>>>(L, d, x, x_dtype, T, w, ks);
     else
-        k_gateup<1><<<grid, kGemvWarps * 32, gemv_smem_bytes(d.H), s>>>(L, d, T, w);
+        k_gateup<1><<<grid, kGemvWarps * 32, sm, s>>>(L, d, x, x_dtype, T, w, ks);
     return ok_or_fail();
 }
 
 int launch_down(const LayerView& L, const MoeDims& d, int T, const MoeWork& w, cudaStream_t s) {
     const int maxa = min(d.E, T * d.k);
     const int tiles = d.H / 16;
-    dim3 grid(maxa, (tiles + kGemvWarps - 1) / kGemvWarps);
-    k_down<<<grid, kGemvWarps * 32, gemv_smem_bytes(d.F), s>>>(L, d, T, w);
+    const int ks = pick_ksplit(tiles * maxa);
+    const int per = kGemvWarps / ks;
+    dim3 grid(maxa, (tiles + per - 1) / per);
+    k_down<<<grid, kGemvWarps * 32, gemv_smem_bytes(d.F, T), s>>>(L, d, T, w, ks);
     return ok_or_fail();
 }
 
 int launch_combine(const MoeDims& d, int T, const MoeWork& w, float* out, int accumulate,
-                   cudaStream_t s) {
+                   void* x_next, int x_dtype, cudaStream_t s) {
     dim3 grid((d.H / 4 + 255) / 256, T);
-    k_combine<<<grid, 256, 0, s>>>(d, w, out, accumulate);
+    k_combine<<<grid, 256, 0, s>>>(d, w, out, accumulate, x_next, x_dtype);
+    return ok_or_fail();
+}
+
+int launch_xprep(const void* x, int x_dtype, int T, int H, __half* x16, float* xmul,
+                 cudaStream_t s) {
+    k_xprep<<<T, 256, 0, s>>>(x, H, x_dtype, H, x16, xmul);
     return ok_or_fail();
 }
 
 int launch_gemv_batched(int count, const uint8_t* packed, int64_t packed_stride,
                         const uint8_t* scales, int64_t scale_stride, const uint16_t* bias,
-                        int64_t bias_stride, const __half* x16, int64_t x_stride,
-                        const float* xmul, float* y, int64_t y_stride, int rows, int cols,
+                        int64_t bias_stride, const void* x, int64_t x_stride, int x_dtype,
+                        __half* x16, float* xmul, float* y, int64_t y_stride, int rows, int cols,
                         cudaStream_t s) {
+    const int nx = x_stride == 0 ? 1 : count;
+    k_xprep<<<nx, 256, 0, s>>>(x, x_stride, x_dtype, cols, x16, xmul);
+    if (cudaPeekAtLastError() != cudaSuccess) return -1;
     const int tiles = (rows + 15) / 16;
     dim3 grid(count, (tiles + kGemvWarps - 1) / kGemvWarps);
-    k_gemv<<<grid, kGemvWarps * 32, gemv_smem_bytes(cols), s>>>(
-        packed, packed_stride, scales, scale_stride, bias, bias_stride, x16, x_stride, xmul, y,
-        y_stride, rows, cols);
-    return ok_or_fail();
+    k_gemv<<<grid, kGemvWarps * 32, gemv_smem_bytes(cols, 1), s>>>(
+        packed, packed_stride, scales, scale_stride, bias, bias_stride, x16, xmul,
+        x_stride == 0 ? 0 : 1, y, y_stride, rows, cols);
+    return cudaPeekAtLastError() == cudaSuccess ? 2 : -1;
 }
 
 int launch_dequant(const uint8_t* packed, const uint8_t* scales, int rows, int cols, float* w,

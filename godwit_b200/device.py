@@ -29,9 +29,19 @@ def dtype_code(t: torch.Tensor) -> int:
         raise _abi.GodwitCUDAError(_abi.GW_E_ARG, f"unsupported activation dtype {t.dtype}") from None
 
 
-def bind_stream(ctx: Context, stream: torch.cuda.Stream | None = None) -> None:
+def bind_stream(ctx: Context, stream: torch.cuda.Stream | None = None) -> torch.cuda.Stream:
+    """Orders the library's work on `stream` (default: torch's current stream).
+
+    The legacy default stream has handle 0, which the C-ABI reads as "the
+    context's own stream"; in that case a dedicated torch stream is created and
+    made current, so torch ops, CUDA events and the library share one stream.
+    """
     s = stream or torch.cuda.current_stream(ctx.device)
+    if s.cuda_stream == 0:
+        s = torch.cuda.Stream(device=ctx.device)
+        torch.cuda.set_stream(s)
     ctx.set_stream(s.cuda_stream)
+    return s
 
 
 def gemv_batched(ctx: Context, packed: torch.Tensor, scales: torch.Tensor, bias: torch.Tensor | None,

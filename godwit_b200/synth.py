@@ -70,8 +70,8 @@ def hash_bf16_normal(key: int, count: int, std: float = 0.02) -> np.ndarray:
         u1 = ((mix64(k + np.uint64(2) * j) >> np.uint64(11)).astype(np.float64) + 0.5) / 2.0 ** 53
         u2 = (mix64(k + np.uint64(2) * j + np.uint64(1)) >> np.uint64(11)).astype(np.float64) / 2.0 ** 53
     z = np.sqrt(-2.0 * np.log(u1)) * np.cos(2.0 * np.pi * u2) * std
-    # the device converts float64 -> bf16 directly (round to nearest even)
-    return f64_to_bf16_bits(z)
+    # as the device: float64 -> fp32 (nearest), then fp32 -> bf16 (nearest even)
+    return f32_to_bf16_bits(z.astype(np.float32))
 
 
 def f64_to_bf16_bits(z: np.ndarray) -> np.ndarray:

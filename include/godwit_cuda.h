@@ -234,6 +234,10 @@ typedef struct gw_profile {
     double  gemv_ms;
     int64_t expert_passes;     /* sum over profiled layers of experts streamed */
     int64_t gemv_matrices;     /* matrices processed by the profiled GEMVs    */
+    int64_t router_launches;   /* router + top-k (or grouping) kernels        */
+    int64_t combine_launches;  /* combine (+ residual) kernels                */
+    double  router_ms;
+    double  combine_ms;
 } gw_profile;
 /* Enables (1) or disables (0) kernel timing; enabling clears the counters. */
 GW_API gw_status gw_profile_enable(gw_ctx* ctx, int32_t enable);
