@@ -83,6 +83,17 @@ struct gw_ctx {
     DevBuf nlog;              // nactive per profiled layer
     int nlog_used = 0;
     gw_profile acc{};
+    // CUDA graph of the last stack forward (replayed while its inputs match)
+    struct StackGraph {
+        cudaGraphExec_t exec = nullptr;
+        const void* bank = nullptr;
+        const void* x = nullptr;
+        const float* stream = nullptr;
+        cudaStream_t on = nullptr;
+        int T = 0, dtype = -1;
+        int64_t kernels = 0;
+        void* work = nullptr;
+    } graph;
 };
 
 struct gw_bank {
@@ -342,6 +353,7 @@ gw_status gw_shutdown(gw_ctx* c) {
         cudaSetDevice(c->device);
         cudaStreamSynchronize(c->cur);
         drop_timed(c);
+        if (c->graph.exec) cudaGraphExecDestroy(c->graph.exec);
         c->nlog.release();
         c->work.release();
         c->staging.release();
@@ -517,6 +529,10 @@ gw_status gw_bank_destroy(gw_bank* b) {
     if (!b) return fail(GW_E_ARG, "null bank");
     if (b->ctx) {
         CtxLock lk(b->ctx);
+        if (b->ctx->graph.bank == b) {
+            if (b->ctx->graph.exec) cudaGraphExecDestroy(b->ctx->graph.exec);
+            b->ctx->graph = gw_ctx::StackGraph{};
+        }
         cudaSetDevice(b->ctx->device);
         cudaStreamSynchronize(b->ctx->cur);
         for (uint8_t* p : b->layer_mem)
@@ -662,15 +678,56 @@ gw_status gw_moe_stack_forward_async(gw_ctx* c, gw_bank* b, const void* x_dev, i
     const int64_t n = (int64_t)T * b->d.hidden;
     // stream = x widened to fp32; then stream += moe_l(round(stream)) per layer.
     // Each layer's combine writes round(stream) into the workspace's x buffer,
-    // which is the next layer's input.
+    // which is the next layer's input.  The launch sequence is captured once
+    // as a CUDA graph and replayed while the bank, buffers, stream and T are
+    // unchanged (profiling runs launch eagerly so each kernel can be timed).
     if ((st = ensure_work(c, b, T))) return st;
-    if ((st = count(c, gw::launch_widen(x_dev, x_dtype, stream_dev, n, c->cur)))) return st;
-    for (int l = 0; l < b->d.layers; ++l) {
-        const void* src = (l == 0) ? x_dev : c->w.xr;
-        void* next = (l + 1 < b->d.layers) ? c->w.xr : nullptr;
-        st = moe_layer_device(c, b, l, src, x_dtype, T, nullptr, nullptr, stream_dev, 1, next);
-        if (st) return st;
+    auto enqueue = [&]() -> gw_status {
+        gw_status s2 = count(c, gw::launch_widen(x_dev, x_dtype, stream_dev, n, c->cur));
+        if (s2) return s2;
+        for (int l = 0; l < b->d.layers; ++l) {
+            const void* src = (l == 0) ? x_dev : c->w.xr;
+            void* next = (l + 1 < b->d.layers) ? c->w.xr : nullptr;
+            s2 = moe_layer_device(c, b, l, src, x_dtype, T, nullptr, nullptr, stream_dev, 1, next);
+            if (s2) return s2;
+        }
+        return GW_OK;
+    };
+    if (c->prof) return enqueue();
+    auto& g = c->graph;
+    const bool hit = g.exec && g.bank == b && g.x == x_dev && g.stream == stream_dev &&
+                     g.on == c->cur && g.T == T && g.dtype == x_dtype && g.work == c->work.p;
+    if (!hit) {
+        if (g.exec) cudaGraphExecDestroy(g.exec);
+        g.exec = nullptr;
+        const int64_t before = c->launches;
+        GW_CUDA(cudaStreamBeginCapture(c->cur, cudaStreamCaptureModeThreadLocal));
+        st = enqueue();
+        cudaGraph_t graph = nullptr;
+        cudaError_t e = cudaStreamEndCapture(c->cur, &graph);
+        if (st) {
+            if (graph) cudaGraphDestroy(graph);
+            return st;
+        }
+        if (e != cudaSuccess) return cuda_fail(e, "stack graph capture");
+        e = cudaGraphInstantiate(&g.exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (e != cudaSuccess) {
+            g.exec = nullptr;
+            return cuda_fail(e, "stack graph instantiation");
+        }
+        g.kernels = c->launches - before;
+        c->launches = before;
+        g.bank = b;
+        g.x = x_dev;
+        g.stream = stream_dev;
+        g.on = c->cur;
+        g.T = T;
+        g.dtype = x_dtype;
+        g.work = c->work.p;
     }
+    GW_CUDA(cudaGraphLaunch(g.exec, c->cur));
+    c->launches += g.kernels;
     return GW_OK;
 }
 
