@@ -99,6 +99,7 @@ class Profile(C.Structure):
                 ("combine_ms", C.c_double)]
 
 
+SIGNATURES["gw_moe_forward_noalloc_async"] = (ST, [P, P, I32, P, I32, I32, P, P, P])
 SIGNATURES["gw_profile_enable"] = (ST, [P, I32])
 SIGNATURES["gw_profile_read"] = (ST, [P, C.POINTER(Profile)])
 

@@ -997,3 +997,108 @@ gw_status gw_expert_apply(gw_ctx* c, gw_bank* b, int32_t layer, int32_t expert, 
 }
 
 }  // extern "C"
+
+// ---- MoE layer without allocation ------------------------------------------
+//
+// For callers that cannot allocate device memory while they run a layer: an
+// engine that plans all of its memory up front and forbids allocation in the
+// serving loop, a caller running under a driver-level memory cap, or one that
+// must not let a first-call allocation stall or fail mid-request.  Their layer
+// scratch lives in this fixed device array instead of the context workspace.
+// Every device that loads the library holds these bytes until the process
+// exits.
+
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;  // 4 MiB
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of the scratch array on `device` (current), resolved once.
+gw_status noalloc_scratch(int device, void** out) {
+    if (device < 0 || device >= kNoAllocMaxDevices)
+        return fail(GW_E_UNSUPPORTED, "device %d beyond the no-allocation path's device table", device);
+    std::lock_guard<std::mutex> g(g_noalloc_mu);
+    if (!g_noalloc_ptr[device]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-allocation scratch)");
+        g_noalloc_ptr[device] = p;
+    }
+    *out = g_noalloc_ptr[device];
+    return GW_OK;
+}
+
+}  // namespace
+
+extern "C" GW_API gw_status gw_moe_forward_noalloc_async(gw_ctx* c, gw_bank* b, int32_t layer,
+                                                          const void* x_dev, int32_t x_dtype,
+                                                          int32_t T, float* out_dev,
+                                                          int32_t* experts_dev,
+                                                          float* weights_dev) {
+    if (!c || !x_dev || !out_dev) return fail(GW_E_ARG, "null argument");
+    gw_status st = check_bank(b, layer);
+    if (st || (st = check_dtype(x_dtype))) return st;
+    if (T <= 0) return fail(GW_E_ARG, "T must be positive");
+    const int H = b->d.hidden, F = b->d.intermediate, E = b->d.experts, k = b->d.top_k;
+    // the same scratch carve-up as the context workspace, sized for exactly T
+    size_t off = 0;
+    auto take = [&](size_t bytes) { size_t o = off; off += align256(bytes); return o; };
+    const size_t o_x16 = take((size_t)T * H * 2);
+    const size_t o_xmul = take((size_t)T * 4);
+    const size_t o_logits = take((size_t)T * E * 4);
+    const size_t o_experts = take((size_t)T * k * 4);
+    const size_t o_weights = take((size_t)T * k * 4);
+    const size_t o_counts = take((size_t)E * 4);
+    const size_t o_active = take((size_t)E * 4);
+    const size_t o_nactive = take(4);
+    const size_t o_lists = take((size_t)E * T * 4);
+    const size_t o_act = take((size_t)T * k * F * 2);
+    const size_t o_ybuf = take((size_t)T * k * H * 4);
+    const size_t o_done = take((size_t)(T / 8 + 1) * 4);
+    if (off > kNoAllocScratchBytes)
+        return fail(GW_E_ARG,
+                    "T=%d needs %zu bytes of layer scratch; the no-allocation path holds %zu "
+                    "(use gw_moe_forward_async, or fewer tokens per call)",
+                    T, off, kNoAllocScratchBytes);
+    CtxLock lk(c);
+    if ((st = set_device(c))) return st;
+    void* scratch = nullptr;
+    if ((st = noalloc_scratch(c->device, &scratch))) return st;
+    char* base = static_cast<char*>(scratch);
+    gw::MoeWork w{};
+    w.tcap = T;
+    w.xr = nullptr;
+    w.x16 = reinterpret_cast<__half*>(base + o_x16);
+    w.xmul = reinterpret_cast<float*>(base + o_xmul);
+    w.logits = reinterpret_cast<float*>(base + o_logits);
+    w.experts = reinterpret_cast<int32_t*>(base + o_experts);
+    w.weights = reinterpret_cast<float*>(base + o_weights);
+    w.counts = reinterpret_cast<int32_t*>(base + o_counts);
+    w.active = reinterpret_cast<int32_t*>(base + o_active);
+    w.nactive = reinterpret_cast<int32_t*>(base + o_nactive);
+    w.lists = reinterpret_cast<int32_t*>(base + o_lists);
+    w.act = reinterpret_cast<__half*>(base + o_act);
+    w.ybuf = reinterpret_cast<float*>(base + o_ybuf);
+    w.done = reinterpret_cast<unsigned*>(base + o_done);
+    // The array keeps whatever the previous call left: clear the expert counts,
+    // the active-expert count and the router completion counters.
+    GW_CUDA(cudaMemsetAsync(base + o_counts, 0, (size_t)E * 4, c->cur));
+    GW_CUDA(cudaMemsetAsync(base + o_nactive, 0, 4, c->cur));
+    GW_CUDA(cudaMemsetAsync(base + o_done, 0, (size_t)(T / 8 + 1) * 4, c->cur));
+    const gw::MoeDims d = dims_of(b);
+    const gw::LayerView L = layer_of(b, layer);
+    if ((st = count(c, gw::launch_router(L, d, x_dev, x_dtype, T, w, c->cur)))) return st;
+    if ((st = count(c, gw::launch_gateup(L, d, x_dev, x_dtype, T, w, c->cur)))) return st;
+    if ((st = count(c, gw::launch_down(L, d, T, w, c->cur)))) return st;
+    if ((st = count(c, gw::launch_combine(d, T, w, out_dev, 0, nullptr, x_dtype, c->cur)))) return st;
+    const size_t nk = (size_t)T * k;
+    if (experts_dev)
+        GW_CUDA(cudaMemcpyAsync(experts_dev, w.experts, nk * 4, cudaMemcpyDeviceToDevice, c->cur));
+    if (weights_dev)
+        GW_CUDA(cudaMemcpyAsync(weights_dev, w.weights, nk * 4, cudaMemcpyDeviceToDevice, c->cur));
+    return GW_OK;
+}

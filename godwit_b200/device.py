@@ -63,6 +63,16 @@ def moe_forward(ctx: Context, bank: ExpertBank, layer: int, x: torch.Tensor, out
          _p(experts), _p(weights))
 
 
+def moe_forward_noalloc(ctx: Context, bank: ExpertBank, layer: int, x: torch.Tensor,
+                        out: torch.Tensor, experts: torch.Tensor | None = None,
+                        weights: torch.Tensor | None = None) -> None:
+    """moe_forward without any device allocation: the layer's scratch is the
+    library's fixed device array (for callers that plan memory up front or may
+    not allocate while serving).  Limited to small T; calls must not overlap."""
+    call("gw_moe_forward_noalloc_async", ctx.handle, bank.handle, layer, _p(x), dtype_code(x),
+         x.shape[0], _p(out), _p(experts), _p(weights))
+
+
 def moe_apply(ctx: Context, bank: ExpertBank, layer: int, x: torch.Tensor, experts: torch.Tensor,
               weights: torch.Tensor, out: torch.Tensor, accumulate: bool = False) -> None:
     call("gw_moe_apply_async", ctx.handle, bank.handle, layer, _p(x), dtype_code(x), x.shape[0],

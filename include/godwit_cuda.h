@@ -223,6 +223,22 @@ GW_API gw_status gw_moe_apply_async(gw_ctx* ctx, gw_bank* bank, int32_t layer,
  * residual add of TransformerLayer.forward (Runtime/TransformerLayer.swift:232-238). */
 GW_API gw_status gw_residual_round_async(gw_ctx* ctx, float* stream_dev, const float* delta_dev,
                                   void* x_out_dev, int32_t x_dtype, int64_t n);
+/* One MoE layer that allocates no device memory, for callers that cannot
+ * allocate while serving (memory planned up front, a hard memory cap, or no
+ * tolerance for a first-call allocation).  No counterpart in the reference.
+ * Same arguments and results as gw_moe_forward_async; the layer's scratch
+ * lives in a fixed 4 MiB device array that every device loading this library
+ * holds until the process exits, so the token count is limited to what fits
+ * (up to T=55 at GPT-OSS shapes, 50 at Qwen3-30B-A3B shapes); larger T is
+ * rejected with GW_E_ARG.  The first
+ * call on a device resolves the array's address (cudaGetSymbolAddress); make
+ * that first call before any stream capture.  All calls share the array:
+ * calls that overlap on the GPU (other streams, other contexts of the same
+ * device) race. */
+GW_API gw_status gw_moe_forward_noalloc_async(gw_ctx* ctx, gw_bank* bank, int32_t layer,
+                                              const void* x_dev, int32_t x_dtype, int32_t T,
+                                              float* out_dev, int32_t* experts_dev,
+                                              float* weights_dev);
 /* Kernel timing recorded with CUDA events on the context's stream around
  * each expert GEMV launch while profiling is enabled. */
 typedef struct gw_profile {
