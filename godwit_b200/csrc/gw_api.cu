@@ -104,6 +104,7 @@ struct gw_bank {
     uint16_t* router_w = nullptr;     // [L][E][H]
     uint16_t* router_b = nullptr;     // [L][E]
     int64_t bytes = 0;
+    DevBuf stage;                     // one stride in the reference layout (upload/download/fill)
 };
 
 namespace {
@@ -539,6 +540,7 @@ gw_status gw_bank_destroy(gw_bank* b) {
             if (p) cudaFree(p);
         if (b->router_w) cudaFree(b->router_w);
         if (b->router_b) cudaFree(b->router_b);
+        b->stage.release();
     }
     delete b;
     return GW_OK;
@@ -556,6 +558,31 @@ static gw_status expert_ptr(gw_bank* b, int layer, int expert, uint8_t** out) {
     return GW_OK;
 }
 
+// Converts one expert between the reference's installed stride (`ref`) and
+// the bank's resident form (`bank`): the four MXFP4 sections in the tiled
+// layout (tile_layout_offset in gw_device.cuh), the biases unchanged.
+static gw_status relayout_expert(gw_bank* b, const uint8_t* src, uint8_t* dst, int to_tiled) {
+    gw_ctx* c = b->ctx;
+    const int H = b->d.hidden, F = b->d.intermediate;
+    const int64_t* off = b->d.section_offset;
+    const int rows[4] = {2 * F, 2 * F, H, H}, cols[4] = {H, H, F, F}, is_scale[4] = {0, 1, 0, 1};
+    for (int s = 0; s < 4; ++s) {
+        gw_status st = count(c, gw::launch_tile_layout(src + off[s], dst + off[s], rows[s], cols[s],
+                                                       is_scale[s], to_tiled, c->cur));
+        if (st) return st;
+    }
+    for (int s = 4; s < 6; ++s)
+        GW_CUDA(cudaMemcpyAsync(dst + off[s], src + off[s], b->d.section_length[s],
+                                cudaMemcpyDeviceToDevice, c->cur));
+    return GW_OK;
+}
+
+static gw_status bank_stage(gw_bank* b) {
+    cudaError_t e = b->stage.ensure((size_t)b->d.expert_stride);
+    if (e != cudaSuccess) return cuda_fail(e, "bank staging allocation");
+    return GW_OK;
+}
+
 gw_status gw_bank_upload_expert(gw_bank* b, int32_t layer, int32_t expert, const void* bytes,
                                 size_t len) {
     uint8_t* dst;
@@ -566,8 +593,10 @@ gw_status gw_bank_upload_expert(gw_bank* b, int32_t layer, int32_t expert, const
         return fail(GW_E_ARG, "stride is %zu bytes, the bank expects %lld", len,
                     (long long)b->d.expert_stride);
     CtxLock lk(b->ctx);
-    if ((st = set_device(b->ctx))) return st;
-    GW_CUDA(cudaMemcpyAsync(dst, bytes, len, cudaMemcpyHostToDevice, b->ctx->cur));
+    if ((st = set_device(b->ctx)) || (st = bank_stage(b))) return st;
+    uint8_t* stage = static_cast<uint8_t*>(b->stage.p);
+    GW_CUDA(cudaMemcpyAsync(stage, bytes, len, cudaMemcpyHostToDevice, b->ctx->cur));
+    if ((st = relayout_expert(b, stage, dst, 1))) return st;
     GW_CUDA(cudaStreamSynchronize(b->ctx->cur));
     return GW_OK;
 }
@@ -580,8 +609,10 @@ gw_status gw_bank_download_expert(gw_bank* b, int32_t layer, int32_t expert, voi
     if (!bytes || (int64_t)len != b->d.expert_stride)
         return fail(GW_E_ARG, "destination must hold exactly one stride");
     CtxLock lk(b->ctx);
-    if ((st = set_device(b->ctx))) return st;
-    GW_CUDA(cudaMemcpyAsync(bytes, src, len, cudaMemcpyDeviceToHost, b->ctx->cur));
+    if ((st = set_device(b->ctx)) || (st = bank_stage(b))) return st;
+    uint8_t* stage = static_cast<uint8_t*>(b->stage.p);
+    if ((st = relayout_expert(b, src, stage, 0))) return st;
+    GW_CUDA(cudaMemcpyAsync(bytes, stage, len, cudaMemcpyDeviceToHost, b->ctx->cur));
     GW_CUDA(cudaStreamSynchronize(b->ctx->cur));
     return GW_OK;
 }
@@ -609,20 +640,24 @@ gw_status gw_bank_fill_synthetic(gw_bank* b, uint64_t seed) {
     gw_ctx* c = b->ctx;
     gw_status st = set_device(c);
     if (st) return st;
+    if ((st = bank_stage(b))) return st;
+    uint8_t* stage = static_cast<uint8_t*>(b->stage.p);
     const int kinds[6] = {gw::kFillCodes, gw::kFillScales, gw::kFillCodes, gw::kFillScales,
                           gw::kFillBf16Normal, gw::kFillBf16Normal};
     for (int l = 0; l < b->d.layers; ++l) {
         for (int e = b->d.shard_rank; e < b->d.experts; e += b->d.shard_count) {
+            // generate the reference-layout stride, then lay it out in the bank
             uint8_t* ex = b->layer_mem[l] + (int64_t)(e / b->d.shard_count) * b->d.expert_stride;
             for (int s = 0; s < 6; ++s) {
                 const uint64_t key = gw::mix64(seed ^ gw::mix64(((uint64_t)l << 40) |
                                                                 ((uint64_t)e << 8) | (uint64_t)s));
                 int kind = kinds[s];
                 if (s >= 4 && b->d.activation == GW_ACT_SILU) kind = gw::kFillZero;
-                if ((st = count(c, gw::launch_fill_bytes(ex + b->d.section_offset[s],
+                if ((st = count(c, gw::launch_fill_bytes(stage + b->d.section_offset[s],
                                                          b->d.section_length[s], key, kind, c->cur))))
                     return st;
             }
+            if ((st = relayout_expert(b, stage, ex, 1))) return st;
         }
         const uint64_t kw = gw::mix64(seed ^ gw::mix64(((uint64_t)l << 40) | (0xFFFFull << 8) | 6u));
         const uint64_t kb = gw::mix64(seed ^ gw::mix64(((uint64_t)l << 40) | (0xFFFFull << 8) | 7u));

@@ -115,7 +115,12 @@ __device__ __forceinline__ float warp_max(float v) {
 // units of the staged x (the caller applies the token's x scale).
 constexpr int kXBlockHalves = 40;
 
-template <int kTok, int kSets>
+// Weight layouts the tile can stream:
+//   kTiled = false: the reference's row-major layout; rowA / rowB are matrix
+//     rows and packed / scales the matrix base.
+//   kTiled = true: the bank's tiled layout (see tile_layout_offset); rowA /
+//     rowB are rows 0..15 of the tile and packed / scales point at the tile.
+template <int kTok, int kSets, bool kTiled = false>
 __device__ __forceinline__ void mxfp4_tile_diag(const uint8_t* __restrict__ packed,
                                                 const uint8_t* __restrict__ scales, int cols,
                                                 int rowA, int rowB, const __half* xs,
@@ -130,19 +135,36 @@ __device__ __forceinline__ void mxfp4_tile_diag(const uint8_t* __restrict__ pack
     const int row_blocks = cols >> 5;
     const int zero_blk = row_blocks;  // the zero block
     const size_t rb = (size_t)(cols >> 1);
-    const uint4* pA = reinterpret_cast<const uint4*>(packed + (size_t)rowA * rb);
-    const uint4* pB = reinterpret_cast<const uint4*>(packed + (size_t)rowB * rb);
-    const uint8_t* sA = scales + (size_t)rowA * row_blocks;
-    const uint8_t* sB = scales + (size_t)rowB * row_blocks;
+    const uint4* pA = reinterpret_cast<const uint4*>(packed + (kTiled ? 0 : (size_t)rowA * rb));
+    const uint4* pB = reinterpret_cast<const uint4*>(packed + (kTiled ? 0 : (size_t)rowB * rb));
+    const uint8_t* sA = scales + (kTiled ? 0 : (size_t)rowA * row_blocks);
+    const uint8_t* sB = scales + (kTiled ? 0 : (size_t)rowB * row_blocks);
 #pragma unroll
     for (int j = 0; j < kTok * kSets; ++j) { accA[j] = 0.f; accB[j] = 0.f; }
 
+    // Per 8-block group: the group's first block of row A / row B, and its
+    // width in the layout (the tiled layout stores a group's rows w blocks
+    // apart; the row-major layout keeps the row's own stride).
+    auto group_ptrs = [&](int base, const uint4*& gA, const uint4*& gB, const uint8_t*& hA,
+                          const uint8_t*& hB) {
+        if (kTiled) {
+            const int w = min(8, row_blocks - base);
+            const size_t g0 = (size_t)(base >> 3) * 128;
+            gA = pA + g0 + rowA * w; gB = pB + g0 + rowB * w;
+            hA = sA + g0 + rowA * w; hB = sB + g0 + rowB * w;
+        } else {
+            gA = pA + base; gB = pB + base; hA = sA + base; hB = sB + base;
+        }
+    };
     uint4 wa[2], wb[2];
     auto load = [&](int base) {
+        const uint4 *gA, *gB;
+        const uint8_t *hA, *hB;
+        group_ptrs(base, gA, gB, hA, hB);
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
-            const int blk = base + 4 * r + t;
-            if (blk < nblk) { wa[r] = __ldg(pA + blk); wb[r] = __ldg(pB + blk); }
+            const int j = 4 * r + t;
+            if (base + j < nblk) { wa[r] = __ldg(gA + j); wb[r] = __ldg(gB + j); }
             else { wa[r] = make_uint4(0, 0, 0, 0); wb[r] = make_uint4(0, 0, 0, 0); }
         }
     };
@@ -160,6 +182,9 @@ __device__ __forceinline__ void mxfp4_tile_diag(const uint8_t* __restrict__ pack
     };
     load(blk0);
     for (int base = blk0; base < nblk; base += 8) {
+        const uint4 *gA_, *gB_;
+        const uint8_t *hA, *hB;
+        group_ptrs(base, gA_, gB_, hA, hB);
         uint4 ca[2], cb[2];
 #pragma unroll
         for (int r = 0; r < 2; ++r) { ca[r] = wa[r]; cb[r] = wb[r]; }
@@ -191,8 +216,8 @@ __device__ __forceinline__ void mxfp4_tile_diag(const uint8_t* __restrict__ pack
                 // flush this round: column 2t+q = (block base+4r+t, token 2s+q)
                 const int blk = base + 4 * r + t;
                 const bool ok = blk < nblk;
-                const float fa = ok ? gemv_scale(ldg_u8(sA + blk)) : 0.f;
-                const float fb = ok ? gemv_scale(ldg_u8(sB + blk)) : 0.f;
+                const float fa = ok ? gemv_scale(ldg_u8(hA + 4 * r + t)) : 0.f;
+                const float fb = ok ? gemv_scale(ldg_u8(hB + 4 * r + t)) : 0.f;
 #pragma unroll
                 for (int s = 0; s < kSets; ++s) {
 #pragma unroll
@@ -211,8 +236,8 @@ __device__ __forceinline__ void mxfp4_tile_diag(const uint8_t* __restrict__ pack
             for (int q = 0; q < 2; ++q) {
                 const int blk = base + 2 * t + q;
                 const bool ok = blk < nblk;
-                const float fa = ok ? gemv_scale(ldg_u8(sA + blk)) : 0.f;
-                const float fb = ok ? gemv_scale(ldg_u8(sB + blk)) : 0.f;
+                const float fa = ok ? gemv_scale(ldg_u8(hA + 2 * t + q)) : 0.f;
+                const float fb = ok ? gemv_scale(ldg_u8(hB + 2 * t + q)) : 0.f;
                 accA[0] = fmaf(d[0][q], fa, accA[0]);
                 accB[0] = fmaf(d[0][2 + q], fb, accB[0]);
             }
@@ -226,6 +251,20 @@ __device__ __forceinline__ void mxfp4_tile_diag(const uint8_t* __restrict__ pack
         accB[j] += __shfl_xor_sync(0xffffffffu, accB[j], 1);
         accB[j] += __shfl_xor_sync(0xffffffffu, accB[j], 2);
     }
+}
+
+// Tiled bank layout of an MXFP4 matrix [rows][cols] (rows % 16 == 0): the
+// 16-row tiles follow one another; inside a tile the 32-column blocks go in
+// groups of 8 (the last group narrower), and each group stores its 16 rows
+// x w blocks row-major.  A warp's pass over one group of its tile is thus one
+// contiguous 2 KB read, and a tile streams from HBM front to back (the
+// reference's row-major layout makes it 16 interleaved 128-byte-wide streams,
+// which DRAM serves measurably worse).  Scale bytes follow the same scheme
+// with 1-byte elements.  Returns the element offset of (row, blk).
+__host__ __device__ __forceinline__ int64_t tile_layout_offset(int row, int blk, int nblk) {
+    const int tile = row >> 4, lr = row & 15, grp = blk >> 3;
+    const int w = (nblk - (grp << 3)) < 8 ? (nblk - (grp << 3)) : 8;
+    return (int64_t)tile * 16 * nblk + (int64_t)grp * 128 + lr * w + (blk & 7);
 }
 
 // 2^p as an fp32 bit pattern, |p| <= 126.

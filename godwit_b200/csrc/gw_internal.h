@@ -74,6 +74,10 @@ int launch_residual_round(float* stream, const float* delta, void* x_out, int x_
                           int64_t n, cudaStream_t s);
 int launch_xprep(const void* x, int x_dtype, int T, int H, __half* x16, float* xmul,
                  cudaStream_t s);
+// Reference row-major <-> tiled bank layout of one MXFP4 matrix's packed
+// blocks (scales = 0) or scale bytes (scales = 1).
+int launch_tile_layout(const uint8_t* src, uint8_t* dst, int rows, int cols, int scales,
+                       int to_tiled, cudaStream_t s);
 int launch_widen(const void* x, int x_dtype, float* stream, int64_t n, cudaStream_t s);
 size_t gemv_smem_bytes(int cols, int max_tok);
 int configure_kernels();

@@ -273,7 +273,8 @@ __device__ __forceinline__ void split_range(int nblk, int ksplit, int sp, int& b
     b1 = min(nblk, (sp + 1) * per * 8);
 }
 
-// Runs one token chunk (n = 1..kChunk) of a tile split over `ksplit` warps
+// Runs one token chunk (n = 1..kChunk) of a bank tile (tiled layout: packed /
+// scales point at the tile, rowA / rowB are tile rows) split over `ksplit` warps
 // and calls emit(token, rowA total, rowB total) once per (row pair, token)
 // on the split-0 warp.  Every thread of the CTA must call this (it
 // synchronises when ksplit > 1).
@@ -294,16 +295,16 @@ __device__ __forceinline__ void run_tile(int n, bool valid, const uint8_t* packe
         const int st = diag_stride(cols);
         if (n == 1) {
             float a1[1], bb1[1];
-            mxfp4_tile_diag<1, 1>(packed, scales, cols, rowA, rowB, xs, st, 1, b0, b1, a1, bb1);
+            mxfp4_tile_diag<1, 1, true>(packed, scales, cols, rowA, rowB, xs, st, 1, b0, b1, a1, bb1);
             a[0] = a1[0];
             b[0] = bb1[0];
         } else if (n == 2) {
             float a2[2], bb2[2];
-            mxfp4_tile_diag<2, 1>(packed, scales, cols, rowA, rowB, xs, st, 2, b0, b1, a2, bb2);
+            mxfp4_tile_diag<2, 1, true>(packed, scales, cols, rowA, rowB, xs, st, 2, b0, b1, a2, bb2);
             a[0] = a2[0]; a[1] = a2[1];
             b[0] = bb2[0]; b[1] = bb2[1];
         } else {
-            mxfp4_tile_diag<2, 2>(packed, scales, cols, rowA, rowB, xs, st, n, b0, b1, a, b);
+            mxfp4_tile_diag<2, 2, true>(packed, scales, cols, rowA, rowB, xs, st, n, b0, b1, a, b);
         }
     }
     if (ksplit > 1) {
@@ -389,7 +390,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 5) k_gateup(LayerView L, MoeD
         __syncthreads();
         stage_x16(xs, diag_stride(H), w.x16, rows, n, H);
         __syncthreads();
-        run_tile(n, valid, packed, scales, H, rowA, rowB, xs, ksplit,
+        run_tile(n, valid, packed + (size_t)tile * 16 * (H >> 1), scales + (size_t)tile * 16 * (H >> 5),
+                 H, 2 * g, 2 * g + 1, xs, ksplit,
                  [&](int col, float ga, float ub) {
                      const float v = activate<kAct>(ga * xm[col] + bA, ub * xm[col] + bB, d.limit, d.alpha);
                      w.act[(int64_t)slots[col] * F + f] = __float2half_rn(v);
@@ -435,7 +437,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 5) k_down(LayerView L, MoeDim
         __syncthreads();
         stage_x16(xs, diag_stride(F), w.act, slots, n, F);
         __syncthreads();
-        run_tile(n, valid, packed, scales, F, rowA, rowB, xs, ksplit,
+        run_tile(n, valid, packed + (size_t)tile * 16 * (F >> 1), scales + (size_t)tile * 16 * (F >> 5),
+                 F, g, g + 8, xs, ksplit,
                  [&](int col, float ya, float yb) {
                      float* y = w.ybuf + (int64_t)slots[col] * H;
                      y[rowA] = (ya + bA) * wt[col];
@@ -555,6 +558,24 @@ __global__ void k_fill(uint8_t* __restrict__ dst, int64_t n, uint64_t key, int k
             dst[i] = (uint8_t)(118 + mix64(key + (uint64_t)i) % 7);
         else
             dst[i] = 0;
+    }
+}
+
+// k_tile_layout: reference row-major MXFP4 matrix <-> the bank's tiled layout
+// (tile_layout_offset).  `unit` bytes per element (16 for packed blocks, 1 for
+// scales); rows % 16 == 0.  to_tiled = 0 converts back.
+__global__ void k_tile_layout(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int rows,
+                              int nblk, int unit, int to_tiled) {
+    const int64_t n = (int64_t)rows * nblk;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const int row = (int)(i / nblk), blk = (int)(i - (int64_t)row * nblk);
+        const int64_t t = tile_layout_offset(row, blk, nblk);
+        const int64_t a = to_tiled ? i : t, b = to_tiled ? t : i;
+        if (unit == 16)
+            reinterpret_cast<uint4*>(dst)[b] = reinterpret_cast<const uint4*>(src)[a];
+        else
+            dst[b] = src[a];
     }
 }
 
@@ -695,6 +716,15 @@ int launch_residual_round(float* stream, const float* delta, void* x_out, int x_
     int64_t blocks = (n + 255) / 256;
     if (blocks > 148 * 16) blocks = 148 * 16;
     k_residual<<<(unsigned)blocks, 256, 0, s>>>(stream, delta, x_out, x_dtype, n);
+    return ok_or_fail();
+}
+
+int launch_tile_layout(const uint8_t* src, uint8_t* dst, int rows, int cols, int scales,
+                       int to_tiled, cudaStream_t s) {
+    const int nblk = cols / 32;
+    int64_t blocks = ((int64_t)rows * nblk + 255) / 256;
+    if (blocks > 148 * 32) blocks = 148 * 32;
+    k_tile_layout<<<(unsigned)blocks, 256, 0, s>>>(src, dst, rows, nblk, scales ? 1 : 16, to_tiled);
     return ok_or_fail();
 }
 

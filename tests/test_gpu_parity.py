@@ -335,3 +335,10 @@ def test_stack_forward_chains_layers(ctx, oss_bank):
         s = s + o
     assert O.rel_l2(got, s) < 1e-5
     ctx.set_stream(None)
+
+
+def test_bank_round_trips_the_reference_stride(ctx, oss_bank):
+    # upload re-lays the stride out for the kernels; download restores it
+    bank, strides, _ = oss_bank
+    for e in (0, 7):
+        assert np.array_equal(bank.download_expert(1, e), strides[1][e])
