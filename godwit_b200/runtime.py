@@ -123,10 +123,12 @@ class ExpertBank:
     """The HBM-resident expert bank of one model (or one expert shard)."""
 
     def __init__(self, ctx: Context, spec: ModelSpec, *, layers: int | None = None,
-                 shard_rank: int = 0, shard_count: int = 1):
+                 shard_rank: int = 0, shard_count: int = 1, desc: BankDesc | None = None):
+        """`desc` overrides the stride and section spans (e.g. from an
+        installation's manifest); by default they follow ExpertLayout."""
         self.ctx = ctx
         self.spec = spec
-        self.desc: BankDesc = spec.desc(shard_rank, shard_count, layers)
+        self.desc: BankDesc = desc if desc is not None else spec.desc(shard_rank, shard_count, layers)
         self.layers = self.desc.layers
         self.shard_rank, self.shard_count = shard_rank, shard_count
         h = C.c_void_p()
