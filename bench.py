@@ -44,6 +44,7 @@ WORKLOADS = {
     "oss20-decode1": ("gpt-oss-20b", 1, "GPT-OSS-20B-shaped MoE decode, 24 layers, batch 1"),
     "qwen3-decode1": ("qwen3-30b-a3b", 1, "Qwen3-30B-A3B-shaped MoE decode, 48 layers, batch 1"),
     "qwen3-decode32": ("qwen3-30b-a3b", 32, "Qwen3-30B-A3B-shaped MoE decode, 48 layers, batch 32"),
+    "oss120-prefill": ("gpt-oss-120b", 2048, "GPT-OSS-120B-shaped MoE prefill layer, 2048 tokens, 4x hot-expert skew on 8 experts"),
     "gemv": (None, 1, "MXFP4 GEMV 2880x2880 (GPT-OSS down_proj shape), batched over copies"),
 }
 DEFAULT_WORKLOAD = "oss120-decode64"
@@ -290,6 +291,40 @@ def _barrier(world):
         dist.barrier()
 
 
+HOT_EXPERTS = (3, 17, 31, 45, 59, 73, 87, 101)
+
+
+def skewed_router_bias(spec, x_f32, seed=SEED, target=4.0):
+    """Config 4's deliberate skew: the router of layer 0 gets a bias offset
+    delta on 8 fixed experts, found by bisection on these tokens so that the
+    hot experts receive on average `target` x the mean tokens per expert.
+    Returns (bias bf16 [E], delta, histogram)."""
+    import numpy as np
+    from godwit_b200 import synth
+    w, b = synth.hash_router(spec, seed, 0)
+    logits0 = x_f32 @ synth.bf16_bits_to_f32(w).reshape(spec.experts, spec.hidden).T
+    base = synth.bf16_bits_to_f32(b)
+    mean = x_f32.shape[0] * spec.top_k / spec.experts
+
+    def hist(delta):
+        bb = base.copy()
+        bb[list(HOT_EXPERTS)] += delta
+        bb = synth.bf16_bits_to_f32(synth.f32_to_bf16_bits(bb))
+        top = np.argsort(-(logits0 + bb), axis=1)[:, :spec.top_k]
+        return np.bincount(top.ravel(), minlength=spec.experts), bb
+
+    lo, hi = 0.0, 1.0
+    for _ in range(40):
+        mid = 0.5 * (lo + hi)
+        h, _ = hist(mid)
+        if h[list(HOT_EXPERTS)].mean() < target * mean:
+            lo = mid
+        else:
+            hi = mid
+    h, bb = hist(hi)
+    return synth.f32_to_bf16_bits(bb), hi, h
+
+
 def run_decode(args):
     import torch
 
@@ -303,6 +338,8 @@ def run_decode(args):
     world, rank, local = _dist_setup(args)
     preset, T, desc = WORKLOADS[args.workload]
     spec = PRESETS[preset]
+    if args.workload == "oss120-prefill":
+        spec = spec.with_(layers=1)
     if args.layers:
         spec = spec.with_(layers=args.layers)
     ctx = Context(local)
@@ -314,6 +351,14 @@ def run_decode(args):
     H = spec.hidden
     rng = np.random.default_rng(SEED)
     xb = synth.make_hidden(rng, T, H, "bf16")
+    skew = None
+    if args.workload == "oss120-prefill":
+        rb, delta, h = skewed_router_bias(spec, synth.as_f32(xb, "bf16"))
+        rw, _ = synth.hash_router(spec, SEED, 0)
+        bank.upload_router(0, rw, rb)
+        skew = {"hot_experts": list(HOT_EXPERTS), "delta": round(float(delta), 5),
+                "hot_mean_tokens": float(h[list(HOT_EXPERTS)].mean()),
+                "other_mean_tokens": float(np.delete(h, list(HOT_EXPERTS)).mean())}
     x_host = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).pin_memory()
     out_host = torch.empty(T, H, dtype=torch.float32).pin_memory()
     x = x_host.to("cuda")
@@ -396,7 +441,8 @@ def run_decode(args):
                        "hidden": spec.hidden, "intermediate": spec.intermediate, "tokens": T,
                        "parallelism": f"ep{world}" if world > 1 else "single",
                        "l2": "weights streamed per step >> 126 MB L2 (no flush needed)",
-                       "bank_fill_s": round(fill_s, 2), "bank_bytes": bank.nbytes()},
+                       "bank_fill_s": round(fill_s, 2), "bank_bytes": bank.nbytes(),
+                       **({"skew": skew} if skew else {})},
             "e2e": {"value": T / (e2e_ms / 1e3), "unit": unit, "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 4},
             "gpu_launches": launches,
