@@ -75,6 +75,8 @@ struct gw_ctx {
     DevBuf gemv_x;      // f16 x + block scales of GEMV calls
     int work_tcap = 0, work_H = 0, work_F = 0, work_E = 0, work_k = 0;
     gw::MoeWork w{};
+    int sms = 148;          // persistent grid of the tensor-core expert kernels
+    int mma_min_avg = 8;    // tensor-core expert path when T*k >= mma_min_avg * E
     int64_t launches = 0;
     // profiling (gw_profile_enable): event pairs per timed launch
     bool prof = false;
@@ -101,6 +103,7 @@ struct gw_bank {
     gw_bank_desc d{};
     int e_local = 0;
     std::vector<uint8_t*> layer_mem;  // [L] each E_local * stride bytes
+    std::vector<uint8_t*> rowexp;     // [L] each E_local * (2F + H): largest scale exponent per row
     uint16_t* router_w = nullptr;     // [L][E][H]
     uint16_t* router_b = nullptr;     // [L][E]
     int64_t bytes = 0;
@@ -140,6 +143,8 @@ gw::LayerView layer_of(const gw_bank* b, int layer) {
     for (int i = 0; i < 6; ++i) v.off[i] = b->d.section_offset[i];
     v.router_w = b->router_w + (int64_t)layer * b->d.experts * b->d.hidden;
     v.router_b = b->d.has_router_bias ? b->router_b + (int64_t)layer * b->d.experts : nullptr;
+    v.rowexp = b->rowexp[layer];
+    v.rowexp_stride = 2 * (int64_t)b->d.intermediate + b->d.hidden;
     return v;
 }
 
@@ -167,10 +172,12 @@ gw_status ensure_work(gw_ctx* c, const gw_bank* b, int T) {
     const size_t o_act = take((size_t)tcap * kc * Fc * 2);
     const size_t o_ybuf = take((size_t)tcap * kc * Hc * 4);
     const size_t o_done = take((size_t)(tcap / 8 + 1) * 4);
+    const size_t o_status = take(4);
     cudaError_t e = c->work.ensure(off);
     if (e != cudaSuccess) return cuda_fail(e, "workspace allocation");
     char* base = static_cast<char*>(c->work.p);
     GW_CUDA(cudaMemsetAsync(base + o_done, 0, (size_t)(tcap / 8 + 1) * 4, c->cur));
+    GW_CUDA(cudaMemsetAsync(base + o_status, 0, 4, c->cur));
     GW_CUDA(cudaMemsetAsync(base + o_nactive, 0, 4, c->cur));
     GW_CUDA(cudaMemsetAsync(base + o_counts, 0, (size_t)Ec * 4, c->cur));
     gw::MoeWork& w = c->w;
@@ -188,6 +195,8 @@ gw_status ensure_work(gw_ctx* c, const gw_bank* b, int T) {
     w.act = reinterpret_cast<__half*>(base + o_act);
     w.ybuf = reinterpret_cast<float*>(base + o_ybuf);
     w.done = reinterpret_cast<unsigned*>(base + o_done);
+    w.status = reinterpret_cast<unsigned*>(base + o_status);
+    w.mma_min_avg = c->mma_min_avg;
     c->work_tcap = tcap;
     c->work_H = Hc;
     c->work_F = Fc;
@@ -274,9 +283,18 @@ gw_status moe_layer_device(gw_ctx* c, gw_bank* b, int layer, const void* x_dev, 
     else
         st = timed_launch(c, 3, 0, [&] { return gw::launch_router(L, d, x_dev, x_dtype, T, w, c->cur); });
     if (st) return st;
-    if ((st = timed_launch(c, 0, 0, [&] { return gw::launch_gateup(L, d, x_dev, x_dtype, T, w, c->cur); })))
+    // Many tokens per expert: the tensor-core grouped GEMMs; few: the GEMV tiles.
+    const bool mma = w.mma_min_avg > 0 && (int64_t)T * d.k >= (int64_t)w.mma_min_avg * d.E &&
+                     gw::grouped_supported(d, w);
+    if ((st = timed_launch(c, 0, 0, [&] {
+             return mma ? gw::launch_grouped(L, d, w, 0, c->sms, c->cur)
+                        : gw::launch_gateup(L, d, x_dev, x_dtype, T, w, c->cur);
+         })))
         return st;
-    if ((st = timed_launch(c, 1, 0, [&] { return gw::launch_down(L, d, T, w, c->cur); }))) return st;
+    if ((st = timed_launch(c, 1, 0, [&] {
+             return mma ? gw::launch_grouped(L, d, w, 1, c->sms, c->cur) : gw::launch_down(L, d, T, w, c->cur);
+         })))
+        return st;
     if (c->prof && (st = log_nactive(c))) return st;
     return timed_launch(c, 4, 0, [&] {
         return gw::launch_combine(d, T, w, out, accumulate, x_next, x_dtype, c->cur);
@@ -333,9 +351,11 @@ gw_status gw_init(int32_t device, gw_ctx** out) {
     if (prop.major != 10)
         return fail(GW_E_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a",
                     device, prop.major, prop.minor);
-    if (gw::configure_kernels() != 0) return cuda_fail(cudaGetLastError(), "kernel attributes");
+    if (gw::configure_kernels() != 0 || gw::configure_grouped() != 0)
+        return cuda_fail(cudaGetLastError(), "kernel attributes");
     gw_ctx* c = new gw_ctx();
     c->device = device;
+    c->sms = prop.multiProcessorCount;
     e = cudaStreamCreateWithFlags(&c->own, cudaStreamNonBlocking);
     if (e != cudaSuccess) {
         delete c;
@@ -377,6 +397,27 @@ gw_status gw_sync(gw_ctx* c) {
     CtxLock lk(c);
     GW_CUDA(cudaSetDevice(c->device));
     GW_CUDA(cudaStreamSynchronize(c->cur));
+    if (c->w.status) {  // a bounded wait in a tensor-core expert kernel ran out
+        unsigned bits = 0;
+        GW_CUDA(cudaMemcpy(&bits, c->w.status, 4, cudaMemcpyDeviceToHost));
+        if (bits) {
+            GW_CUDA(cudaMemset(c->w.status, 0, 4));
+            return fail(GW_E_CUDA, "tensor-core expert kernel gave up waiting (status bits 0x%x)", bits);
+        }
+    }
+    return GW_OK;
+}
+
+gw_status gw_set_tensor_core_min_tokens(gw_ctx* c, int32_t min_avg) {
+    if (!c) return fail(GW_E_ARG, "null context");
+    if (min_avg < 0) return fail(GW_E_ARG, "min_avg must be >= 0");
+    CtxLock lk(c);
+    c->mma_min_avg = min_avg;
+    c->w.mma_min_avg = min_avg;
+    if (c->graph.exec) {  // a captured stack forward baked the old choice in
+        cudaGraphExecDestroy(c->graph.exec);
+        c->graph = gw_ctx::StackGraph{};
+    }
     return GW_OK;
 }
 
@@ -497,14 +538,20 @@ gw_status gw_bank_create(gw_ctx* c, const gw_bank_desc* d, gw_bank** out) {
     b->d = *d;
     b->e_local = (d->experts - d->shard_rank + d->shard_count - 1) / d->shard_count;
     const size_t per_layer = (size_t)b->e_local * d->expert_stride;
+    const size_t rexp_layer = (size_t)b->e_local * (2 * F + H);
     b->layer_mem.assign(d->layers, nullptr);
+    b->rowexp.assign(d->layers, nullptr);
     for (int l = 0; l < d->layers; ++l) {
-        cudaError_t e = cudaMalloc(&b->layer_mem[l], std::max<size_t>(per_layer, 256));
+        // 256 bytes of tail: the tensor-core path reads scale bytes in
+        // aligned 16-byte windows that may reach past the last row
+        cudaError_t e = cudaMalloc(&b->layer_mem[l], per_layer + 256);
+        if (e == cudaSuccess) e = cudaMalloc(&b->rowexp[l], std::max<size_t>(rexp_layer, 256));
+        if (e == cudaSuccess) e = cudaMemsetAsync(b->rowexp[l], 127, std::max<size_t>(rexp_layer, 256), c->cur);
         if (e != cudaSuccess) {
             gw_bank_destroy(b);
             return cuda_fail(e, "bank layer allocation");
         }
-        b->bytes += per_layer;
+        b->bytes += per_layer + rexp_layer;
     }
     const size_t rw = (size_t)d->layers * d->experts * d->hidden * 2;
     const size_t rb = (size_t)d->layers * d->experts * 2;
@@ -538,6 +585,8 @@ gw_status gw_bank_destroy(gw_bank* b) {
         cudaStreamSynchronize(b->ctx->cur);
         for (uint8_t* p : b->layer_mem)
             if (p) cudaFree(p);
+        for (uint8_t* p : b->rowexp)
+            if (p) cudaFree(p);
         if (b->router_w) cudaFree(b->router_w);
         if (b->router_b) cudaFree(b->router_b);
         b->stage.release();
@@ -558,13 +607,24 @@ static gw_status expert_ptr(gw_bank* b, int layer, int expert, uint8_t** out) {
     return GW_OK;
 }
 
+static uint8_t* rowexp_ptr(gw_bank* b, int layer, int expert) {
+    return b->rowexp[layer] +
+           (int64_t)(expert / b->d.shard_count) * (2 * (int64_t)b->d.intermediate + b->d.hidden);
+}
+
 // Converts one expert between the reference's installed stride (`ref`) and
 // the bank's resident form (`bank`): the four MXFP4 sections in the tiled
 // layout (tile_layout_offset in gw_device.cuh), the biases unchanged.
-static gw_status relayout_expert(gw_bank* b, const uint8_t* src, uint8_t* dst, int to_tiled) {
+static gw_status relayout_expert(gw_bank* b, const uint8_t* src, uint8_t* dst, int to_tiled,
+                                 uint8_t* rowexp = nullptr) {
     gw_ctx* c = b->ctx;
     const int H = b->d.hidden, F = b->d.intermediate;
     const int64_t* off = b->d.section_offset;
+    if (rowexp) {  // per-row exponent maxima from the reference-layout scales
+        gw_status st = count(c, gw::launch_rowexp(src + off[1], 2 * F, H, rowexp, c->cur));
+        if (!st) st = count(c, gw::launch_rowexp(src + off[3], H, F, rowexp + 2 * F, c->cur));
+        if (st) return st;
+    }
     const int rows[4] = {2 * F, 2 * F, H, H}, cols[4] = {H, H, F, F}, is_scale[4] = {0, 1, 0, 1};
     for (int s = 0; s < 4; ++s) {
         gw_status st = count(c, gw::launch_tile_layout(src + off[s], dst + off[s], rows[s], cols[s],
@@ -596,7 +656,7 @@ gw_status gw_bank_upload_expert(gw_bank* b, int32_t layer, int32_t expert, const
     if ((st = set_device(b->ctx)) || (st = bank_stage(b))) return st;
     uint8_t* stage = static_cast<uint8_t*>(b->stage.p);
     GW_CUDA(cudaMemcpyAsync(stage, bytes, len, cudaMemcpyHostToDevice, b->ctx->cur));
-    if ((st = relayout_expert(b, stage, dst, 1))) return st;
+    if ((st = relayout_expert(b, stage, dst, 1, rowexp_ptr(b, layer, expert)))) return st;
     GW_CUDA(cudaStreamSynchronize(b->ctx->cur));
     return GW_OK;
 }
@@ -657,7 +717,7 @@ gw_status gw_bank_fill_synthetic(gw_bank* b, uint64_t seed) {
                                                          b->d.section_length[s], key, kind, c->cur))))
                     return st;
             }
-            if ((st = relayout_expert(b, stage, ex, 1))) return st;
+            if ((st = relayout_expert(b, stage, ex, 1, rowexp_ptr(b, l, e)))) return st;
         }
         const uint64_t kw = gw::mix64(seed ^ gw::mix64(((uint64_t)l << 40) | (0xFFFFull << 8) | 6u));
         const uint64_t kb = gw::mix64(seed ^ gw::mix64(((uint64_t)l << 40) | (0xFFFFull << 8) | 7u));

@@ -267,6 +267,20 @@ __host__ __device__ __forceinline__ int64_t tile_layout_offset(int row, int blk,
     return (int64_t)tile * 16 * nblk + (int64_t)grp * 128 + lr * w + (blk & 7);
 }
 
+// Expert activation on one (gate, up) pair, kAct 0 = clamped GLU, 1 = SiLU.
+template <int kAct>
+__device__ __forceinline__ float activate(float gate, float up, float limit, float alpha) {
+    if (kAct == 0) {  // gptoss_expert_activation, expert.metal:92-101
+        gate = fminf(gate, limit);
+        up = fminf(fmaxf(up, -limit), limit);
+        const float glu = gate * (1.0f / (1.0f + expf(-alpha * gate)));
+        return (up + 1.0f) * glu;
+    } else {  // expert_activation_swiglu, expert.metal:388-392
+        const float silu = gate * (1.0f / (1.0f + expf(-gate)));
+        return silu * up;
+    }
+}
+
 // 2^p as an fp32 bit pattern, |p| <= 126.
 __device__ __forceinline__ float pow2f(int p) { return __uint_as_float((uint32_t)(127 + p) << 23); }
 

@@ -25,6 +25,8 @@ struct LayerView {
     int64_t off[6];            // section offsets within a stride
     const uint16_t* router_w;  // bf16 [E][H]
     const uint16_t* router_b;  // bf16 [E] or nullptr
+    const uint8_t* rowexp;     // [E_local][2F + H] largest E8M0 exponent per weight row
+    int64_t rowexp_stride;     // bytes per local expert in rowexp (2F + H)
 };
 
 struct MoeDims {
@@ -49,6 +51,8 @@ struct MoeWork {
     __half* act;       // [tcap*k][F]  activated gate_up output (f16, as the reference)
     float* ybuf;       // [tcap*k][H]  routing-weighted down output per slot
     unsigned* done;    // [tcap/8+1]   router completion counter per token chunk (self-resetting)
+    unsigned* status;  // [1]          sticky error bits set by bounded waits (nullptr: none)
+    int mma_min_avg;   // tensor-core expert path when T*k >= mma_min_avg * E (0: never)
 };
 
 // Host-side launchers; each returns the number of kernels it launched (or -1
@@ -80,6 +84,14 @@ int launch_tile_layout(const uint8_t* src, uint8_t* dst, int rows, int cols, int
                        int to_tiled, cudaStream_t s);
 int launch_widen(const void* x, int x_dtype, float* stream, int64_t n, cudaStream_t s);
 size_t gemv_smem_bytes(int cols, int max_tok);
+// Tensor-core grouped expert GEMM (gw_grouped.cu): which 0 = gate_up + activation,
+// 1 = down + routing weight.  `sms` persistent CTAs.
+int launch_grouped(const LayerView& L, const MoeDims& d, const MoeWork& w, int which, int sms,
+                   cudaStream_t s);
+bool grouped_supported(const MoeDims& d, const MoeWork& w);
+int configure_grouped();
+// Row-exponent table entries of a row-major scale matrix.
+int launch_rowexp(const uint8_t* scales, int rows, int cols, uint8_t* out, cudaStream_t s);
 int configure_kernels();
 
 // Counter hash used by the synthetic bank generator (splitmix64 finaliser).

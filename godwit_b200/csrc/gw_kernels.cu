@@ -335,20 +335,6 @@ __device__ __forceinline__ void run_tile(int n, bool valid, const uint8_t* packe
 }
 
 template <int kAct>
-__device__ __forceinline__ float activate(float gate, float up, float limit, float alpha) {
-    if (kAct == 0) {  // gptoss_expert_activation, expert.metal:92-101
-        gate = fminf(gate, limit);
-        up = fminf(fmaxf(up, -limit), limit);
-        const float glu = gate * (1.0f / (1.0f + expf(-alpha * gate)));
-        return (up + 1.0f) * glu;
-    } else {  // expert_activation_swiglu, expert.metal:388-392
-        const float silu = gate * (1.0f / (1.0f + expf(-gate)));
-        return silu * up;
-    }
-}
-
-
-template <int kAct>
 __global__ void __launch_bounds__(kGemvWarps * 32, 5) k_gateup(LayerView L, MoeDims d, const void* x,
                                                               int x_dtype, int T, MoeWork w,
                                                               int ksplit) {

@@ -71,6 +71,12 @@ class Context:
     def sync(self) -> None:
         call("gw_sync", self.handle)
 
+    def set_tensor_core_min_tokens(self, min_avg: int) -> None:
+        """Experts of a layer run as tensor-core grouped GEMMs when
+        T * top_k >= min_avg * experts, else as MXFP4 GEMV tiles (0: always
+        GEMV).  Default 8."""
+        call("gw_set_tensor_core_min_tokens", self.handle, int(min_avg))
+
     def launch_count(self) -> int:
         v = C.c_int64()
         call("gw_last_launch_count", self.handle, C.byref(v))

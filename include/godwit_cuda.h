@@ -116,8 +116,15 @@ GW_API gw_status gw_shutdown(gw_ctx* ctx);
 /* Orders subsequent `_async` work on `cuda_stream` (a cudaStream_t; NULL =
  * the context's own stream). */
 GW_API gw_status gw_ctx_set_stream(gw_ctx* ctx, void* cuda_stream);
-/* Waits for all work queued on the context's stream. */
+/* Waits for all work queued on the context's stream.  Also reports (and
+ * clears) a bounded wait that ran out inside a tensor-core expert kernel. */
 GW_API gw_status gw_sync(gw_ctx* ctx);
+/* Expert-path policy (no reference counterpart: the reference runs every
+ * (expert, token) assignment as GEMVs, ExpertRunner.applyAssignments,
+ * Runtime/ExpertRunner.swift:108-183).  A layer with T tokens runs its experts as tensor-core grouped GEMMs when
+ * T * top_k >= min_avg * experts, else as the MXFP4 GEMV tiles; 0 = always
+ * the GEMV tiles.  Default 8. */
+GW_API gw_status gw_set_tensor_core_min_tokens(gw_ctx* ctx, int32_t min_avg);
 
 /* ---- layout (ExpertLayout.init, Install/InstallLayout.swift:50-92) ------ */
 
