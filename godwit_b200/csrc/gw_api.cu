@@ -171,6 +171,7 @@ gw_status ensure_work(gw_ctx* c, const gw_bank* b, int T) {
     const size_t o_lists = take((size_t)Ec * tcap * 4);
     const size_t o_act = take((size_t)tcap * kc * Fc * 2);
     const size_t o_ybuf = take((size_t)tcap * kc * Hc * 4);
+    const size_t o_xg = take((size_t)tcap * kc * Hc * 2);
     const size_t o_done = take((size_t)(tcap / 8 + 1) * 4);
     const size_t o_status = take(4);
     cudaError_t e = c->work.ensure(off);
@@ -194,6 +195,7 @@ gw_status ensure_work(gw_ctx* c, const gw_bank* b, int T) {
     w.lists = reinterpret_cast<int32_t*>(base + o_lists);
     w.act = reinterpret_cast<__half*>(base + o_act);
     w.ybuf = reinterpret_cast<float*>(base + o_ybuf);
+    w.xg = reinterpret_cast<__half*>(base + o_xg);
     w.done = reinterpret_cast<unsigned*>(base + o_done);
     w.status = reinterpret_cast<unsigned*>(base + o_status);
     w.mma_min_avg = c->mma_min_avg;

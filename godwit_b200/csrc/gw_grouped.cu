@@ -11,22 +11,28 @@
 // f16, down projection times the routing weight — for all of an expert's
 // tokens from one pass over its weights.
 //
-// One persistent CTA per SM walks a static list of work items (expert, token
-// chunk of <= 128, 128-row tile).  Warp roles:
-//   warps 0-7   converters: cp.async the tile's MXFP4 blocks and scale bytes
-//               into a raw ring 7 stages ahead, then widen each 128 x 64
-//               stage to f16 (cvt.rn.f16x2.e2m1x2, times the block scale) in
-//               the canonical K-major layout tcgen05 reads.
-//   warps 8-11  token loaders: cp.async the chunk's f16 activation rows into
-//               the same stage.
-//   warp 16     MMA issuer: one thread, tcgen05.mma kind::f16 M=128 N=n K=16,
+// One persistent CTA per SM walks a static list of work items (128-row tile,
+// expert, token chunk of <= 128).  Warp roles:
+//   warp 12     weight producer: one thread bulk-copies (cp.async.bulk) each
+//               8-block group of the tile — in the bank's tiled layout a
+//               contiguous 16 x 8 x 16-byte run per 16-row tile, plus its
+//               scale bytes — into a 3-group ring (mbarrier transaction
+//               counts signal arrival).
+//   warps 0-7   converters: widen each 128 x 64 stage of the ring to f16
+//               (cvt.rn.f16x2.e2m1x2, times the block scale) in the canonical
+//               K-major no-swizzle layout tcgen05 reads.
+//   warp 13     token producer: one thread, one 2D TMA (128 rows x 64
+//               columns, 128B swizzle) per stage from the expert-ordered f16
+//               token rows (x16 gathered by k_gather for gate_up; the gate_up
+//               epilogue writes its activations in that order for down).
+//   warp 14     MMA issuer: one thread, tcgen05.mma kind::f16 M=128 N=n K=16,
 //               fp32 accumulators in TMEM (two 128-column buffers so the
 //               epilogue of one item overlaps the main loop of the next).
-//   warps 12-15 epilogue: tcgen05.ld the accumulators (one row per thread),
+//   warps 8-11  epilogue: tcgen05.ld the accumulators (one row per thread),
 //               scale, bias, activation / routing weight, store.
-// Every wait is bounded (2 s); a wait that runs out sets a bit in the
-// workspace status word and makes the whole CTA wind down: it drains its
-// copies, waits for its MMAs and frees its TMEM before returning.
+// Every wait is bounded (~2 s); a wait that runs out sets a bit in the
+// workspace status word and makes the whole CTA wind down: it lets its copies
+// land, waits for its MMAs and frees its TMEM before returning.
 //
 // f16 operands are exact: x16 rows are the router's power-of-two-shifted
 // activations, and each weight row is multiplied by 2^(128 - emax_row) with
@@ -35,8 +41,12 @@
 // within 25 binades of them is exact in f16 (normal or subnormal); blocks
 // further down, whose products are below 2^-25 of the row's largest, flush to
 // zero.  The epilogue undoes both shifts in fp32.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
+
+#include <mutex>
 
 #include "gw_device.cuh"
 #include "gw_internal.h"
@@ -44,36 +54,45 @@
 namespace gw {
 namespace {
 
-constexpr int kM = 128;                  // weight rows per tile (MMA M)
-constexpr int kNMax = 128;               // token columns per chunk (MMA N max)
-constexpr int kKS = 64;                  // columns per stage (two MXFP4 blocks)
-constexpr int kStages = 5;               // operand ring the MMA reads
-constexpr int kRaw = 8;                  // raw weight ring depth (stages in flight)
-constexpr int kScaleSlots = 6;           // per-group scale ring
-constexpr int kASlot = kM * kKS * 2;     // 16 KB of f16 weights per stage
-constexpr int kBSlot = kNMax * kKS * 2;  // 16 KB of f16 tokens per stage
-constexpr int kRawSlot = kM * kKS / 2;   // 4 KB of MXFP4 blocks per stage
-constexpr int kScaleSlot = 2 * kM * 16;  // 16 bytes per converter thread per 8-block group
+constexpr int kM = 128;                   // weight rows per tile (MMA M)
+constexpr int kNMax = 128;                // token columns per chunk (MMA N max)
+constexpr int kKS = 64;                   // columns per stage (two MXFP4 blocks)
+constexpr int kStages = 5;                // operand ring the MMA reads
+constexpr int kGroups = 3;                // raw weight ring, in 8-block groups
+constexpr int kASlot = kM * kKS * 2;      // 16 KB of f16 weights per stage
+constexpr int kBSlot = kNMax * kKS * 2;   // 16 KB of f16 tokens per stage
+constexpr int kTileRun = 16 * 8 * 16;     // one 16-row tile's blocks of a full group
+constexpr int kGroupPk = 8 * kTileRun;    // 16 KB of MXFP4 blocks per group
+constexpr int kGroupSc = 8 * 16 * 8;      // 1 KB of scale bytes per group
 constexpr int kRingBytes = kStages * (kASlot + kBSlot);
-constexpr int kRawOff = kRingBytes;
-constexpr int kScaleOff = kRawOff + kRaw * kRawSlot;
-constexpr int kDynSmem = kScaleOff + kScaleSlots * kScaleSlot + 1024;  // + alignment slack
-constexpr int kThreads = 17 * 32;
+constexpr int kGroupOff = kRingBytes;
+constexpr int kDynSmem = kGroupOff + kGroups * (kGroupPk + kGroupSc) + 1024;  // + alignment slack
+constexpr int kThreads = 15 * 32;
 constexpr int kTmemCols = 2 * kNMax;
 constexpr long long kWaitCycles = 4000000000ll;  // ~2 s at the B200's clocks
+
+// Warp roles.
+constexpr int kConvWarps = 8, kEpiWarp0 = 8, kWeightWarp = 12, kTokenWarp = 13, kMmaWarp = 14;
 
 // Per-role cycle counters, compiled in with -DGW_GROUPED_TRACE: lane 0 of
 // the first warp of each role adds the cycles it spent in each phase to
 // g_grouped_trace[slot] (summed over CTAs); read with gw_grouped_trace().
 #ifdef GW_GROUPED_TRACE
 __device__ unsigned long long g_grouped_trace[16];
-__device__ unsigned long long g_grouped_trace_conv;
 #define GT_START(v) const long long v = clock64()
 #define GT_ADD(slot, v, lead) \
-    do { if (lead) atomicAdd(&g_grouped_trace[slot], (unsigned long long)(clock64() - (v))); } while (0)
+    do { if (lead) gt_acc[slot] += clock64() - (v); } while (0)
 #define GT_COUNT(slot, lead) \
-    do { if (lead) atomicAdd(&g_grouped_trace[slot], 1ull); } while (0)
+    do { if (lead) gt_acc[slot] += 1; } while (0)
+#define GT_FLUSH(lead)                                                                           \
+    do {                                                                                         \
+        if (lead)                                                                                \
+            for (int i_ = 0; i_ < 16; ++i_)                                                      \
+                if (gt_acc[i_]) atomicAdd(&g_grouped_trace[i_], (unsigned long long)gt_acc[i_]); \
+    } while (0)
 #else
+#define GT_FLUSH(lead) \
+    do { } while (0)
 #define GT_START(v) \
     do { } while (0)
 #define GT_ADD(slot, v, lead) \
@@ -89,7 +108,6 @@ struct GroupedArgs {
     int M, K;                 // rows and columns of the expert matrix
     int sec_packed, sec_scales, sec_bias;
     int rexp_off;             // row offset of this matrix in the row-exponent table
-    const __half* bsrc;       // token rows (x16 for gate_up, act for down)
     int bdiv;                 // token row = slot / bdiv
     int mode;                 // 0 gate_up clamped GLU, 1 gate_up SiLU, 2 down
 };
@@ -104,7 +122,7 @@ __device__ __forceinline__ void bar_init(uint64_t* b, uint32_t n) {
 // True once the phase with `parity` has completed.
 __device__ __forceinline__ bool bar_try(uint64_t* b, uint32_t parity) {
     uint32_t ok;
-#ifdef GW_TRACE_TEST_WAIT
+#ifdef GW_TRACE_SPIN_WAIT
     asm volatile(
         "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
@@ -124,26 +142,35 @@ __device__ __forceinline__ bool bar_try(uint64_t* b, uint32_t parity) {
 __device__ __forceinline__ void bar_arrive(uint64_t* b) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(b)) : "memory");
 }
+__device__ __forceinline__ void bar_arrive_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(b)), "r"(bytes)
+                 : "memory");
+}
+// Contiguous global -> shared copy of `bytes` (multiple of 16, both ends
+// 16-byte aligned), counted on `b` as it lands.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* b) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            saddr(dst)),
+        "l"(src), "r"(bytes), "r"(saddr(b))
+        : "memory");
+}
+// One 2D tile of `map` at (x, y) -> shared, counted on `b`.
+__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* b) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+        "%3}], [%4];" ::"r"(saddr(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(saddr(b))
+        : "memory");
+}
+// Brings one 2D tile of `map` at (x, y) into L2 (no shared-memory write).
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int x, int y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(x), "r"(y)
+                 : "memory");
+}
 __device__ __forceinline__ void fence_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
-__device__ __forceinline__ void cp16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp8(void* dst, const void* src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(saddr(dst)), "l"(src) : "memory");
-}
-// Arrives on `b` once every cp.async this thread issued so far has landed
-// (counts as one of the barrier's expected arrivals).
-__device__ __forceinline__ void cp_arrive_noinc(uint64_t* b) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(saddr(b)) : "memory");
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 __device__ __forceinline__ void tc_after_sync() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
@@ -163,12 +190,13 @@ __device__ __forceinline__ void tc_mma(uint32_t tmem, uint64_t ad, uint64_t bd, 
         "l"(ad), "l"(bd), "r"(idesc), "r"(accumulate)
         : "memory");
 }
-// Shared-memory matrix descriptor, K-major, no swizzle: core matrices of 8
-// rows x 16 bytes; lbo = byte distance between the two K-adjacent core
-// matrices of one MMA, sbo = byte distance between 8-row groups.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+// Shared-memory matrix descriptor, K-major.  layout 0 = no swizzle (core
+// matrices of 8 rows x 16 bytes; lbo = distance between the two K-adjacent
+// core matrices of one MMA, sbo = distance between 8-row groups); layout 2 =
+// 128-byte swizzle (rows of 128 bytes, sbo = 1024 between 8-row atoms).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
     return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
-           ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | ((uint64_t)1 << 46);
+           ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | ((uint64_t)1 << 46) | ((uint64_t)layout << 61);
 }
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     uint32_t r[16];
@@ -228,13 +256,15 @@ __device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
 }
 
 struct Shared {
-    uint64_t full[kStages], empty[kStages], tfull[2], tempty[2], fin;
+    uint64_t full[kStages], empty[kStages], gfull[kGroups], gempty[kGroups], tfull[2], tempty[2], fin;
     uint32_t tmem;
     int abort;
-    int nact, nitems;
+    int nact, nitems, chunks, mt;
     int prefix[kMaxExperts + 1];  // token chunks before active expert a
     int expert[kMaxExperts];
     int count[kMaxExperts];
+    int goff[kMaxExperts];        // first expert-ordered row of active expert a
+    int epre[kMaxExperts];        // expert-ordered rows before expert e (all experts)
     int col_slot[kNMax];          // epilogue: slot of each token column
     float col_mul[kNMax];         // epilogue: xmul (gate_up) or routing weight (down)
 #ifdef GW_GROUPED_TRACE
@@ -244,14 +274,14 @@ struct Shared {
 
 struct Item {
     int e, m0, c0, n;
+    int g0;  // expert-ordered row of the chunk's first token
 };
 
-// Items are numbered tile-major (item = m * chunks + j): CTAs that run at
-// the same time take different experts' token chunks, so no set of token rows
-// is read by dozens of SMs at once.
-__device__ __forceinline__ Item decode(const Shared& sh, int it, int mt) {
-    const int chunks = sh.nitems / mt;
-    const int m = it / chunks, j = it - m * chunks;
+// Items are numbered chunk-major (item = j * mt + m): the row tiles of one
+// token chunk run at about the same time on neighbouring CTAs, so the chunk's
+// token rows come from DRAM once and from L2 for the other tiles.
+__device__ __forceinline__ Item decode(const Shared& sh, int it) {
+    const int j = it / sh.mt, m = it - j * sh.mt;
     Item r;
     r.m0 = m * kM;
     int lo = 0, hi = sh.nact;
@@ -262,6 +292,7 @@ __device__ __forceinline__ Item decode(const Shared& sh, int it, int mt) {
     r.e = sh.expert[lo];
     r.c0 = (j - sh.prefix[lo]) * kNMax;
     r.n = min(kNMax, sh.count[lo] - r.c0);
+    r.g0 = sh.goff[lo] + r.c0;
     return r;
 }
 
@@ -287,262 +318,265 @@ __device__ __forceinline__ bool wait_on(Shared& sh, uint64_t* b, uint32_t parity
                                         unsigned bit) {
     return bar_try(b, parity) || wait_slow(sh, b, parity, status, bit);
 }
+// The same, waited for by lane 0 for its whole warp.
+__device__ __forceinline__ bool warp_wait(Shared& sh, uint64_t* b, uint32_t parity, unsigned* status,
+                                          unsigned bit) {
+    bool ok = true;
+    if ((threadIdx.x & 31) == 0) ok = wait_on(sh, b, parity, status, bit);
+    return __shfl_sync(0xffffffffu, ok, 0);
+}
 
 // ---- roles ----------------------------------------------------------------
 
-// Converters: thread c owns weight row m0 + (c & 127) and, of each stage's
-// two 32-column blocks, block (c >> 7).  One lane per warp does the ring's
-// barrier work for its warp.
-__device__ __forceinline__ void role_convert(Shared& sh, const GroupedArgs& a, char* smem, int mt) {
-    const int c = threadIdx.x;
-    const int r = c & (kM - 1), h = c >> 7, lane = c & 31;
-    const int lr = r & 15;  // m0 is a multiple of 128
-    const int nblk = a.K >> 5, ks = a.K / kKS;
-    const int stride_g = gridDim.x;
+// Weight producer (one warp, converged): for every item, every 8-block group
+// of its 128-row tile, once the ring slot is free; lane t copies tile t.
+__device__ __forceinline__ void role_weights(Shared& sh, const GroupedArgs& a, char* smem, long long (&gt_acc)[16]) {
+    const int nblk = a.K >> 5, ngrp = (nblk + 7) >> 3;
+    const int lane = threadIdx.x & 31;
     unsigned* status = a.w.status;
-    char* raw = smem + kRawOff + h * (kRawSlot / 2) + r * 16;
-    char* scl = smem + kScaleOff + h * (kScaleSlot / 2) + r * 16;
-
-    // issue cursor (kRaw - 1 stages ahead of the consume cursor)
-    int it_i = blockIdx.x, s_i = 0, g_i = 0, gr_i = 0;
-    bool valid_i = false;
-    const uint8_t *pk_i = nullptr, *sc_i = nullptr;
-    int emax_pending = 127;
-    auto issue = [&]() {
-        if (it_i < sh.nitems) {
-            if (s_i == 0) {
-                const Item item = decode(sh, it_i, mt);
-                const int R = item.m0 + r;
-                valid_i = R < a.M;
-                const int64_t le = item.e / a.d.shard_count;
-                const uint8_t* ex = a.L.base + le * a.L.stride;
-                const int64_t tile_blocks = (int64_t)(R >> 4) * 16 * nblk;
-                pk_i = ex + a.L.off[a.sec_packed] + tile_blocks * 16;
-                sc_i = ex + a.L.off[a.sec_scales] + tile_blocks;
-                emax_pending = valid_i ? (int)a.L.rowexp[le * a.L.rowexp_stride + a.rexp_off + R] : 127;
-            }
-            const int grp = s_i >> 2, w = min(8, nblk - 8 * grp);
+    char* ring = smem + kGroupOff;
+    int gq = 0;
+    for (int it = blockIdx.x; it < sh.nitems; it += gridDim.x) {
+        const Item item = decode(sh, it);
+        const int64_t le = item.e / a.d.shard_count;
+        const uint8_t* ex = a.L.base + le * a.L.stride;
+        const int64_t tile0 = item.m0 >> 4;
+        const uint8_t* pk = ex + a.L.off[a.sec_packed] + tile0 * 16 * nblk * 16;
+        const uint8_t* sc = ex + a.L.off[a.sec_scales] + tile0 * 16 * nblk;
+        const int tiles = min(8, (a.M - item.m0) >> 4);
+        for (int grp = 0; grp < ngrp; ++grp, ++gq) {
+            const int slot = gq % kGroups;
+            GT_START(t0);
+            if (!warp_wait(sh, &sh.gempty[slot], ((gq / kGroups) & 1) ^ 1, status, 1u)) return;
+            GT_ADD(0, t0, lane == 0);
+            const int w = min(8, nblk - 8 * grp);
+            const uint32_t run = 16 * w * 16, srun = 16 * w;  // bytes per tile: blocks, scales
+            char* dpk = ring + slot * (kGroupPk + kGroupSc);
+            char* dsc = dpk + kGroupPk;
 #ifdef GW_TRACE_SKIP_RAW
+            if (lane == 0) bar_arrive(&sh.gfull[slot]);
             if (false) {
 #else
-            if (valid_i) {
+            if (lane == 0) bar_arrive_tx(&sh.gfull[slot], tiles * (run + srun));
+            __syncwarp();
+            if (lane < tiles) {
 #endif
-                const int64_t blk = (int64_t)grp * 128 + lr * w + ((2 * s_i + h) & 7);
-                cp16(raw + (g_i % kRaw) * kRawSlot, pk_i + blk * 16);
-                if ((s_i & 3) == 0) {
-                    const int64_t off = (int64_t)grp * 128 + ((lr * w) & ~7);
-                    char* sd = scl + (gr_i % kScaleSlots) * kScaleSlot;
-                    cp8(sd, sc_i + off);
-                    cp8(sd + 8, sc_i + off + 8);
+                const int t = lane;
+                bulk_g2s(dpk + t * kTileRun, pk + (int64_t)t * 16 * nblk * 16 + grp * 128 * 16, run,
+                         &sh.gfull[slot]);
+                bulk_g2s(dsc + t * 128, sc + (int64_t)t * 16 * nblk + grp * 128, srun, &sh.gfull[slot]);
+            }
+        }
+    }
+}
+
+// Converters: thread c owns weight row m0 + (c & 127) and, of each stage's
+// two 32-column blocks, block (c >> 7).  Lane 0 of each warp does the
+// barrier work for its warp.
+__device__ __forceinline__ void role_convert(Shared& sh, const GroupedArgs& a, char* smem, long long (&gt_acc)[16]) {
+    const int c = threadIdx.x;
+    const int r = c & (kM - 1), h = c >> 7, lane = c & 31;
+    const int lr = r & 15, tile = r >> 4;
+    const int nblk = a.K >> 5, ks = a.K / kKS;
+    unsigned* status = a.w.status;
+    const char* ring = smem + kGroupOff;
+    auto row_emax = [&](int it) -> int {
+        if (it >= sh.nitems) return 127;
+        const Item item = decode(sh, it);
+        const int R = item.m0 + r;
+        if (R >= a.M) return 127;
+        return a.L.rowexp[(int64_t)(item.e / a.d.shard_count) * a.L.rowexp_stride + a.rexp_off + R];
+    };
+    int emax_next = row_emax(blockIdx.x);
+    int g = 0, gq = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; ok && it < sh.nitems; it += gridDim.x) {
+        const Item item = decode(sh, it);
+        const bool valid = item.m0 + r < a.M;
+        const int emax = emax_next;
+        emax_next = row_emax(it + gridDim.x);  // lands while this item runs
+        for (int s = 0; s < ks; ++s, ++g) {
+            [[maybe_unused]] const bool lead = c == 0;
+            const int sub = s & 3, w = min(8, nblk - 8 * (s >> 2));
+            const bool group_end = 2 * sub + 2 == w;
+            const int gslot = gq % kGroups;
+            bool ok_w = true;
+            GT_START(t0);
+            if (sub == 0) ok_w = warp_wait(sh, &sh.gfull[gslot], (gq / kGroups) & 1, status, 2u);
+            GT_ADD(1, t0, lead);
+            GT_START(t1);
+            uint4 out[4];
+#ifdef GW_TRACE_SKIP_CONVERT
+            if (false) {
+#else
+            if (ok_w && valid) {
+#endif
+                const char* gb = ring + gslot * (kGroupPk + kGroupSc);
+                const int bl = 2 * sub + h;
+                const uint4 q = *reinterpret_cast<const uint4*>(gb + tile * kTileRun + (lr * w + bl) * 16);
+                const uint32_t sb = *reinterpret_cast<const uint8_t*>(gb + kGroupPk + tile * 128 + lr * w + bl);
+                const uint32_t hs = block_scale_h2(sb, emax);
+                const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    out[j].x = hmul2_bits(e2m1x2(wd[j] & 0xFF), hs);
+                    out[j].y = hmul2_bits(e2m1x2((wd[j] >> 8) & 0xFF), hs);
+                    out[j].z = hmul2_bits(e2m1x2((wd[j] >> 16) & 0xFF), hs);
+                    out[j].w = hmul2_bits(e2m1x2(wd[j] >> 24), hs);
                 }
             }
-            if ((s_i & 3) == 0) ++gr_i;
-            ++g_i;
-            if (++s_i == ks) { s_i = 0; it_i += stride_g; }
-        }
-        cp_commit();
-    };
-
-    for (int i = 0; i < kRaw - 1; ++i) issue();
-
-    int it_c = blockIdx.x, s_c = 0, g_c = 0, gr_c = 0, gslot = 0, sub = 0;
-    int emax = 127;
-    bool valid_c = false;
-    while (it_c < sh.nitems) {
-        [[maybe_unused]] const bool lead = c == 0;
-        if (s_c == 0) {
-            const Item item = decode(sh, it_c, mt);
-            valid_c = item.m0 + r < a.M;
-            emax = emax_pending;
-        }
-        if ((s_c & 3) == 0) {
-            const int w = min(8, nblk - 8 * (s_c >> 2));
-            sub = (lr * w) & 7;
-            gslot = gr_c % kScaleSlots;
-            ++gr_c;
-        }
-        GT_START(t0);
-        issue();
-        cp_wait<kRaw - 1>();
-        GT_ADD(0, t0, lead);
-        GT_START(t1);
-        uint4 out[4];
+            GT_ADD(2, t1, lead);
+            const int slot = g % kStages;
+            GT_START(t2);
+            if (ok_w) ok_w = warp_wait(sh, &sh.empty[slot], ((g / kStages) & 1) ^ 1, status, 4u);
+            GT_ADD(3, t2, lead);
 #ifdef GW_TRACE_SKIP_CONVERT
-        if (false) {
+            if (false) {
 #else
-        if (valid_c) {
+            if (ok_w && valid) {
 #endif
-            const uint4 q = *reinterpret_cast<const uint4*>(raw + (g_c % kRaw) * kRawSlot);
-            const uint8_t sb = *(reinterpret_cast<const uint8_t*>(scl + gslot * kScaleSlot) + sub +
-                                 ((2 * s_c + h) & 7));
-            const uint32_t hs = block_scale_h2(sb, emax);
-            const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+                char* A = smem + slot * (kASlot + kBSlot) + (r >> 3) * 1024 + (r & 7) * 16 + h * 512;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                out[j].x = hmul2_bits(e2m1x2(wd[j] & 0xFF), hs);
-                out[j].y = hmul2_bits(e2m1x2((wd[j] >> 8) & 0xFF), hs);
-                out[j].z = hmul2_bits(e2m1x2((wd[j] >> 16) & 0xFF), hs);
-                out[j].w = hmul2_bits(e2m1x2(wd[j] >> 24), hs);
+                for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(A + j * 128) = out[j];
+                fence_async_smem();
             }
-        }
-        const int slot = g_c % kStages;
-        GT_ADD(1, t1, lead);
-        GT_START(t2);
-        bool ok = true;
-        if (lane == 0) ok = wait_on(sh, &sh.empty[slot], ((g_c / kStages) & 1) ^ 1, status, 1u);
-        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
-        GT_ADD(2, t2, lead);
-        GT_START(t3);
-        if (valid_c) {
-            char* A = smem + slot * (kASlot + kBSlot) + (r >> 3) * 1024 + (r & 7) * 16 + h * 512;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(A + j * 128) = out[j];
-            fence_async_smem();
-        }
-        __syncwarp();
+            if (!ok_w) { ok = false; break; }
+            __syncwarp();
 #ifdef GW_GROUPED_TRACE
-        if (lead) *(volatile long long*)&sh.conv_arrived[slot] = clock64();
+            if (c == 224) *(volatile long long*)&sh.conv_arrived[slot] = clock64();  // last converter warp
 #endif
-        if (lane == 0) bar_arrive(&sh.full[slot]);
-        GT_ADD(3, t3, lead);
-        GT_COUNT(13, lead);
-        ++g_c;
-        if (++s_c == ks) { s_c = 0; it_c += stride_g; }
+            if (lane == 0) {
+                bar_arrive(&sh.full[slot]);
+                if (group_end) bar_arrive(&sh.gempty[gslot]);  // its group bytes have been read
+            }
+            if (group_end) ++gq;
+            GT_COUNT(13, lead);
+        }
     }
-    cp_wait_all();
 }
 
-// Token loaders: thread t copies 16-byte column chunk (t & 7) of chunk rows
-// (t >> 3) + 16 q, q = 0..7.  Completion is signalled to the stage's full
-// barrier by the copies themselves, so the loaders run ahead as far as the
-// ring allows.
-__device__ __forceinline__ void role_tokens(Shared& sh, const GroupedArgs& a, char* smem, int mt) {
-    constexpr int kRows = kNMax / 16;
-    const int t = threadIdx.x - 256;
-    const int c = t & 7, rb = t >> 3;
+// Token producer (one warp, converged; lane 0 issues): the chunk's rows are consecutive in the
+// expert-ordered token matrix, so each stage is one 2D TMA of 128 rows x 64
+// columns (rows past the chunk belong to the next expert and only fill
+// columns the epilogue ignores; rows past the matrix read as zero).
+__device__ __forceinline__ void role_tokens(Shared& sh, const GroupedArgs& a, char* smem,
+                                            const CUtensorMap* map, long long (&gt_acc)[16]) {
     const int ks = a.K / kKS;
+    const int lane = threadIdx.x & 31;
     unsigned* status = a.w.status;
-    int rid[kRows], nrid[kRows];
-    auto load_rows = [&](int it, int (&dst)[kRows]) {
-        if (it >= sh.nitems) return;
-        const Item item = decode(sh, it, mt);
-        const int32_t* list = a.w.lists + (int64_t)item.e * a.w.tcap + item.c0;
-#pragma unroll
-        for (int q = 0; q < kRows; ++q) {
-            const int row = rb + 16 * q;
-            dst[q] = row < item.n ? __ldg(list + row) / a.bdiv : -1;
-        }
-    };
-    load_rows(blockIdx.x, nrid);
-    int it = blockIdx.x, s = 0, g = 0;
-    while (it < sh.nitems) {
-        if (s == 0) {
-#pragma unroll
-            for (int q = 0; q < kRows; ++q) rid[q] = nrid[q];
-            load_rows(it + gridDim.x, nrid);  // next item's rows, landing during this one
-        }
-        const int slot = g % kStages;
-        GT_START(t0);
-        if (!wait_on(sh, &sh.empty[slot], ((g / kStages) & 1) ^ 1, status, 2u)) break;
-        GT_ADD(4, t0, t == 0);
-        GT_START(t1);
-        char* B = smem + slot * (kASlot + kBSlot) + kASlot + c * 128;
-        const __half* src = a.bsrc + s * kKS + c * 8;
-#pragma unroll
-        for (int q = 0; q < kRows; ++q) {
-            const int row = rb + 16 * q;
-#ifndef GW_TRACE_SKIP_TOKENS
-            if (rid[q] >= 0) cp16(B + (row >> 3) * 1024 + (row & 7) * 16, src + (int64_t)rid[q] * a.K);
+    constexpr int kAhead = 8;  // stages between a tile's L2 prefetch and its load
+    int g = 0;
+    for (int it = blockIdx.x; it < sh.nitems; it += gridDim.x) {
+        const Item item = decode(sh, it);
+        const int nit = it + gridDim.x;
+        const int g0_next = nit < sh.nitems ? decode(sh, nit).g0 : -1;
+        if (it == (int)blockIdx.x && lane == 0)
+            for (int s = 0; s < kAhead && s < ks; ++s) tma_prefetch_2d(map, s * kKS, item.g0);
+        for (int s = 0; s < ks; ++s, ++g) {
+            const int slot = g % kStages;
+            if (lane == 0) {  // the tile kAhead stages on, possibly in the next item
+                const int sp = s + kAhead;
+                if (sp < ks) tma_prefetch_2d(map, sp * kKS, item.g0);
+                else if (g0_next >= 0 && sp - ks < ks) tma_prefetch_2d(map, (sp - ks) * kKS, g0_next);
+            }
+            GT_START(t0);
+            if (!warp_wait(sh, &sh.empty[slot], ((g / kStages) & 1) ^ 1, status, 8u)) return;
+            GT_ADD(4, t0, lane == 0);
+            if (lane == 0) {
+                char* B = smem + slot * (kASlot + kBSlot) + kASlot;
+#ifdef GW_TRACE_SKIP_TOKENS
+                bar_arrive(&sh.full[slot]);
+                (void)B; (void)map;
+#else
+                bar_arrive_tx(&sh.full[slot], kBSlot);
+                tma_2d(B, map, s * kKS, item.g0, &sh.full[slot]);
 #endif
-        }
-        cp_arrive_noinc(&sh.full[slot]);
-        GT_ADD(5, t1, t == 0);
 #ifdef GW_GROUPED_TRACE
-        if (t == 0) *(volatile long long*)&sh.tok_issued[slot] = clock64();
+                *(volatile long long*)&sh.tok_issued[slot] = clock64();
 #endif
-        ++g;
-        if (++s == ks) { s = 0; it += gridDim.x; }
+            }
+            __syncwarp();
+        }
     }
-    cp_wait_all();
 }
 
-// MMA issuer: one thread.
-__device__ __forceinline__ void role_mma(Shared& sh, const GroupedArgs& a, char* smem, int mt) {
+// MMA issuer: one warp, converged; lane 0 issues.
+__device__ __forceinline__ void role_mma(Shared& sh, const GroupedArgs& a, char* smem, long long (&gt_acc)[16]) {
     const int ks = a.K / kKS;
+    const int lane = threadIdx.x & 31;
     unsigned* status = a.w.status;
     const uint32_t base = saddr(smem);
-    int it = blockIdx.x, g = 0, il = 0;
+    int g = 0, il = 0;
     bool ok = true;
-    while (ok && it < sh.nitems) {
-        const Item item = decode(sh, it, mt);
+    for (int it = blockIdx.x; ok && it < sh.nitems; it += gridDim.x, ++il) {
+        const Item item = decode(sh, it);
         const int n = max(16, (item.n + 15) & ~15);
         const uint32_t idesc = (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kM >> 4) << 24);
         const int b = il & 1;
         GT_START(t0);
-        if (!wait_on(sh, &sh.tempty[b], ((il >> 1) & 1) ^ 1, status, 4u)) break;
-        GT_ADD(7, t0, true);
+        if (!warp_wait(sh, &sh.tempty[b], ((il >> 1) & 1) ^ 1, status, 16u)) break;
+        GT_ADD(7, t0, lane == 0);
         tc_after_sync();
         const uint32_t tmem = sh.tmem + b * kNMax;
         for (int s = 0; s < ks; ++s, ++g) {
             const int slot = g % kStages;
             GT_START(t1);
-            if (!wait_on(sh, &sh.full[slot], (g / kStages) & 1, status, 8u)) { ok = false; break; }
-            GT_ADD(6, t1, true);
+            if (!warp_wait(sh, &sh.full[slot], (g / kStages) & 1, status, 32u)) { ok = false; break; }
+            GT_ADD(6, t1, lane == 0);
 #ifdef GW_GROUPED_TRACE
             {
-                // time from the token loads' issue / the converters' arrival to full
                 const long long now = clock64();
-                atomicAdd(&g_grouped_trace[15], (unsigned long long)(now - *(volatile long long*)&sh.tok_issued[slot]));
-                atomicAdd(&g_grouped_trace_conv, (unsigned long long)(now - *(volatile long long*)&sh.conv_arrived[slot]));
+                if (lane == 0) {
+                    gt_acc[5] += now - *(volatile long long*)&sh.tok_issued[slot];
+                    gt_acc[15] += now - *(volatile long long*)&sh.conv_arrived[slot];
+                }
             }
 #endif
             GT_START(t2);
             tc_after_sync();
-            fence_async_smem();  // token rows landed through cp.async (generic proxy)
             const uint32_t A = base + slot * (kASlot + kBSlot), B = A + kASlot;
+            if (lane == 0) {
 #pragma unroll
-            for (int k = 0; k < kKS / 16; ++k)
+                for (int k = 0; k < kKS / 16; ++k)
 #ifndef GW_TRACE_SKIP_MMA
-                tc_mma(tmem, smem_desc(A + k * 256, 128, 1024), smem_desc(B + k * 256, 128, 1024), idesc,
-                       (s | k) != 0);
+                    tc_mma(tmem, smem_desc(A + k * 256, 128, 1024, 0), smem_desc(B + k * 32, 16, 1024, 2),
+                           idesc, (s | k) != 0);
 #else
-                ;
+                    (void)idesc;
 #endif
-            tc_commit(&sh.empty[slot]);
-            GT_ADD(8, t2, true);
-#ifdef GW_TRACE_COMMIT_LATENCY
-            {
-                GT_START(t3);
-                while (!bar_try(&sh.empty[slot], (g / kStages) & 1)) {}
-                GT_ADD(15, t3, true);
+                tc_commit(&sh.empty[slot]);
             }
-#endif
+            __syncwarp();
+            GT_ADD(8, t2, lane == 0);
         }
         if (!ok) break;
-        tc_commit(&sh.tfull[b]);
-        ++il;
-        it += gridDim.x;
+        if (lane == 0) tc_commit(&sh.tfull[b]);
+        __syncwarp();
     }
-    // every MMA this thread issued has finished before TMEM is freed
-    tc_commit(&sh.fin);
-    const long long t0 = clock64();
-    while (!bar_try(&sh.fin, 0)) {
-        if (clock64() - t0 > kWaitCycles) {
-            if (status) atomicOr(status, 16u);
-            break;
+    // every MMA this warp issued has finished before TMEM is freed
+    if (lane == 0) {
+        tc_commit(&sh.fin);
+        const long long t0 = clock64();
+        while (!bar_try(&sh.fin, 0)) {
+            if (clock64() - t0 > kWaitCycles) {
+                if (status) atomicOr(status, 64u);
+                break;
+            }
         }
     }
+    __syncwarp();
 }
 
+// Epilogue: thread t (0..127) owns TMEM lane t = tile row m0 + t.
 template <int kMode>
-__device__ __forceinline__ void role_epilogue(Shared& sh, const GroupedArgs& a, int mt) {
-    const int t = threadIdx.x - 384;  // 0..127 = TMEM lane = tile row
+__device__ __forceinline__ void role_epilogue(Shared& sh, const GroupedArgs& a, long long (&gt_acc)[16]) {
+    const int t = threadIdx.x - kEpiWarp0 * 32;
     const int ew = t >> 5, lane = t & 31;
     unsigned* status = a.w.status;
-    int it = blockIdx.x, il = 0;
-    while (it < sh.nitems) {
+    int il = 0;
+    for (int it = blockIdx.x; it < sh.nitems; it += gridDim.x, ++il) {
         GT_START(t0);
-        const Item item = decode(sh, it, mt);
+        const Item item = decode(sh, it);
         const int R = item.m0 + t;
         const bool valid = R < a.M;
         const int64_t le = item.e / a.d.shard_count;
@@ -552,7 +586,7 @@ __device__ __forceinline__ void role_epilogue(Shared& sh, const GroupedArgs& a, 
         const float bv = valid ? bf16_bits_to_f32(bias[R]) : 0.f;
         const int p = emax - 128, p1 = p / 2;  // undoes the 2^(1 - emax) row shift
         const float rs1 = pow2f(p1), rs2 = pow2f(p - p1);
-        // column metadata for the chunk
+        // column metadata for the chunk, one column per thread
         const int32_t* list = a.w.lists + (int64_t)item.e * a.w.tcap + item.c0;
         static_assert(kNMax == 128, "one column per epilogue thread");
         const int cs = t < item.n ? __ldg(list + t) : 0;
@@ -564,18 +598,14 @@ __device__ __forceinline__ void role_epilogue(Shared& sh, const GroupedArgs& a, 
         const int b = il & 1;
         GT_ADD(11, t0, t == 0);
         GT_START(t1);
-        const bool got = wait_on(sh, &sh.tfull[b], (il >> 1) & 1, status, 32u);
+        const bool got = wait_on(sh, &sh.tfull[b], (il >> 1) & 1, status, 128u);
         if (group_any(!got, 2, 128)) break;
         GT_ADD(9, t1, t == 0);
         GT_START(t2);
         tc_after_sync();
         const uint32_t taddr = sh.tmem + b * kNMax + ((uint32_t)(ew * 32) << 16);
-        float pbv = __shfl_xor_sync(0xffffffffu, bv, 1);
-#ifdef GW_TRACE_SKIP_EPILOGUE
-        for (int j0 = 0; j0 < 0; j0 += 16) {
-#else
+        const float pbv = __shfl_xor_sync(0xffffffffu, bv, 1);
         for (int j0 = 0; j0 < item.n; j0 += 16) {
-#endif
             float v[16];
             tmem_ld16(taddr + j0, v);
 #pragma unroll
@@ -589,9 +619,8 @@ __device__ __forceinline__ void role_epilogue(Shared& sh, const GroupedArgs& a, 
                     const float partner = __shfl_xor_sync(0xffffffffu, acc, 1);
                     if (valid && (lane & 1) == 0 && col < item.n) {
                         const float xm = sh.col_mul[col];
-                        const float y = activate<kMode>(acc * xm + bv, partner * xm + pbv, a.d.limit,
-                                                            a.d.alpha);
-                        a.w.act[(int64_t)sh.col_slot[col] * a.d.F + (R >> 1)] = __float2half_rn(y);
+                        const float y = activate<kMode>(acc * xm + bv, partner * xm + pbv, a.d.limit, a.d.alpha);
+                        a.w.act[(int64_t)(item.g0 + col) * a.d.F + (R >> 1)] = __float2half_rn(y);
                     }
                 }
             }
@@ -600,13 +629,12 @@ __device__ __forceinline__ void role_epilogue(Shared& sh, const GroupedArgs& a, 
         bar_arrive(&sh.tempty[b]);
         GT_ADD(10, t2, t == 0);
         GT_COUNT(14, t == 0);
-        ++il;
-        it += gridDim.x;
     }
 }
 
 template <int kMode>
-__global__ void __launch_bounds__(kThreads, 1) k_grouped(GroupedArgs a) {
+__global__ void __launch_bounds__(kThreads, 1) k_grouped(const __grid_constant__ CUtensorMap bmap,
+                                                         GroupedArgs a) {
     extern __shared__ unsigned char dyn_raw[];
     __shared__ Shared sh;
     char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(dyn_raw) + 1023) & ~uintptr_t(1023));
@@ -626,7 +654,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_grouped(GroupedArgs a) {
     if (tid == 0) {
         sh.abort = 0;
         sh.nact = nact;
-        for (int i = 0; i < kStages; ++i) { bar_init(&sh.full[i], 8 + 128); bar_init(&sh.empty[i], 1); }
+        for (int i = 0; i < kStages; ++i) { bar_init(&sh.full[i], kConvWarps + 1); bar_init(&sh.empty[i], 1); }
+        for (int i = 0; i < kGroups; ++i) { bar_init(&sh.gfull[i], 1); bar_init(&sh.gempty[i], kConvWarps); }
         for (int i = 0; i < 2; ++i) { bar_init(&sh.tfull[i], 1); bar_init(&sh.tempty[i], 128); }
         bar_init(&sh.fin, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -653,11 +682,34 @@ __global__ void __launch_bounds__(kThreads, 1) k_grouped(GroupedArgs a) {
             if (i < nact) sh.prefix[i] = run;
             run += v[j];
         }
-        if (lane == 31) { sh.prefix[nact] = incl; sh.nitems = incl * mt; }
+        if (lane == 31) { sh.prefix[nact] = incl; sh.chunks = incl; sh.mt = mt; sh.nitems = incl * mt; }
+    } else if (warp == 1) {  // expert-ordered row offsets: exclusive prefix over all experts' counts
+        int v[8], sum = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int e = lane * 8 + j;
+            v[j] = e < a.d.E ? min(a.w.counts[e], a.w.tcap) : 0;
+            sum += v[j];
+        }
+        int incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        int run = incl - sum;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int e = lane * 8 + j;
+            if (e < a.d.E) sh.epre[e] = run;
+            run += v[j];
+        }
     }
     __syncthreads();
+    for (int i = tid; i < nact; i += blockDim.x) sh.goff[i] = sh.epre[sh.expert[i]];
+    __syncthreads();
     if (sh.nitems <= (int)blockIdx.x) return;  // no work for this CTA (uniform)
-    if (warp == 16) {
+    if (warp == kMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&sh.tmem)),
                      "r"(kTmemCols)
                      : "memory");
@@ -667,65 +719,50 @@ __global__ void __launch_bounds__(kThreads, 1) k_grouped(GroupedArgs a) {
     __syncthreads();
     tc_after_sync();
 
-    if (warp < 8) role_convert(sh, a, smem, mt);
-    else if (warp < 12) role_tokens(sh, a, smem, mt);
-    else if (warp < 16) role_epilogue<kMode>(sh, a, mt);
-    else if (lane == 0) role_mma(sh, a, smem, mt);
+    [[maybe_unused]] long long gt_acc[16] = {};  // phase cycle counters (trace builds)
+    if (warp < kConvWarps) role_convert(sh, a, smem, gt_acc);
+    else if (warp < kWeightWarp) role_epilogue<kMode>(sh, a, gt_acc);
+    else if (warp == kWeightWarp) role_weights(sh, a, smem, gt_acc);
+    else if (warp == kTokenWarp) role_tokens(sh, a, smem, &bmap, gt_acc);
+    else role_mma(sh, a, smem, gt_acc);
 
     tc_before_sync();
     __syncthreads();
     tc_after_sync();
+    // A CTA that gave up may still have bulk copies landing in its shared
+    // memory: give them time (they complete in microseconds) before exiting.
+    if (*(volatile int*)&sh.abort) {
+        const long long t0 = clock64();
+        while (clock64() - t0 < 2000000) {}
+    }
     GT_ADD(12, tk, tid == 0);
-    if (warp == 16)
+    GT_FLUSH(true);
+    if (warp == kMmaWarp)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(sh.tmem), "r"(kTmemCols)
                      : "memory");
 }
 
-}  // namespace
-
-int grouped_smem_bytes() { return kDynSmem; }
-
-int configure_grouped() {
-    if (cudaFuncSetAttribute(k_grouped<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem) != cudaSuccess)
-        return -1;
-    if (cudaFuncSetAttribute(k_grouped<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem) != cudaSuccess)
-        return -1;
-    if (cudaFuncSetAttribute(k_grouped<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem) != cudaSuccess)
-        return -1;
-    return 0;
-}
-
-bool grouped_supported(const MoeDims& d, const MoeWork& w) {
-    // rows of both matrices split in 128-row tiles; columns in 64-column
-    // stages, at least one raw ring's worth per item
-    return w.status != nullptr && d.H % kKS == 0 && d.F % kKS == 0 && d.H / kKS >= kRaw &&
-           d.F / kKS >= kRaw;
-}
-
-int launch_grouped(const LayerView& L, const MoeDims& d, const MoeWork& w, int which, int sms,
-                   cudaStream_t s) {
-    GroupedArgs a;
-    a.L = L;
-    a.d = d;
-    a.w = w;
-    if (which == 0) {
-        a.M = 2 * d.F; a.K = d.H;
-        a.sec_packed = 0; a.sec_scales = 1; a.sec_bias = 4;
-        a.rexp_off = 0;
-        a.bsrc = w.x16; a.bdiv = d.k;
-        a.mode = d.act == 0 ? 0 : 1;
-    } else {
-        a.M = d.H; a.K = d.F;
-        a.sec_packed = 2; a.sec_scales = 3; a.sec_bias = 5;
-        a.rexp_off = 2 * d.F;
-        a.bsrc = w.act; a.bdiv = 1;
-        a.mode = 2;
+// x16 rows in expert order: row epre[e] + i = x16[list[e][i] / k] (epre the
+// exclusive prefix of the experts' token counts).  grid (E, 32), 256 threads.
+__global__ void __launch_bounds__(256) k_gather(MoeDims d, MoeWork w, int H) {
+    __shared__ int off;
+    const int e = blockIdx.x;
+    if (threadIdx.x < 32) {
+        int s = 0;
+        for (int j = threadIdx.x; j < e; j += 32) s += min(w.counts[j], w.tcap);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (threadIdx.x == 0) off = s;
     }
-    const dim3 grid(sms), block(kThreads);
-    if (a.mode == 0) k_grouped<0><<<grid, block, kDynSmem, s>>>(a);
-    else if (a.mode == 1) k_grouped<1><<<grid, block, kDynSmem, s>>>(a);
-    else k_grouped<2><<<grid, block, kDynSmem, s>>>(a);
-    return cudaGetLastError() == cudaSuccess ? 1 : -1;
+    __syncthreads();
+    const int cnt = min(w.counts[e], w.tcap);
+    const int chunks = H >> 3;  // 16-byte pieces per row
+    for (int i = blockIdx.y; i < cnt; i += gridDim.y) {
+        const int tok = w.lists[(int64_t)e * w.tcap + i] / d.k;
+        const uint4* src = reinterpret_cast<const uint4*>(w.x16 + (int64_t)tok * H);
+        uint4* dst = reinterpret_cast<uint4*>(w.xg + (int64_t)(off + i) * H);
+        for (int c = threadIdx.x; c < chunks; c += blockDim.x) dst[c] = src[c];
+    }
 }
 
 // Largest E8M0 exponent of each row (bytes 1..254; 127 when the row has
@@ -741,6 +778,81 @@ __global__ void k_rowexp(const uint8_t* __restrict__ scales, int rows, int nblk,
     out[r] = (uint8_t)(m == 0 ? 127 : m);
 }
 
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+}  // namespace
+
+int configure_grouped() {
+    if (cudaFuncSetAttribute(k_grouped<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem) != cudaSuccess)
+        return -1;
+    if (cudaFuncSetAttribute(k_grouped<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem) != cudaSuccess)
+        return -1;
+    if (cudaFuncSetAttribute(k_grouped<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem) != cudaSuccess)
+        return -1;
+    return 0;
+}
+
+bool grouped_supported(const MoeDims& d, const MoeWork& w) {
+    // 64-column stages in 8-block groups; rows of both matrices are multiples
+    // of 16 (bank creation requires multiples of 32 for H and F)
+    return w.status != nullptr && d.H % kKS == 0 && d.F % kKS == 0 && tensor_map_encoder() != nullptr;
+}
+
+int launch_grouped(const LayerView& L, const MoeDims& d, const MoeWork& w, int which, int sms,
+                   cudaStream_t s) {
+    GroupedArgs a;
+    a.L = L;
+    a.d = d;
+    a.w = w;
+    const void* bsrc;
+    uint64_t brows;
+    if (which == 0) {
+        a.M = 2 * d.F; a.K = d.H;
+        a.sec_packed = 0; a.sec_scales = 1; a.sec_bias = 4;
+        a.rexp_off = 0;
+        bsrc = w.xg; brows = (uint64_t)w.tcap * d.k; a.bdiv = d.k;
+        a.mode = d.act == 0 ? 0 : 1;
+    } else {
+        a.M = d.H; a.K = d.F;
+        a.sec_packed = 2; a.sec_scales = 3; a.sec_bias = 5;
+        a.rexp_off = 2 * d.F;
+        bsrc = w.act; brows = (uint64_t)w.tcap * d.k; a.bdiv = 1;
+        a.mode = 2;
+    }
+    // expert-ordered token rows: [brows][K] f16, loaded 64 columns x 128 rows
+    // at a time into 128-byte-swizzled shared rows
+    CUtensorMap map;
+    const cuuint64_t gdim[2] = {(cuuint64_t)a.K, (cuuint64_t)brows};
+    const cuuint64_t gstride[1] = {(cuuint64_t)a.K * 2};
+    const cuuint32_t box[2] = {kKS, kNMax}, estride[2] = {1, 1};
+    auto enc = tensor_map_encoder();
+    if (!enc || enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(bsrc), gdim, gstride, box,
+                    estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return -1;
+    int launched = 0;
+    if (which == 0) {
+        k_gather<<<dim3(d.E, 32), 256, 0, s>>>(d, w, d.H);
+        ++launched;
+    }
+    const dim3 grid(sms), block(kThreads);
+    if (a.mode == 0) k_grouped<0><<<grid, block, kDynSmem, s>>>(map, a);
+    else if (a.mode == 1) k_grouped<1><<<grid, block, kDynSmem, s>>>(map, a);
+    else k_grouped<2><<<grid, block, kDynSmem, s>>>(map, a);
+    return cudaGetLastError() == cudaSuccess ? launched + 1 : -1;
+}
+
 int launch_rowexp(const uint8_t* scales, int rows, int cols, uint8_t* out, cudaStream_t s) {
     k_rowexp<<<(rows + 127) / 128, 128, 0, s>>>(scales, rows, cols >> 5, out);
     return cudaGetLastError() == cudaSuccess ? 1 : -1;
@@ -749,9 +861,6 @@ int launch_rowexp(const uint8_t* scales, int rows, int cols, uint8_t* out, cudaS
 #ifdef GW_GROUPED_TRACE
 extern "C" __attribute__((visibility("default"))) int gw_grouped_trace(unsigned long long* out, int reset) {
     if (cudaMemcpyFromSymbol(out, g_grouped_trace, sizeof(g_grouped_trace)) != cudaSuccess) return -1;
-    unsigned long long conv = 0;
-    if (cudaMemcpyFromSymbol(&conv, g_grouped_trace_conv, sizeof(conv)) != cudaSuccess) return -1;
-    out[16] = conv;
     if (reset) {
         static const unsigned long long zero[16] = {};
         if (cudaMemcpyToSymbol(g_grouped_trace, zero, sizeof(zero)) != cudaSuccess) return -1;

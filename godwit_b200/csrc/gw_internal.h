@@ -48,7 +48,9 @@ struct MoeWork {
     int32_t* active;   // [E]          experts with at least one token (any order)
     int32_t* nactive;  // [1]
     int32_t* lists;    // [E][tcap]    slot ids (t*k + j) per expert
-    __half* act;       // [tcap*k][F]  activated gate_up output (f16, as the reference)
+    __half* act;       // [tcap*k][F]  activated gate_up output (f16, as the reference); slot
+                       //              order on the GEMV path, expert order on the tensor-core path
+    __half* xg;        // [tcap*k][H]  x16 rows gathered in expert order (tensor-core path)
     float* ybuf;       // [tcap*k][H]  routing-weighted down output per slot
     unsigned* done;    // [tcap/8+1]   router completion counter per token chunk (self-resetting)
     unsigned* status;  // [1]          sticky error bits set by bounded waits (nullptr: none)
