@@ -13,21 +13,24 @@
 //
 // One persistent CTA per SM walks a static list of work items (128-row tile,
 // expert, token chunk of <= 128).  Warp roles:
-//   warp 12     weight producer: one thread bulk-copies (cp.async.bulk) each
-//               8-block group of the tile — in the bank's tiled layout a
-//               contiguous 16 x 8 x 16-byte run per 16-row tile, plus its
-//               scale bytes — into a 3-group ring (mbarrier transaction
-//               counts signal arrival).
-//   warps 0-7   converters: widen each 128 x 64 stage of the ring to f16
-//               (cvt.rn.f16x2.e2m1x2, times the block scale) in the canonical
-//               K-major no-swizzle layout tcgen05 reads.
-//   warp 13     token producer: one thread, one 2D TMA (128 rows x 64
-//               columns, 128B swizzle) per stage from the expert-ordered f16
-//               token rows (x16 gathered by k_gather for gate_up; the gate_up
-//               epilogue writes its activations in that order for down).
-//   warp 14     MMA issuer: one thread, tcgen05.mma kind::f16 M=128 N=n K=16,
-//               fp32 accumulators in TMEM (two 128-column buffers so the
-//               epilogue of one item overlaps the main loop of the next).
+//   warp 12     weight producer: bulk-copies (cp.async.bulk) each 8-block
+//               group of the tile — in the bank's tiled layout a contiguous
+//               16 x w x 16-byte run per 16-row tile, plus its scale bytes —
+//               into a 3-group shared ring (mbarrier transaction counts
+//               signal arrival).
+//   warps 0-7   converters: widen each stage (128 rows x up to 128 columns)
+//               to f16 (cvt.rn.f16x2.e2m1x2, times the block scale) straight
+//               into tensor memory (tcgen05.st: thread = row = TMEM lane), a
+//               4-stage ring of 64 columns each.
+//   warp 13     token producer: one or two 2D TMAs (128 rows x 64 columns,
+//               128B swizzle) per stage from the expert-ordered f16 token rows
+//               (x16 gathered by k_gather for gate_up; the gate_up epilogue
+//               writes its activations in that order for down) into a 4-stage
+//               shared ring.
+//   warp 14     MMA issuer: one lane, tcgen05.mma kind::f16 M=128 N=n K=16
+//               with A in TMEM and B in shared memory, fp32 accumulators in
+//               TMEM (two 128-column buffers so the epilogue of one item
+//               overlaps the main loop of the next).
 //   warps 8-11  epilogue: tcgen05.ld the accumulators (one row per thread),
 //               scale, bias, activation / routing weight, store.
 // Every wait is bounded (~2 s); a wait that runs out sets a bit in the
@@ -56,19 +59,23 @@ namespace {
 
 constexpr int kM = 128;                   // weight rows per tile (MMA M)
 constexpr int kNMax = 128;                // token columns per chunk (MMA N max)
-constexpr int kKS = 64;                   // columns per stage (two MXFP4 blocks)
-constexpr int kStages = 5;                // operand ring the MMA reads
+constexpr int kKS = 128;                  // columns per stage (up to four MXFP4 blocks)
+constexpr int kStages = 4;                // operand ring the MMA reads
 constexpr int kGroups = 3;                // raw weight ring, in 8-block groups
-constexpr int kASlot = kM * kKS * 2;      // 16 KB of f16 weights per stage
-constexpr int kBSlot = kNMax * kKS * 2;   // 16 KB of f16 tokens per stage
+constexpr int kBox = 64;                  // token columns per TMA box (one 128-byte swizzled row)
+constexpr int kBBox = kNMax * kBox * 2;   // 16 KB: one box of token rows
+constexpr int kBSlot = 2 * kBBox;         // 32 KB of f16 tokens per stage
+constexpr int kACols = kKS / 2;           // TMEM columns of one stage's f16 weights (2 per column)
 constexpr int kTileRun = 16 * 8 * 16;     // one 16-row tile's blocks of a full group
 constexpr int kGroupPk = 8 * kTileRun;    // 16 KB of MXFP4 blocks per group
 constexpr int kGroupSc = 8 * 16 * 8;      // 1 KB of scale bytes per group
-constexpr int kRingBytes = kStages * (kASlot + kBSlot);
+constexpr int kRingBytes = kStages * kBSlot;
 constexpr int kGroupOff = kRingBytes;
 constexpr int kDynSmem = kGroupOff + kGroups * (kGroupPk + kGroupSc) + 1024;  // + alignment slack
 constexpr int kThreads = 15 * 32;
-constexpr int kTmemCols = 2 * kNMax;
+constexpr int kTmemCols = 512;            // accumulators 2 x kNMax, then the weight ring
+constexpr int kAColBase = 2 * kNMax;
+static_assert(kAColBase + kStages * kACols <= kTmemCols, "TMEM budget");
 constexpr long long kWaitCycles = 4000000000ll;  // ~2 s at the B200's clocks
 
 // Warp roles.
@@ -163,14 +170,6 @@ __device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x,
         "l"(map), "r"(x), "r"(y), "r"(saddr(b))
         : "memory");
 }
-// Brings one 2D tile of `map` at (x, y) into L2 (no shared-memory write).
-__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int x, int y) {
-    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(x), "r"(y)
-                 : "memory");
-}
-__device__ __forceinline__ void fence_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 __device__ __forceinline__ void tc_after_sync() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
@@ -182,14 +181,28 @@ __device__ __forceinline__ void tc_commit(uint64_t* b) {
                      saddr(b))
                  : "memory");
 }
-__device__ __forceinline__ void tc_mma(uint32_t tmem, uint64_t ad, uint64_t bd, uint32_t idesc,
-                                       uint32_t accumulate) {
+// The same with A read from tensor memory (128 lanes = rows, two f16 per
+// 32-bit column along K).
+__device__ __forceinline__ void tc_mma_ta(uint32_t tmem, uint32_t a_tmem, uint64_t bd, uint32_t idesc,
+                                          uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
-        "l"(ad), "l"(bd), "r"(idesc), "r"(accumulate)
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem),
+        "r"(a_tmem), "l"(bd), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// 32 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+        "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+        "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // Shared-memory matrix descriptor, K-major.  layout 0 = no swizzle (core
 // matrices of 8 rows x 16 bytes; lbo = distance between the two K-adjacent
 // core matrices of one MMA, sbo = distance between 8-row groups); layout 2 =
@@ -327,6 +340,10 @@ __device__ __forceinline__ bool warp_wait(Shared& sh, uint64_t* b, uint32_t pari
 }
 
 // ---- roles ----------------------------------------------------------------
+//
+// A K-range of an item is walked in stages of up to four 32-column blocks
+// that never straddle an 8-block group: a group of w blocks (w = 8, or the
+// even remainder of the last group) is ceil(w / 4) stages of 4, 4 or 2 blocks.
 
 // Weight producer (one warp, converged): for every item, every 8-block group
 // of its 128-row tile, once the ring slot is free; lane t copies tile t.
@@ -370,16 +387,18 @@ __device__ __forceinline__ void role_weights(Shared& sh, const GroupedArgs& a, c
     }
 }
 
-// Converters: thread c owns weight row m0 + (c & 127) and, of each stage's
-// two 32-column blocks, block (c >> 7).  Lane 0 of each warp does the
-// barrier work for its warp.
+// Converters: thread c owns weight row m0 + (c & 127) — its TMEM lane — and,
+// of each stage's up-to-four blocks, blocks 2h and 2h + 1 (h = c >> 7),
+// which it widens to 64 f16 and stores as 32 TMEM columns.  Lane 0 of each
+// warp does the barrier work for its warp.
 __device__ __forceinline__ void role_convert(Shared& sh, const GroupedArgs& a, char* smem, long long (&gt_acc)[16]) {
     const int c = threadIdx.x;
-    const int r = c & (kM - 1), h = c >> 7, lane = c & 31;
+    const int r = c & (kM - 1), h = c >> 7, lane = c & 31, warp = c >> 5;
     const int lr = r & 15, tile = r >> 4;
-    const int nblk = a.K >> 5, ks = a.K / kKS;
+    const int nblk = a.K >> 5, ngrp = (nblk + 7) >> 3;
     unsigned* status = a.w.status;
     const char* ring = smem + kGroupOff;
+    const uint32_t tlane = (uint32_t)((warp & 3) * 32) << 16;
     auto row_emax = [&](int it) -> int {
         if (it >= sh.nitems) return 127;
         const Item item = decode(sh, it);
@@ -395,114 +414,117 @@ __device__ __forceinline__ void role_convert(Shared& sh, const GroupedArgs& a, c
         const bool valid = item.m0 + r < a.M;
         const int emax = emax_next;
         emax_next = row_emax(it + gridDim.x);  // lands while this item runs
-        for (int s = 0; s < ks; ++s, ++g) {
-            [[maybe_unused]] const bool lead = c == 0;
-            const int sub = s & 3, w = min(8, nblk - 8 * (s >> 2));
-            const bool group_end = 2 * sub + 2 == w;
+        for (int grp = 0; ok && grp < ngrp; ++grp, ++gq) {
+            const int w = min(8, nblk - 8 * grp);
             const int gslot = gq % kGroups;
-            bool ok_w = true;
+            [[maybe_unused]] const bool lead = c == 0;
             GT_START(t0);
-            if (sub == 0) ok_w = warp_wait(sh, &sh.gfull[gslot], (gq / kGroups) & 1, status, 2u);
+            if (!warp_wait(sh, &sh.gfull[gslot], (gq / kGroups) & 1, status, 2u)) { ok = false; break; }
             GT_ADD(1, t0, lead);
-            GT_START(t1);
-            uint4 out[4];
+            const char* gb = ring + gslot * (kGroupPk + kGroupSc);
+            for (int sub = 0; sub * 4 < w; ++sub, ++g) {
+                const int kb = min(4, w - 4 * sub);  // blocks in this stage (4 or 2)
+                const bool mine = 2 * h < kb;        // this thread's two blocks exist
+                const int bl = 4 * sub + 2 * h;      // its first block within the group
+                GT_START(t1);
+                uint32_t v[32];
 #ifdef GW_TRACE_SKIP_CONVERT
-            if (false) {
+                if (false) {
 #else
-            if (ok_w && valid) {
+                if (valid && mine) {
 #endif
-                const char* gb = ring + gslot * (kGroupPk + kGroupSc);
-                const int bl = 2 * sub + h;
-                const uint4 q = *reinterpret_cast<const uint4*>(gb + tile * kTileRun + (lr * w + bl) * 16);
-                const uint32_t sb = *reinterpret_cast<const uint8_t*>(gb + kGroupPk + tile * 128 + lr * w + bl);
-                const uint32_t hs = block_scale_h2(sb, emax);
-                const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+                    const uint4* q = reinterpret_cast<const uint4*>(gb + tile * kTileRun + (lr * w + bl) * 16);
+                    const uint8_t* sb = reinterpret_cast<const uint8_t*>(gb + kGroupPk + tile * 128 + lr * w + bl);
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    out[j].x = hmul2_bits(e2m1x2(wd[j] & 0xFF), hs);
-                    out[j].y = hmul2_bits(e2m1x2((wd[j] >> 8) & 0xFF), hs);
-                    out[j].z = hmul2_bits(e2m1x2((wd[j] >> 16) & 0xFF), hs);
-                    out[j].w = hmul2_bits(e2m1x2(wd[j] >> 24), hs);
+                    for (int b2 = 0; b2 < 2; ++b2) {
+                        const uint4 qq = q[b2];
+                        const uint32_t hs = block_scale_h2(sb[b2], emax);
+                        const uint32_t wd[4] = {qq.x, qq.y, qq.z, qq.w};
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            v[16 * b2 + 4 * j + 0] = hmul2_bits(e2m1x2(wd[j] & 0xFF), hs);
+                            v[16 * b2 + 4 * j + 1] = hmul2_bits(e2m1x2((wd[j] >> 8) & 0xFF), hs);
+                            v[16 * b2 + 4 * j + 2] = hmul2_bits(e2m1x2((wd[j] >> 16) & 0xFF), hs);
+                            v[16 * b2 + 4 * j + 3] = hmul2_bits(e2m1x2(wd[j] >> 24), hs);
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = 0;
                 }
-            }
-            GT_ADD(2, t1, lead);
-            const int slot = g % kStages;
-            GT_START(t2);
-            if (ok_w) ok_w = warp_wait(sh, &sh.empty[slot], ((g / kStages) & 1) ^ 1, status, 4u);
-            GT_ADD(3, t2, lead);
-#ifdef GW_TRACE_SKIP_CONVERT
-            if (false) {
-#else
-            if (ok_w && valid) {
-#endif
-                char* A = smem + slot * (kASlot + kBSlot) + (r >> 3) * 1024 + (r & 7) * 16 + h * 512;
-#pragma unroll
-                for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(A + j * 128) = out[j];
-                fence_async_smem();
-            }
-            if (!ok_w) { ok = false; break; }
-            __syncwarp();
+                if (4 * sub + 4 >= w) {  // the group's last stage has been read: free its slot
+                    __syncwarp();
+                    if (lane == 0) bar_arrive(&sh.gempty[gslot]);
+                }
+                GT_ADD(2, t1, lead);
+                const int slot = g % kStages;
+                GT_START(t2);
+                if (!warp_wait(sh, &sh.empty[slot], ((g / kStages) & 1) ^ 1, status, 4u)) { ok = false; break; }
+                GT_ADD(3, t2, lead);
+                // the warp's 32 rows, columns [32h, 32h + 32) of the stage's weight slot
+                if (2 * h < kb) {  // uniform over the warp
+                    tmem_st32(sh.tmem + tlane + kAColBase + slot * kACols + 32 * h, v);
+                    tmem_st_wait();
+                }
+                tc_before_sync();
+                __syncwarp();
 #ifdef GW_GROUPED_TRACE
-            if (c == 224) *(volatile long long*)&sh.conv_arrived[slot] = clock64();  // last converter warp
+                if (c == 224) *(volatile long long*)&sh.conv_arrived[slot] = clock64();  // last converter warp
 #endif
-            if (lane == 0) {
-                bar_arrive(&sh.full[slot]);
-                if (group_end) bar_arrive(&sh.gempty[gslot]);  // its group bytes have been read
+                if (lane == 0) bar_arrive(&sh.full[slot]);
+                GT_COUNT(13, lead);
             }
-            if (group_end) ++gq;
-            GT_COUNT(13, lead);
         }
     }
 }
 
-// Token producer (one warp, converged; lane 0 issues): the chunk's rows are consecutive in the
-// expert-ordered token matrix, so each stage is one 2D TMA of 128 rows x 64
-// columns (rows past the chunk belong to the next expert and only fill
-// columns the epilogue ignores; rows past the matrix read as zero).
+// Token producer (one warp, converged; lane 0 issues): the chunk's rows are
+// consecutive in the expert-ordered token matrix, so each stage is one or two
+// 2D TMAs of 128 rows x 64 columns (rows past the chunk belong to the next
+// expert and only fill columns the epilogue ignores; rows past the matrix
+// read as zero).
 __device__ __forceinline__ void role_tokens(Shared& sh, const GroupedArgs& a, char* smem,
                                             const CUtensorMap* map, long long (&gt_acc)[16]) {
-    const int ks = a.K / kKS;
+    const int nblk = a.K >> 5, ngrp = (nblk + 7) >> 3;
     const int lane = threadIdx.x & 31;
     unsigned* status = a.w.status;
-    constexpr int kAhead = 8;  // stages between a tile's L2 prefetch and its load
     int g = 0;
     for (int it = blockIdx.x; it < sh.nitems; it += gridDim.x) {
         const Item item = decode(sh, it);
-        const int nit = it + gridDim.x;
-        const int g0_next = nit < sh.nitems ? decode(sh, nit).g0 : -1;
-        if (it == (int)blockIdx.x && lane == 0)
-            for (int s = 0; s < kAhead && s < ks; ++s) tma_prefetch_2d(map, s * kKS, item.g0);
-        for (int s = 0; s < ks; ++s, ++g) {
-            const int slot = g % kStages;
-            if (lane == 0) {  // the tile kAhead stages on, possibly in the next item
-                const int sp = s + kAhead;
-                if (sp < ks) tma_prefetch_2d(map, sp * kKS, item.g0);
-                else if (g0_next >= 0 && sp - ks < ks) tma_prefetch_2d(map, (sp - ks) * kKS, g0_next);
-            }
-            GT_START(t0);
-            if (!warp_wait(sh, &sh.empty[slot], ((g / kStages) & 1) ^ 1, status, 8u)) return;
-            GT_ADD(4, t0, lane == 0);
-            if (lane == 0) {
-                char* B = smem + slot * (kASlot + kBSlot) + kASlot;
+        for (int grp = 0; grp < ngrp; ++grp) {
+            const int w = min(8, nblk - 8 * grp);
+            for (int sub = 0; sub * 4 < w; ++sub, ++g) {
+                const int kb = min(4, w - 4 * sub);
+                const int slot = g % kStages;
+                GT_START(t0);
+                if (!warp_wait(sh, &sh.empty[slot], ((g / kStages) & 1) ^ 1, status, 8u)) return;
+                GT_ADD(4, t0, lane == 0);
+                if (lane == 0) {
+                    char* B = smem + slot * kBSlot;
+                    const int x0 = (8 * grp + 4 * sub) * 32;
 #ifdef GW_TRACE_SKIP_TOKENS
-                bar_arrive(&sh.full[slot]);
-                (void)B; (void)map;
+                    bar_arrive(&sh.full[slot]);
+                    (void)B; (void)map; (void)x0; (void)kb;
 #else
-                bar_arrive_tx(&sh.full[slot], kBSlot);
-                tma_2d(B, map, s * kKS, item.g0, &sh.full[slot]);
+                    bar_arrive_tx(&sh.full[slot], (uint32_t)(kb / 2) * kBBox);
+                    for (int cb = 0; cb < kb / 2; ++cb)
+                        tma_2d(B + cb * kBBox, map, x0 + cb * kBox, item.g0, &sh.full[slot]);
 #endif
 #ifdef GW_GROUPED_TRACE
-                *(volatile long long*)&sh.tok_issued[slot] = clock64();
+                    *(volatile long long*)&sh.tok_issued[slot] = clock64();
 #endif
+                }
+                __syncwarp();
             }
-            __syncwarp();
         }
     }
 }
 
-// MMA issuer: one warp, converged; lane 0 issues.
+// MMA issuer: one warp, converged; lane 0 issues.  A stage of kb blocks is
+// 2 kb MMAs of K = 16: A from the stage's TMEM columns, B from its shared
+// slot (box cb = k / 4, 32 bytes per K step inside the swizzled row).
 __device__ __forceinline__ void role_mma(Shared& sh, const GroupedArgs& a, char* smem, long long (&gt_acc)[16]) {
-    const int ks = a.K / kKS;
+    const int nblk = a.K >> 5, ngrp = (nblk + 7) >> 3;
     const int lane = threadIdx.x & 31;
     unsigned* status = a.w.status;
     const uint32_t base = saddr(smem);
@@ -517,37 +539,44 @@ __device__ __forceinline__ void role_mma(Shared& sh, const GroupedArgs& a, char*
         if (!warp_wait(sh, &sh.tempty[b], ((il >> 1) & 1) ^ 1, status, 16u)) break;
         GT_ADD(7, t0, lane == 0);
         tc_after_sync();
-        const uint32_t tmem = sh.tmem + b * kNMax;
-        for (int s = 0; s < ks; ++s, ++g) {
-            const int slot = g % kStages;
-            GT_START(t1);
-            if (!warp_wait(sh, &sh.full[slot], (g / kStages) & 1, status, 32u)) { ok = false; break; }
-            GT_ADD(6, t1, lane == 0);
+        const uint32_t dtm = sh.tmem + b * kNMax;
+        bool first = true;
+        for (int grp = 0; ok && grp < ngrp; ++grp) {
+            const int w = min(8, nblk - 8 * grp);
+            for (int sub = 0; sub * 4 < w; ++sub, ++g) {
+                const int kb = min(4, w - 4 * sub);
+                const int slot = g % kStages;
+                GT_START(t1);
+                if (!warp_wait(sh, &sh.full[slot], (g / kStages) & 1, status, 32u)) { ok = false; break; }
+                GT_ADD(6, t1, lane == 0);
 #ifdef GW_GROUPED_TRACE
-            {
-                const long long now = clock64();
-                if (lane == 0) {
-                    gt_acc[5] += now - *(volatile long long*)&sh.tok_issued[slot];
-                    gt_acc[15] += now - *(volatile long long*)&sh.conv_arrived[slot];
+                {
+                    const long long now = clock64();
+                    if (lane == 0) {
+                        gt_acc[5] += now - *(volatile long long*)&sh.tok_issued[slot];
+                        gt_acc[15] += now - *(volatile long long*)&sh.conv_arrived[slot];
+                    }
                 }
-            }
 #endif
-            GT_START(t2);
-            tc_after_sync();
-            const uint32_t A = base + slot * (kASlot + kBSlot), B = A + kASlot;
-            if (lane == 0) {
-#pragma unroll
-                for (int k = 0; k < kKS / 16; ++k)
+                GT_START(t2);
+                tc_after_sync();
+                if (lane == 0) {
+                    const uint32_t atm = sh.tmem + kAColBase + slot * kACols;
+                    const uint32_t B = base + slot * kBSlot;
+                    for (int k = 0; k < 2 * kb; ++k) {
 #ifndef GW_TRACE_SKIP_MMA
-                    tc_mma(tmem, smem_desc(A + k * 256, 128, 1024, 0), smem_desc(B + k * 32, 16, 1024, 2),
-                           idesc, (s | k) != 0);
+                        tc_mma_ta(dtm, atm + k * 8, smem_desc(B + (k >> 2) * kBBox + (k & 3) * 32, 16, 1024, 2),
+                                  idesc, first ? 0u : 1u);
 #else
-                    (void)idesc;
+                        (void)idesc; (void)atm; (void)B;
 #endif
-                tc_commit(&sh.empty[slot]);
+                        first = false;
+                    }
+                    tc_commit(&sh.empty[slot]);
+                }
+                __syncwarp();
+                GT_ADD(8, t2, lane == 0);
             }
-            __syncwarp();
-            GT_ADD(8, t2, lane == 0);
         }
         if (!ok) break;
         if (lane == 0) tc_commit(&sh.tfull[b]);
@@ -804,9 +833,10 @@ int configure_grouped() {
 }
 
 bool grouped_supported(const MoeDims& d, const MoeWork& w) {
-    // 64-column stages in 8-block groups; rows of both matrices are multiples
-    // of 16 (bank creation requires multiples of 32 for H and F)
-    return w.status != nullptr && d.H % kKS == 0 && d.F % kKS == 0 && tensor_map_encoder() != nullptr;
+    // an even number of 32-column blocks per row (stages of 4 or 2 blocks);
+    // rows of both matrices are multiples of 16 (bank creation requires
+    // multiples of 32 for H and F)
+    return w.status != nullptr && d.H % 64 == 0 && d.F % 64 == 0 && tensor_map_encoder() != nullptr;
 }
 
 int launch_grouped(const LayerView& L, const MoeDims& d, const MoeWork& w, int which, int sms,
@@ -831,11 +861,11 @@ int launch_grouped(const LayerView& L, const MoeDims& d, const MoeWork& w, int w
         a.mode = 2;
     }
     // expert-ordered token rows: [brows][K] f16, loaded 64 columns x 128 rows
-    // at a time into 128-byte-swizzled shared rows
+    // per box into 128-byte-swizzled shared rows
     CUtensorMap map;
     const cuuint64_t gdim[2] = {(cuuint64_t)a.K, (cuuint64_t)brows};
     const cuuint64_t gstride[1] = {(cuuint64_t)a.K * 2};
-    const cuuint32_t box[2] = {kKS, kNMax}, estride[2] = {1, 1};
+    const cuuint32_t box[2] = {kBox, kNMax}, estride[2] = {1, 1};
     auto enc = tensor_map_encoder();
     if (!enc || enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(bsrc), gdim, gstride, box,
                     estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
