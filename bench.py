@@ -15,7 +15,10 @@ combine -> residual.  At N > 1 the experts are sharded by index
 
 Other workloads (parity/inspection, not the headline): gemv (config 0,
 batched over copies > 4x L2), oss20-decode1 (config 1), oss120-decode1
-(config 2, batch 1), qwen3-decode1 / qwen3-decode32 (config 3).
+(config 2, batch 1), qwen3-decode1 / qwen3-decode32 (config 3),
+oss120-prefill (config 4: one GPT-OSS-120B layer, 2048 tokens, 4x skew on 8
+hot experts; its experts run on the tensor cores, so its roofline line is
+the grouped GEMM's TFLOP/s, with its HBM figures beside it).
 
 `value` is device-timed with inputs resident in HBM; `e2e` times the same
 step through the public C-ABI with the hidden states copied from pinned host
@@ -51,12 +54,16 @@ DEFAULT_WORKLOAD = "oss120-decode64"
 SEED = 0
 
 
-def peaks():
+def peaks(kind: str = "hbm"):
+    """Roofline denominator: measured HBM copy GB/s, or dense bf16 TFLOP/s
+    (burst: the kernels are timed alone)."""
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    key, fallback = ("hbm_gbs", 6650.0) if kind == "hbm" else ("bf16_tflops", 1590.0)
     if os.path.exists(p):
         d = json.load(open(p))
-        return d["hbm_gbs"], "measured"
-    return 6650.0, "fallback"
+        if key in d:
+            return d[key], "measured"
+    return fallback, "fallback"
 
 
 class ClockSampler:
@@ -241,7 +248,8 @@ def run_reference(args, workload):
 def metric_unit(workload):
     if workload == "gemv":
         return "MXFP4 expert GEMV HBM GB/s", "GB/s"
-    return "MoE decode tokens/s (" + WORKLOADS[workload][2] + ")", "tokens/s"
+    kind = "prefill" if "prefill" in workload else "decode"
+    return f"MoE {kind} tokens/s (" + WORKLOADS[workload][2] + ")", "tokens/s"
 
 
 def main():
@@ -338,8 +346,11 @@ def run_decode(args):
     world, rank, local = _dist_setup(args)
     preset, T, desc = WORKLOADS[args.workload]
     spec = PRESETS[preset]
-    if args.workload == "oss120-prefill":
+    prefill = args.workload == "oss120-prefill"
+    if prefill:
         spec = spec.with_(layers=1)
+        # one layer is ~2 ms: time enough steps for the clock sampler to see them
+        args.steps = max(args.steps, 150)
     if args.layers:
         spec = spec.with_(layers=args.layers)
     ctx = Context(local)
@@ -425,6 +436,30 @@ def run_decode(args):
     achieved = alg_bytes / (expert_ms / 1e3) / 1e9 if expert_ms > 0 else None
     peak, peak_kind = peaks()
     step_bytes_total = _max_over_ranks(alg_bytes / prof_steps, 1)
+    # prefill runs its experts on the tensor cores (k_grouped): FLOPs of the
+    # slots this rank computed, 2 * (2F*H + H*F) each
+    slots = T * spec.top_k / world
+    flops = 2.0 * slots * (2 * spec.intermediate * spec.hidden + spec.hidden * spec.intermediate)
+    tpeak, tpeak_kind = peaks("tensor")
+    if prefill:
+        roofline = {"bound": "tensor", "kernel": "k_grouped (tcgen05 kind::f16 grouped expert GEMM, "
+                    "gate_up + down)", "achieved": flops / (expert_ms / prof_steps / 1e3) / 1e12,
+                    "peak": tpeak, "unit": "TFLOP/s", "peak_kind": tpeak_kind, "traffic": None,
+                    "flops_per_step": flops,
+                    "hbm_achieved_gbs": achieved, "hbm_peak_gbs": peak,
+                    "hbm_frac": (achieved / peak) if achieved else None}
+        roofline["frac"] = roofline["achieved"] / tpeak
+    else:
+        roofline = {"bound": "hbm", "kernel": "k_gateup + k_down (expert MXFP4 GEMVs)",
+                    "achieved": achieved, "peak": peak, "unit": "GB/s",
+                    "frac": (achieved / peak) if achieved else None,
+                    "peak_kind": peak_kind, "traffic": None}
+    roofline.update({"alg_bytes_per_step": step_bytes_total,
+                     "expert_passes_per_step": prof["expert_passes"] / prof_steps,
+                     "expert_ms_per_step": expert_ms / prof_steps,
+                     "launches_timed": launches_prof,
+                     "kernel_ms_per_step": {k: round(prof[k + "_ms"] / prof_steps, 4)
+                                            for k in ("router", "gateup", "down", "combine")}})
 
     if rank == 0:
         value = T / (ms / 1e3)
@@ -446,16 +481,7 @@ def run_decode(args):
             "e2e": {"value": T / (e2e_ms / 1e3), "unit": unit, "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 4},
             "gpu_launches": launches,
-            "roofline": {"bound": "hbm", "kernel": "k_gateup + k_down (expert MXFP4 GEMVs)",
-                         "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": (achieved / peak) if achieved else None,
-                         "peak_kind": peak_kind, "traffic": None,
-                         "alg_bytes_per_step": step_bytes_total,
-                         "expert_passes_per_step": prof["expert_passes"] / prof_steps,
-                         "expert_ms_per_step": expert_ms / prof_steps,
-                         "launches_timed": launches_prof,
-                         "kernel_ms_per_step": {k: round(prof[k + "_ms"] / prof_steps, 4)
-                                                for k in ("router", "gateup", "down", "combine")}},
+            "roofline": roofline,
             "clocks": clocks,
         }
         if not args.no_cpu_baseline and world == 1:
