@@ -239,6 +239,114 @@ __global__ void k_xprep(const void* __restrict__ x, int64_t x_stride, int x_dtyp
         prep_block(xm, x_dtype, cols, 0, blk, shift, x16 + (size_t)m * cols);
 }
 
+// k_router_mma: the router for large bf16 batches.  grid ceil(T/16), 4 warps.
+// A CTA owns 16 tokens outright: their row maxima (the x16 shift), the
+// logits of all E experts (E a multiple of 32, <= 256) as a small GEMM on
+// mma.sync.m16n8k16 bf16 (exact products, fp32 sums; warp w takes experts
+// [w E/4, (w+1) E/4)), their x16 rows, and their top-k + grouping — so no
+// cross-CTA completion counting is needed and each x row is read by one CTA
+// instead of E/4.  Same results as k_router up to fp32 summation order
+// (Router.logits, Runtime/Router.swift:38-66; Router.select :78-98).
+__global__ void __launch_bounds__(128) k_router_mma(LayerView L, MoeDims d, const uint16_t* __restrict__ x,
+                                                    int T, MoeWork w) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, tq = lane & 3;
+    const int t0 = blockIdx.x * 16;
+    const int H = d.H, E = d.E;
+    __shared__ int shift[16];
+    __shared__ int ord[4][kMaxExperts];
+    // row maxima of the CTA's tokens: warp w takes tokens 4w .. 4w+3
+    for (int q = 0; q < 4; ++q) {
+        const int t = t0 + warp * 4 + q;
+        float m = 0.f;
+        if (t < T) {
+            const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)t * H);
+            for (int c = lane; c < (H >> 3); c += 32) {
+                const uint4 v = __ldg(xr + c);
+                const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    m = fmaxf(m, fmaxf(fabsf(__uint_as_float(u[j] << 16)),
+                                       fabsf(__uint_as_float(u[j] & 0xffff0000u))));
+            }
+        }
+        m = warp_max(m);
+        if (lane == 0) {
+            const int p = t < T ? row_exponent_shift(m) : 0;
+            shift[warp * 4 + q] = p;
+            if (t < T) w.xmul[t] = pow2f(-p);
+        }
+    }
+    // logits
+    const int per = E >> 2, ntile = per >> 3;  // experts per warp, n-tiles of 8
+    float c[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) c[n][0] = c[n][1] = c[n][2] = c[n][3] = 0.f;
+    const int ra = min(t0 + g, T - 1), rb = min(t0 + g + 8, T - 1);  // rows past T reuse a valid row
+    const uint32_t* xa = reinterpret_cast<const uint32_t*>(x + (int64_t)ra * H);
+    const uint32_t* xb = reinterpret_cast<const uint32_t*>(x + (int64_t)rb * H);
+    const uint32_t* wbase = reinterpret_cast<const uint32_t*>(L.router_w) + (int64_t)(warp * per + g) * (H >> 1);
+#pragma unroll 4
+    for (int k0 = 0; k0 < H; k0 += 16) {
+        const int kk = (k0 >> 1) + tq;  // u32 holding columns k0 + 2 tq, + 1
+        const uint32_t a0 = __ldg(xa + kk), a1 = __ldg(xb + kk), a2 = __ldg(xa + kk + 4), a3 = __ldg(xb + kk + 4);
+#pragma unroll
+        for (int n = 0; n < 8; ++n) {
+            if (n < ntile) {
+                const uint32_t* wr = wbase + (int64_t)n * 8 * (H >> 1);
+                const uint32_t b0 = __ldg(wr + kk), b1 = __ldg(wr + kk + 4);
+                asm volatile(
+                    "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+                    "{%8,%9}, {%0,%1,%2,%3};"
+                    : "+f"(c[n][0]), "+f"(c[n][1]), "+f"(c[n][2]), "+f"(c[n][3])
+                    : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+            }
+        }
+    }
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+        if (n >= ntile) break;
+        const int e0 = warp * per + n * 8 + 2 * tq;
+        const float bias0 = L.router_b ? bf16_bits_to_f32(L.router_b[e0]) : 0.f;
+        const float bias1 = L.router_b ? bf16_bits_to_f32(L.router_b[e0 + 1]) : 0.f;
+        if (t0 + g < T) {
+            w.logits[(int64_t)(t0 + g) * E + e0] = c[n][0] + bias0;
+            w.logits[(int64_t)(t0 + g) * E + e0 + 1] = c[n][1] + bias1;
+        }
+        if (t0 + g + 8 < T) {
+            w.logits[(int64_t)(t0 + g + 8) * E + e0] = c[n][2] + bias0;
+            w.logits[(int64_t)(t0 + g + 8) * E + e0 + 1] = c[n][3] + bias1;
+        }
+    }
+    __syncthreads();
+    // the tokens' f16 rows (x * 2^shift, exact), eight values per thread and step
+    const int n8 = H >> 3;
+#pragma unroll 4
+    for (int i = threadIdx.x; i < 16 * n8; i += blockDim.x) {
+        const int q = i / n8, c8 = i - q * n8, t = t0 + q;
+        if (t >= T) continue;
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(x + (int64_t)t * H) + c8);
+        const float m = pow2f(shift[q]);
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const __half2 h = __floats2half2_rn(__uint_as_float(u[j] << 16) * m,
+                                                __uint_as_float(u[j] & 0xffff0000u) * m);
+            o[j] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        reinterpret_cast<uint4*>(w.x16 + (int64_t)t * H)[c8] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    // their top-k and grouping
+    for (int q = warp; q < 16; q += 4) {
+        const int t = t0 + q;
+        if (t >= T) break;
+        select_topk_warp(w.logits + (int64_t)t * E, E, d.k, ord[warp], w.experts + (int64_t)t * d.k,
+                         w.weights + (int64_t)t * d.k);
+        if (lane < d.k) group_slot(d, w, __ldcg(w.experts + (int64_t)t * d.k + lane), t * d.k + lane);
+    }
+}
+
 // k_group: one CTA; a caller-supplied routing [T][k] (copied into the
 // workspace) is grouped by expert.  Expert ids outside [0, E) are skipped.
 __global__ void __launch_bounds__(256) k_group(MoeDims d, const int32_t* __restrict__ experts_in,
@@ -614,6 +722,10 @@ int configure_kernels() {
 
 int launch_router(const LayerView& L, const MoeDims& d, const void* x, int x_dtype, int T,
                   const MoeWork& w, cudaStream_t s) {
+    if (x_dtype == kBF16 && T >= kRouterMmaMinTokens && d.E % 32 == 0 && d.E <= kMaxExperts) {
+        k_router_mma<<<(T + 15) / 16, 128, 0, s>>>(L, d, static_cast<const uint16_t*>(x), T, w);
+        return ok_or_fail();
+    }
     dim3 grid((d.E + 3) / 4, (T + kTokTile - 1) / kTokTile);
     k_router<<<grid, 128, 0, s>>>(L, d, x, x_dtype, T, w);
     return ok_or_fail();

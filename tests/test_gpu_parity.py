@@ -153,6 +153,35 @@ def test_router_matches_oracle(ctx, oss_bank, T, dtype):
     check_topk(ex, ref_ex, ref, spec.top_k)
 
 
+@pytest.mark.parametrize("E,T", [(32, 128), (128, 300), (128, 2048)])
+def test_batch_router_matches_oracle(ctx, E, T):
+    """Large bf16 batches take the tensor-core router (k_router_mma): same
+    logits up to summation order, same top-k (near-ties excepted), same x16."""
+    spec = GPT_OSS_20B.with_(experts=E, layers=1)
+    bank = ExpertBank(ctx, spec, layers=1)
+    try:
+        rng = np.random.default_rng(E + T)
+        w, b = synth.make_router(spec, rng)
+        bank.upload_router(0, w, b)
+        xb = synth.make_hidden(rng, T, spec.hidden, "bf16")
+        x = synth.as_f32(xb, "bf16")
+        r = Router(ctx, bank)
+        lg = r.logits(xb, 0, "bf16")
+        ref = np.stack([O.router_logits(w, b, x[t]) for t in range(T)])
+        assert np.all(np.abs(lg - ref) <= 1e-4 * (1 + np.abs(ref)))
+        ex, wt = r.route_batch(xb, 0, "bf16")
+        ref_ex = np.zeros_like(ex)
+        for t in range(T):
+            e, ww = O.router_select(ref[t], spec.top_k)
+            ref_ex[t] = e
+            if list(ex[t]) == list(e):
+                assert np.allclose(wt[t], ww, rtol=1e-5, atol=1e-6)
+        check_topk(ex, ref_ex, ref, spec.top_k)
+        assert np.mean(np.all(ex == ref_ex, axis=1)) > 0.99
+    finally:
+        bank.close()
+
+
 def test_router_tie_rule_on_device(ctx):
     # Router weights that give exact logit ties: experts 0 and 1 tie at 1.0,
     # expert 2 wins with 5.0 — Router.select returns [2, 1], not [2, 0].
