@@ -77,6 +77,7 @@ struct gw_ctx {
     gw::MoeWork w{};
     int sms = 148;          // persistent grid of the tensor-core expert kernels
     int mma_min_avg = 8;    // tensor-core expert path when T*k >= mma_min_avg * E
+    bool streamed = false;  // decode GEMVs with bulk-copied weights (k_stream) vs per-thread loads
     int64_t launches = 0;
     // profiling (gw_profile_enable): event pairs per timed launch
     bool prof = false;
@@ -288,13 +289,17 @@ gw_status moe_layer_device(gw_ctx* c, gw_bank* b, int layer, const void* x_dev, 
     // Many tokens per expert: the tensor-core grouped GEMMs; few: the GEMV tiles.
     const bool mma = w.mma_min_avg > 0 && (int64_t)T * d.k >= (int64_t)w.mma_min_avg * d.E &&
                      gw::grouped_supported(d, w);
+    const bool streamed = !mma && c->streamed && gw::stream_supported(d, w);
     if ((st = timed_launch(c, 0, 0, [&] {
-             return mma ? gw::launch_grouped(L, d, w, 0, c->sms, c->cur)
-                        : gw::launch_gateup(L, d, x_dev, x_dtype, T, w, c->cur);
+             return mma        ? gw::launch_grouped(L, d, w, 0, c->sms, c->cur)
+                    : streamed ? gw::launch_stream(L, d, w, 0, c->sms, c->cur)
+                               : gw::launch_gateup(L, d, x_dev, x_dtype, T, w, c->cur);
          })))
         return st;
     if ((st = timed_launch(c, 1, 0, [&] {
-             return mma ? gw::launch_grouped(L, d, w, 1, c->sms, c->cur) : gw::launch_down(L, d, T, w, c->cur);
+             return mma        ? gw::launch_grouped(L, d, w, 1, c->sms, c->cur)
+                    : streamed ? gw::launch_stream(L, d, w, 1, c->sms, c->cur)
+                               : gw::launch_down(L, d, T, w, c->cur);
          })))
         return st;
     if (c->prof && (st = log_nactive(c))) return st;
@@ -353,7 +358,8 @@ gw_status gw_init(int32_t device, gw_ctx** out) {
     if (prop.major != 10)
         return fail(GW_E_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a",
                     device, prop.major, prop.minor);
-    if (gw::configure_kernels() != 0 || gw::configure_grouped() != 0)
+    if (gw::configure_kernels() != 0 || gw::configure_grouped() != 0 ||
+        gw::configure_stream(gw::kStreamMaxCols) != 0)
         return cuda_fail(cudaGetLastError(), "kernel attributes");
     gw_ctx* c = new gw_ctx();
     c->device = device;
@@ -406,6 +412,17 @@ gw_status gw_sync(gw_ctx* c) {
             GW_CUDA(cudaMemset(c->w.status, 0, 4));
             return fail(GW_E_CUDA, "tensor-core expert kernel gave up waiting (status bits 0x%x)", bits);
         }
+    }
+    return GW_OK;
+}
+
+gw_status gw_set_decode_streaming(gw_ctx* c, int32_t enable) {
+    if (!c) return fail(GW_E_ARG, "null context");
+    CtxLock lk(c);
+    c->streamed = enable != 0;
+    if (c->graph.exec) {  // a captured stack forward baked the old choice in
+        cudaGraphExecDestroy(c->graph.exec);
+        c->graph = gw_ctx::StackGraph{};
     }
     return GW_OK;
 }

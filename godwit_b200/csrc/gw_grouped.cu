@@ -51,6 +51,7 @@
 
 #include <mutex>
 
+#include "gw_async.cuh"
 #include "gw_device.cuh"
 #include "gw_internal.h"
 
@@ -76,7 +77,6 @@ constexpr int kThreads = 15 * 32;
 constexpr int kTmemCols = 512;            // accumulators 2 x kNMax, then the weight ring
 constexpr int kAColBase = 2 * kNMax;
 static_assert(kAColBase + kStages * kACols <= kTmemCols, "TMEM budget");
-constexpr long long kWaitCycles = 4000000000ll;  // ~2 s at the B200's clocks
 
 // Warp roles.
 constexpr int kConvWarps = 8, kEpiWarp0 = 8, kWeightWarp = 12, kTokenWarp = 13, kMmaWarp = 14;
@@ -119,49 +119,7 @@ struct GroupedArgs {
     int mode;                 // 0 gate_up clamped GLU, 1 gate_up SiLU, 2 down
 };
 
-// ---- PTX wrappers ---------------------------------------------------------
-__device__ __forceinline__ uint32_t saddr(const void* p) {
-    return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ void bar_init(uint64_t* b, uint32_t n) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(b)), "r"(n) : "memory");
-}
-// True once the phase with `parity` has completed.
-__device__ __forceinline__ bool bar_try(uint64_t* b, uint32_t parity) {
-    uint32_t ok;
-#ifdef GW_TRACE_SPIN_WAIT
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(saddr(b)), "r"(parity)
-        : "memory");
-#else
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(saddr(b)), "r"(parity)
-        : "memory");
-#endif
-    return ok != 0;
-}
-__device__ __forceinline__ void bar_arrive(uint64_t* b) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(b)) : "memory");
-}
-__device__ __forceinline__ void bar_arrive_tx(uint64_t* b, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(b)), "r"(bytes)
-                 : "memory");
-}
-// Contiguous global -> shared copy of `bytes` (multiple of 16, both ends
-// 16-byte aligned), counted on `b` as it lands.
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* b) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            saddr(dst)),
-        "l"(src), "r"(bytes), "r"(saddr(b))
-        : "memory");
-}
+// ---- PTX wrappers (the mbarrier / bulk-copy ones are in gw_async.cuh) ------
 // One 2D tile of `map` at (x, y) -> shared, counted on `b`.
 __device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* b) {
     asm volatile(
@@ -222,21 +180,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// All threads of one role group (the 128 epilogue threads) agree on a flag.
-__device__ __forceinline__ bool group_any(bool v, int id, int n) {
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, %2, %3, p;\n\t"
-        "selp.u32 %0, 1, 0, q;\n\t}"
-        : "=r"(r)
-        : "r"((uint32_t)v), "r"(id), "r"(n)
-        : "memory");
-    return r != 0;
-}
-__device__ __forceinline__ void group_sync(int id, int n) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
 // e2m1 pair (one packed byte) -> f16x2, low nibble in the low half.
@@ -309,36 +252,6 @@ __device__ __forceinline__ Item decode(const Shared& sh, int it) {
     return r;
 }
 
-// Bounded wait; false when the CTA is winding down (this wait ran out, or
-// another role's did).
-__device__ __noinline__ bool wait_slow(Shared& sh, uint64_t* b, uint32_t parity, unsigned* status,
-                                       unsigned bit) {
-    const long long t0 = clock64();
-    volatile int* ab = &sh.abort;
-    for (uint32_t i = 1;; ++i) {
-        if (bar_try(b, parity)) return true;
-        if ((i & 63) == 0) {
-            if (*ab) return false;
-            if (clock64() - t0 > kWaitCycles) {
-                *ab = 1;
-                if (status) atomicOr(status, bit);
-                return false;
-            }
-        }
-    }
-}
-__device__ __forceinline__ bool wait_on(Shared& sh, uint64_t* b, uint32_t parity, unsigned* status,
-                                        unsigned bit) {
-    return bar_try(b, parity) || wait_slow(sh, b, parity, status, bit);
-}
-// The same, waited for by lane 0 for its whole warp.
-__device__ __forceinline__ bool warp_wait(Shared& sh, uint64_t* b, uint32_t parity, unsigned* status,
-                                          unsigned bit) {
-    bool ok = true;
-    if ((threadIdx.x & 31) == 0) ok = wait_on(sh, b, parity, status, bit);
-    return __shfl_sync(0xffffffffu, ok, 0);
-}
-
 // ---- roles ----------------------------------------------------------------
 //
 // A K-range of an item is walked in stages of up to four 32-column blocks
@@ -364,7 +277,7 @@ __device__ __forceinline__ void role_weights(Shared& sh, const GroupedArgs& a, c
         for (int grp = 0; grp < ngrp; ++grp, ++gq) {
             const int slot = gq % kGroups;
             GT_START(t0);
-            if (!warp_wait(sh, &sh.gempty[slot], ((gq / kGroups) & 1) ^ 1, status, 1u)) return;
+            if (!warp_wait(&sh.abort, &sh.gempty[slot], ((gq / kGroups) & 1) ^ 1, status, 1u)) return;
             GT_ADD(0, t0, lane == 0);
             const int w = min(8, nblk - 8 * grp);
             const uint32_t run = 16 * w * 16, srun = 16 * w;  // bytes per tile: blocks, scales
@@ -419,7 +332,7 @@ __device__ __forceinline__ void role_convert(Shared& sh, const GroupedArgs& a, c
             const int gslot = gq % kGroups;
             [[maybe_unused]] const bool lead = c == 0;
             GT_START(t0);
-            if (!warp_wait(sh, &sh.gfull[gslot], (gq / kGroups) & 1, status, 2u)) { ok = false; break; }
+            if (!warp_wait(&sh.abort, &sh.gfull[gslot], (gq / kGroups) & 1, status, 2u)) { ok = false; break; }
             GT_ADD(1, t0, lead);
             const char* gb = ring + gslot * (kGroupPk + kGroupSc);
             for (int sub = 0; sub * 4 < w; ++sub, ++g) {
@@ -459,7 +372,7 @@ __device__ __forceinline__ void role_convert(Shared& sh, const GroupedArgs& a, c
                 GT_ADD(2, t1, lead);
                 const int slot = g % kStages;
                 GT_START(t2);
-                if (!warp_wait(sh, &sh.empty[slot], ((g / kStages) & 1) ^ 1, status, 4u)) { ok = false; break; }
+                if (!warp_wait(&sh.abort, &sh.empty[slot], ((g / kStages) & 1) ^ 1, status, 4u)) { ok = false; break; }
                 GT_ADD(3, t2, lead);
                 // the warp's 32 rows, columns [32h, 32h + 32) of the stage's weight slot
                 if (2 * h < kb) {  // uniform over the warp
@@ -497,7 +410,7 @@ __device__ __forceinline__ void role_tokens(Shared& sh, const GroupedArgs& a, ch
                 const int kb = min(4, w - 4 * sub);
                 const int slot = g % kStages;
                 GT_START(t0);
-                if (!warp_wait(sh, &sh.empty[slot], ((g / kStages) & 1) ^ 1, status, 8u)) return;
+                if (!warp_wait(&sh.abort, &sh.empty[slot], ((g / kStages) & 1) ^ 1, status, 8u)) return;
                 GT_ADD(4, t0, lane == 0);
                 if (lane == 0) {
                     char* B = smem + slot * kBSlot;
@@ -536,7 +449,7 @@ __device__ __forceinline__ void role_mma(Shared& sh, const GroupedArgs& a, char*
         const uint32_t idesc = (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kM >> 4) << 24);
         const int b = il & 1;
         GT_START(t0);
-        if (!warp_wait(sh, &sh.tempty[b], ((il >> 1) & 1) ^ 1, status, 16u)) break;
+        if (!warp_wait(&sh.abort, &sh.tempty[b], ((il >> 1) & 1) ^ 1, status, 16u)) break;
         GT_ADD(7, t0, lane == 0);
         tc_after_sync();
         const uint32_t dtm = sh.tmem + b * kNMax;
@@ -547,7 +460,7 @@ __device__ __forceinline__ void role_mma(Shared& sh, const GroupedArgs& a, char*
                 const int kb = min(4, w - 4 * sub);
                 const int slot = g % kStages;
                 GT_START(t1);
-                if (!warp_wait(sh, &sh.full[slot], (g / kStages) & 1, status, 32u)) { ok = false; break; }
+                if (!warp_wait(&sh.abort, &sh.full[slot], (g / kStages) & 1, status, 32u)) { ok = false; break; }
                 GT_ADD(6, t1, lane == 0);
 #ifdef GW_GROUPED_TRACE
                 {
@@ -627,7 +540,7 @@ __device__ __forceinline__ void role_epilogue(Shared& sh, const GroupedArgs& a, 
         const int b = il & 1;
         GT_ADD(11, t0, t == 0);
         GT_START(t1);
-        const bool got = wait_on(sh, &sh.tfull[b], (il >> 1) & 1, status, 128u);
+        const bool got = wait_on(&sh.abort, &sh.tfull[b], (il >> 1) & 1, status, 128u);
         if (group_any(!got, 2, 128)) break;
         GT_ADD(9, t1, t == 0);
         GT_START(t2);

@@ -93,6 +93,13 @@ int launch_grouped(const LayerView& L, const MoeDims& d, const MoeWork& w, int w
                    cudaStream_t s);
 bool grouped_supported(const MoeDims& d, const MoeWork& w);
 int configure_grouped();
+// Decode expert GEMVs with bulk-copied weights (gw_stream.cu): which 0 =
+// gate_up + activation, 1 = down + routing weight; `sms` persistent CTAs.
+constexpr int kStreamMaxCols = 4096;
+int launch_stream(const LayerView& L, const MoeDims& d, const MoeWork& w, int which, int sms,
+                  cudaStream_t s);
+bool stream_supported(const MoeDims& d, const MoeWork& w);
+int configure_stream(int max_cols);
 // Row-exponent table entries of a row-major scale matrix.
 int launch_rowexp(const uint8_t* scales, int rows, int cols, uint8_t* out, cudaStream_t s);
 int configure_kernels();

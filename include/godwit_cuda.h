@@ -125,6 +125,11 @@ GW_API gw_status gw_sync(gw_ctx* ctx);
  * T * top_k >= min_avg * experts, else as the MXFP4 GEMV tiles; 0 = always
  * the GEMV tiles.  Default 8. */
 GW_API gw_status gw_set_tensor_core_min_tokens(gw_ctx* ctx, int32_t min_avg);
+/* Decode-size layers (below the tensor-core threshold): 1 streams the expert
+ * weights with bulk copies into a shared-memory ring consumed by the MXFP4
+ * GEMV tiles (k_stream); 0 (default, currently the faster) runs the same
+ * tiles on per-thread loads.  The results agree to fp32 summation order. */
+GW_API gw_status gw_set_decode_streaming(gw_ctx* ctx, int32_t enable);
 
 /* ---- layout (ExpertLayout.init, Install/InstallLayout.swift:50-92) ------ */
 
