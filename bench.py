@@ -260,6 +260,8 @@ def main():
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prefill-f16", action="store_true",
+                    help="oss120-prefill: exact f16 activations instead of config 4's MXFP8 block-scaled MMAs")
     ap.add_argument("--layers", type=int, default=None,
                     help="profiling only: hold and run this many layers instead of the model's")
     args = ap.parse_args()
@@ -354,6 +356,9 @@ def run_decode(args):
     if args.layers:
         spec = spec.with_(layers=args.layers)
     ctx = Context(local)
+    block_scaled = prefill and not getattr(args, "prefill_f16", False)
+    if block_scaled:
+        ctx.set_block_scaled(True)  # config 4: MXFP4 x MXFP8 tcgen05 block-scaled MMAs
     cur = D.bind_stream(ctx)
     bank = ExpertBank(ctx, spec, shard_rank=rank, shard_count=world)
     t0 = time.time()
@@ -441,9 +446,12 @@ def run_decode(args):
     slots = T * spec.top_k / world
     flops = 2.0 * slots * (2 * spec.intermediate * spec.hidden + spec.hidden * spec.intermediate)
     tpeak, tpeak_kind = peaks("tensor")
+    if block_scaled:  # no measured MXF8F6F4 peak: NVIDIA's dense FP8 figure
+        tpeak, tpeak_kind = 4500.0, "nominal dense fp8/mxf8f6f4 (no measured figure)"
     if prefill:
-        roofline = {"bound": "tensor", "kernel": "k_grouped (tcgen05 kind::f16 grouped expert GEMM, "
-                    "gate_up + down)", "achieved": flops / (expert_ms / prof_steps / 1e3) / 1e12,
+        roofline = {"bound": "tensor", "kernel": "k_grouped (tcgen05 " +
+                    ("kind::mxf8f6f4.block_scale" if block_scaled else "kind::f16") +
+                    " grouped expert GEMM, gate_up + down)", "achieved": flops / (expert_ms / prof_steps / 1e3) / 1e12,
                     "peak": tpeak, "unit": "TFLOP/s", "peak_kind": tpeak_kind, "traffic": None,
                     "flops_per_step": flops,
                     "hbm_achieved_gbs": achieved, "hbm_peak_gbs": peak,
@@ -468,7 +476,8 @@ def run_decode(args):
             "metric": metric, "value": value, "unit": unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "mxfp4 weights x bf16 activations, fp32 accumulate",
+            "dtype": ("mxfp4 weights x mxfp8 (e4m3 + e8m0 per 32) activations, fp32 accumulate"
+                      if block_scaled else "mxfp4 weights x bf16 activations, fp32 accumulate"),
             "data": "synthetic (seeded random-init bank, hidden ~N(0,1))",
             "config": {"workload": args.workload, "description": desc if not args.layers else
                        f"{desc} (profiling run: {spec.layers} layers)", "model_shape": spec.name,

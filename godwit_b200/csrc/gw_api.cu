@@ -78,6 +78,7 @@ struct gw_ctx {
     int sms = 148;          // persistent grid of the tensor-core expert kernels
     int mma_min_avg = 8;    // tensor-core expert path when T*k >= mma_min_avg * E
     bool streamed = false;  // decode GEMVs with bulk-copied weights (k_stream) vs per-thread loads
+    int block_scaled = 0;   // tensor-core path: block-scaled MXFP4 x MXFP8 instead of exact f16
     int64_t launches = 0;
     // profiling (gw_profile_enable): event pairs per timed launch
     bool prof = false;
@@ -173,6 +174,10 @@ gw_status ensure_work(gw_ctx* c, const gw_bank* b, int T) {
     const size_t o_act = take((size_t)tcap * kc * Fc * 2);
     const size_t o_ybuf = take((size_t)tcap * kc * Hc * 4);
     const size_t o_xg = take((size_t)tcap * kc * Hc * 2);
+    const size_t o_xq = take((size_t)tcap * kc * Hc);
+    const size_t o_xsf = take((size_t)tcap * kc * ((Hc + 127) / 128) * 4);
+    const size_t o_aq = take((size_t)tcap * kc * Fc);
+    const size_t o_asf = take((size_t)tcap * kc * ((Fc + 127) / 128) * 4);
     const size_t o_done = take((size_t)(tcap / 8 + 1) * 4);
     const size_t o_status = take(4);
     cudaError_t e = c->work.ensure(off);
@@ -197,9 +202,14 @@ gw_status ensure_work(gw_ctx* c, const gw_bank* b, int T) {
     w.act = reinterpret_cast<__half*>(base + o_act);
     w.ybuf = reinterpret_cast<float*>(base + o_ybuf);
     w.xg = reinterpret_cast<__half*>(base + o_xg);
+    w.xq = reinterpret_cast<uint8_t*>(base + o_xq);
+    w.xsf = reinterpret_cast<uint32_t*>(base + o_xsf);
+    w.aq = reinterpret_cast<uint8_t*>(base + o_aq);
+    w.asf = reinterpret_cast<uint32_t*>(base + o_asf);
     w.done = reinterpret_cast<unsigned*>(base + o_done);
     w.status = reinterpret_cast<unsigned*>(base + o_status);
     w.mma_min_avg = c->mma_min_avg;
+    w.block_scaled = c->block_scaled;
     c->work_tcap = tcap;
     c->work_H = Hc;
     c->work_F = Fc;
@@ -291,7 +301,7 @@ gw_status moe_layer_device(gw_ctx* c, gw_bank* b, int layer, const void* x_dev, 
                      gw::grouped_supported(d, w);
     const bool streamed = !mma && c->streamed && gw::stream_supported(d, w);
     if ((st = timed_launch(c, 0, 0, [&] {
-             return mma        ? gw::launch_grouped(L, d, w, 0, c->sms, c->cur)
+             return mma        ? gw::launch_grouped(L, d, w, 0, c->sms, c->cur, x_dev, x_dtype)
                     : streamed ? gw::launch_stream(L, d, w, 0, c->sms, c->cur)
                                : gw::launch_gateup(L, d, x_dev, x_dtype, T, w, c->cur);
          })))
@@ -412,6 +422,18 @@ gw_status gw_sync(gw_ctx* c) {
             GW_CUDA(cudaMemset(c->w.status, 0, 4));
             return fail(GW_E_CUDA, "tensor-core expert kernel gave up waiting (status bits 0x%x)", bits);
         }
+    }
+    return GW_OK;
+}
+
+gw_status gw_set_block_scaled(gw_ctx* c, int32_t enable) {
+    if (!c) return fail(GW_E_ARG, "null context");
+    CtxLock lk(c);
+    c->block_scaled = enable != 0;
+    c->w.block_scaled = c->block_scaled;
+    if (c->graph.exec) {  // a captured stack forward baked the old choice in
+        cudaGraphExecDestroy(c->graph.exec);
+        c->graph = gw_ctx::StackGraph{};
     }
     return GW_OK;
 }

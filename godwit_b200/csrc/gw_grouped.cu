@@ -50,6 +50,7 @@
 #include <stdint.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "gw_async.cuh"
 #include "gw_device.cuh"
@@ -72,11 +73,22 @@ constexpr int kGroupPk = 8 * kTileRun;    // 16 KB of MXFP4 blocks per group
 constexpr int kGroupSc = 8 * 16 * 8;      // 1 KB of scale bytes per group
 constexpr int kRingBytes = kStages * kBSlot;
 constexpr int kGroupOff = kRingBytes;
-constexpr int kDynSmem = kGroupOff + kGroups * (kGroupPk + kGroupSc) + 1024;  // + alignment slack
+constexpr int kTsfOff = kGroupOff + kGroups * (kGroupPk + kGroupSc);  // block-scaled: token scale words
+constexpr int kTsfSlot = kNMax * 4;                                   // 128 tokens x one word per stage
+constexpr int kDynSmem = kTsfOff + kStages * kTsfSlot + 1024;         // + alignment slack
 constexpr int kThreads = 15 * 32;
 constexpr int kTmemCols = 512;            // accumulators 2 x kNMax, then the weight ring
 constexpr int kAColBase = 2 * kNMax;
 static_assert(kAColBase + kStages * kACols <= kTmemCols, "TMEM budget");
+// Block-scaled mode: per stage 128 x 128 e2m1 weights in shared memory (the
+// MMA's unpacked form: 16 values in 8 bytes, then 8 bytes of padding, so a
+// row of 128 values is 128 bytes) and 128 x 128 E4M3 token codes; scale words
+// (four E8M0 bytes = the stage's four blocks) in TMEM after the accumulators.
+constexpr int kMxASlot = kM * 128;        // 16 KB
+constexpr int kMxBSlot = kNMax * 128;     // 16 KB
+constexpr int kMxSfa = 2 * kNMax;         // TMEM columns: weight scales, 4 per stage
+constexpr int kMxSfb = kMxSfa + 4 * kStages;  // token scales, 4 per stage (tokens 32j..32j+31)
+static_assert(kStages * (kMxASlot + kMxBSlot) <= kRingBytes, "block-scaled ring fits the f16 ring");
 
 // Warp roles.
 constexpr int kConvWarps = 8, kEpiWarp0 = 8, kWeightWarp = 12, kTokenWarp = 13, kMmaWarp = 14;
@@ -117,6 +129,7 @@ struct GroupedArgs {
     int rexp_off;             // row offset of this matrix in the row-exponent table
     int bdiv;                 // token row = slot / bdiv
     int mode;                 // 0 gate_up clamped GLU, 1 gate_up SiLU, 2 down
+    const uint32_t* bsf;      // block-scaled mode: token scale words [rows][ceil(K/128)]
 };
 
 // ---- PTX wrappers (the mbarrier / bulk-copy ones are in gw_async.cuh) ------
@@ -148,6 +161,25 @@ __device__ __forceinline__ void tc_mma_ta(uint32_t tmem, uint32_t a_tmem, uint64
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem),
         "r"(a_tmem), "l"(bd), "r"(idesc), "r"(accumulate)
         : "memory");
+}
+// Block-scaled MMA: A e2m1 and B e4m3 from shared memory (descriptors), fp32
+// accumulators in TMEM, E8M0 scale factors in TMEM at sfa / sfb (the byte
+// used is chosen by the instruction descriptor's scale-factor ids).
+__device__ __forceinline__ void tc_mma_mx(uint32_t tmem, uint64_t ad, uint64_t bd, uint32_t idesc,
+                                          uint32_t accumulate, uint32_t sfa, uint32_t sfb) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(tmem),
+        "l"(ad), "l"(bd), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st1(uint32_t taddr, uint32_t v) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, uint32_t v0, uint32_t v1, uint32_t v2, uint32_t v3) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr), "r"(v0), "r"(v1),
+                 "r"(v2), "r"(v3)
+                 : "memory");
 }
 // 32 consecutive 32-bit TMEM columns of this thread's lane.
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
@@ -213,6 +245,7 @@ __device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
 
 struct Shared {
     uint64_t full[kStages], empty[kStages], gfull[kGroups], gempty[kGroups], tfull[2], tempty[2], fin;
+    uint64_t tsf[kStages];  // block-scaled: the stage's token scale words are in shared memory
     uint32_t tmem;
     int abort;
     int nact, nitems, chunks, mt;
@@ -509,8 +542,183 @@ __device__ __forceinline__ void role_mma(Shared& sh, const GroupedArgs& a, char*
     __syncwarp();
 }
 
+// ---- block-scaled roles (gw_set_block_scaled) ------------------------------
+
+// Unpackers (warps 0-7, in place of the converters): thread c owns weight row
+// r = m0 + (c & 127) and blocks 2h, 2h + 1 of each stage (h = c >> 7).  It
+// copies them from the group ring into the MMA's unpacked e2m1 layout (each
+// 16-value half block = 8 bytes of codes + 8 bytes of zeros, canonical
+// K-major core matrices of 8 rows x 16 bytes); the h = 0 threads write the
+// row's four block scales as one TMEM word (lane r, column sfa + r / 32), and
+// the h = 1 warps — one per TMEM lane quarter — copy the chunk's token scale
+// words into their quarter (lane n % 32, column sfb + n / 32: every quarter
+// holds the whole token scale vector).
+__device__ __forceinline__ void role_unpack(Shared& sh, const GroupedArgs& a, char* smem) {
+    const int c = threadIdx.x;
+    const int r = c & (kM - 1), h = c >> 7, lane = c & 31, warp = c >> 5;
+    const int lr = r & 15, tile = r >> 4;
+    const int nblk = a.K >> 5, ngrp = (nblk + 7) >> 3;
+    unsigned* status = a.w.status;
+    const char* ring = smem + kGroupOff;
+    const uint32_t tlane = (uint32_t)((warp & 3) * 32) << 16;
+    int g = 0, gq = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; ok && it < sh.nitems; it += gridDim.x) {
+        const Item item = decode(sh, it);
+        const bool valid = item.m0 + r < a.M;
+        for (int grp = 0; ok && grp < ngrp; ++grp, ++gq) {
+            const int w = min(8, nblk - 8 * grp);
+            const int gslot = gq % kGroups;
+            if (!warp_wait(&sh.abort, &sh.gfull[gslot], (gq / kGroups) & 1, status, 2u)) { ok = false; break; }
+            const char* gb = ring + gslot * (kGroupPk + kGroupSc);
+            for (int sub = 0; sub * 4 < w; ++sub, ++g) {
+                const int kb = min(4, w - 4 * sub);
+                const bool mine = 2 * h < kb;
+                const int bl = 4 * sub + 2 * h;
+                uint4 q[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+                uint32_t sfw = 0;
+                if (valid && mine) {
+                    const uint4* src = reinterpret_cast<const uint4*>(gb + tile * kTileRun + (lr * w + bl) * 16);
+                    q[0] = src[0];
+                    q[1] = src[1];
+                }
+                if (valid && h == 0) {  // the row's scale bytes of the stage's blocks
+                    const uint8_t* sb = reinterpret_cast<const uint8_t*>(gb + kGroupPk + tile * 128 + lr * w + 4 * sub);
+                    for (int b = 0; b < kb; ++b) sfw |= (uint32_t)sb[b] << (8 * b);
+                }
+                if (4 * sub + 4 >= w) {  // the group's last stage has been read: free its slot
+                    __syncwarp();
+                    if (lane == 0) bar_arrive(&sh.gempty[gslot]);
+                }
+                const int slot = g % kStages;
+                if (!warp_wait(&sh.abort, &sh.empty[slot], ((g / kStages) & 1) ^ 1, status, 4u)) { ok = false; break; }
+                if (valid && mine) {
+                    char* A = smem + slot * (kMxASlot + kMxBSlot) + (r >> 3) * 1024 + (r & 7) * 16;
+#pragma unroll
+                    for (int b2 = 0; b2 < 2; ++b2) {
+                        const int kc = 2 * (2 * h + b2);  // 16-value chunk index in the 128-value stage
+                        *reinterpret_cast<uint4*>(A + kc * 128) = make_uint4(q[b2].x, q[b2].y, 0u, 0u);
+                        *reinterpret_cast<uint4*>(A + (kc + 1) * 128) = make_uint4(q[b2].z, q[b2].w, 0u, 0u);
+                    }
+                    fence_async_smem();
+                }
+                if (h == 0) {
+                    tmem_st1(sh.tmem + tlane + kMxSfa + slot * 4 + (warp & 3), sfw);
+                } else {  // token scale words of the stage (tokens 32j + lane), staged by the token warp
+                    if (!warp_wait(&sh.abort, &sh.tsf[slot], (g / kStages) & 1, status, 4u)) { ok = false; break; }
+                    const uint32_t* tsf = reinterpret_cast<const uint32_t*>(smem + kTsfOff + slot * kTsfSlot);
+                    tmem_st4(sh.tmem + tlane + kMxSfb + slot * 4, tsf[lane], tsf[32 + lane], tsf[64 + lane],
+                             tsf[96 + lane]);
+                }
+                tmem_st_wait();
+                tc_before_sync();
+                __syncwarp();
+                if (lane == 0) bar_arrive(&sh.full[slot]);
+            }
+        }
+    }
+}
+
+// Token producer of the block-scaled mode: one TMA (128 rows x 128 E4M3
+// codes, 128B swizzle) per stage, and the stage's token scale words (one per
+// token) into shared memory for the unpackers, up to a ring ahead of them.
+__device__ __forceinline__ void role_tokens_mx(Shared& sh, const GroupedArgs& a, char* smem,
+                                               const CUtensorMap* map) {
+    const int nblk = a.K >> 5, ngrp = (nblk + 7) >> 3, nst = (a.K + 127) >> 7;
+    const int lane = threadIdx.x & 31;
+    unsigned* status = a.w.status;
+    int g = 0;
+    for (int it = blockIdx.x; it < sh.nitems; it += gridDim.x) {
+        const Item item = decode(sh, it);
+        for (int grp = 0; grp < ngrp; ++grp) {
+            const int w = min(8, nblk - 8 * grp);
+            for (int sub = 0; sub * 4 < w; ++sub, ++g) {
+                const int slot = g % kStages;
+                // token scale words of this stage (loaded before the slot wait: they
+                // only depend on the item)
+                uint32_t tw[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    tw[j] = 32 * j + lane < item.n
+                                ? __ldg(a.bsf + (int64_t)(item.g0 + 32 * j + lane) * nst + 2 * grp + sub)
+                                : 0u;
+                if (!warp_wait(&sh.abort, &sh.empty[slot], ((g / kStages) & 1) ^ 1, status, 8u)) return;
+                uint32_t* tsf = reinterpret_cast<uint32_t*>(smem + kTsfOff + slot * kTsfSlot);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) tsf[32 * j + lane] = tw[j];
+                __syncwarp();
+                if (lane == 0) {
+                    bar_arrive(&sh.tsf[slot]);
+                    char* B = smem + slot * (kMxASlot + kMxBSlot) + kMxASlot;
+                    bar_arrive_tx(&sh.full[slot], kMxBSlot);
+                    tma_2d(B, map, (8 * grp + 4 * sub) * 32, item.g0, &sh.full[slot]);
+                }
+                __syncwarp();
+            }
+        }
+    }
+}
+
+// MMA issuer of the block-scaled mode: kb MMAs of K = 32 per stage, scale
+// bytes k of the stage's words.
+__device__ __forceinline__ void role_mma_mx(Shared& sh, const GroupedArgs& a, char* smem) {
+    const int nblk = a.K >> 5, ngrp = (nblk + 7) >> 3;
+    const int lane = threadIdx.x & 31;
+    unsigned* status = a.w.status;
+    const uint32_t base = saddr(smem);
+    int g = 0, il = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; ok && it < sh.nitems; it += gridDim.x, ++il) {
+        const Item item = decode(sh, it);
+        const int n = max(16, (item.n + 15) & ~15);
+        // a E2M1 (5), b E4M3 (0), E8M0 scales, N, M = 128, K = 32
+        const uint32_t idesc0 = (5u << 7) | (0u << 10) | (1u << 23) | ((uint32_t)(n >> 3) << 17) |
+                                ((uint32_t)(kM >> 4) << 24);
+        const int b = il & 1;
+        if (!warp_wait(&sh.abort, &sh.tempty[b], ((il >> 1) & 1) ^ 1, status, 16u)) break;
+        tc_after_sync();
+        const uint32_t dtm = sh.tmem + b * kNMax;
+        bool first = true;
+        for (int grp = 0; ok && grp < ngrp; ++grp) {
+            const int w = min(8, nblk - 8 * grp);
+            for (int sub = 0; sub * 4 < w; ++sub, ++g) {
+                const int kb = min(4, w - 4 * sub);
+                const int slot = g % kStages;
+                if (!warp_wait(&sh.abort, &sh.full[slot], (g / kStages) & 1, status, 32u)) { ok = false; break; }
+                tc_after_sync();
+                if (lane == 0) {
+                    const uint32_t A = base + slot * (kMxASlot + kMxBSlot), B = A + kMxASlot;
+                    const uint32_t sfa = sh.tmem + kMxSfa + slot * 4, sfb = sh.tmem + kMxSfb + slot * 4;
+                    for (int k = 0; k < kb; ++k) {
+                        const uint32_t idesc = idesc0 | ((uint32_t)k << 29) | ((uint32_t)k << 4);
+                        tc_mma_mx(dtm, smem_desc(A + k * 256, 128, 1024, 0), smem_desc(B + k * 32, 16, 1024, 2),
+                                  idesc, first ? 0u : 1u, sfa, sfb);
+                        first = false;
+                    }
+                    tc_commit(&sh.empty[slot]);
+                }
+                __syncwarp();
+            }
+        }
+        if (!ok) break;
+        if (lane == 0) tc_commit(&sh.tfull[b]);
+        __syncwarp();
+    }
+    if (lane == 0) {
+        tc_commit(&sh.fin);
+        const long long t0 = clock64();
+        while (!bar_try(&sh.fin, 0)) {
+            if (clock64() - t0 > kWaitCycles) {
+                if (status) atomicOr(status, 64u);
+                break;
+            }
+        }
+    }
+    __syncwarp();
+}
+
 // Epilogue: thread t (0..127) owns TMEM lane t = tile row m0 + t.
-template <int kMode>
+template <int kMode, bool kMX>
 __device__ __forceinline__ void role_epilogue(Shared& sh, const GroupedArgs& a, long long (&gt_acc)[16]) {
     const int t = threadIdx.x - kEpiWarp0 * 32;
     const int ew = t >> 5, lane = t & 31;
@@ -524,7 +732,9 @@ __device__ __forceinline__ void role_epilogue(Shared& sh, const GroupedArgs& a, 
         const int64_t le = item.e / a.d.shard_count;
         const uint8_t* ex = a.L.base + le * a.L.stride;
         const uint16_t* bias = reinterpret_cast<const uint16_t*>(ex + a.L.off[a.sec_bias]);
-        const int emax = valid ? (int)a.L.rowexp[le * a.L.rowexp_stride + a.rexp_off + R] : 127;
+        // the f16 path's weights carry the row shift 2^(1 - emax); the block-scaled
+        // path's products are already in the true scale
+        const int emax = kMX ? 128 : (valid ? (int)a.L.rowexp[le * a.L.rowexp_stride + a.rexp_off + R] : 127);
         const float bv = valid ? bf16_bits_to_f32(bias[R]) : 0.f;
         const int p = emax - 128, p1 = p / 2;  // undoes the 2^(1 - emax) row shift
         const float rs1 = pow2f(p1), rs2 = pow2f(p - p1);
@@ -532,7 +742,7 @@ __device__ __forceinline__ void role_epilogue(Shared& sh, const GroupedArgs& a, 
         const int32_t* list = a.w.lists + (int64_t)item.e * a.w.tcap + item.c0;
         static_assert(kNMax == 128, "one column per epilogue thread");
         const int cs = t < item.n ? __ldg(list + t) : 0;
-        const float cm = t < item.n ? (kMode == 2 ? a.w.weights[cs] : a.w.xmul[cs / a.d.k]) : 0.f;
+        const float cm = t < item.n ? (kMode == 2 ? a.w.weights[cs] : (kMX ? 1.f : a.w.xmul[cs / a.d.k])) : 0.f;
         group_sync(1, 128);
         sh.col_slot[t] = cs;
         sh.col_mul[t] = cm;
@@ -574,7 +784,7 @@ __device__ __forceinline__ void role_epilogue(Shared& sh, const GroupedArgs& a, 
     }
 }
 
-template <int kMode>
+template <int kMode, bool kMX>
 __global__ void __launch_bounds__(kThreads, 1) k_grouped(const __grid_constant__ CUtensorMap bmap,
                                                          GroupedArgs a) {
     extern __shared__ unsigned char dyn_raw[];
@@ -599,6 +809,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_grouped(const __grid_constant__
         for (int i = 0; i < kStages; ++i) { bar_init(&sh.full[i], kConvWarps + 1); bar_init(&sh.empty[i], 1); }
         for (int i = 0; i < kGroups; ++i) { bar_init(&sh.gfull[i], 1); bar_init(&sh.gempty[i], kConvWarps); }
         for (int i = 0; i < 2; ++i) { bar_init(&sh.tfull[i], 1); bar_init(&sh.tempty[i], 128); }
+        for (int i = 0; i < kStages; ++i) bar_init(&sh.tsf[i], 1);
         bar_init(&sh.fin, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -662,11 +873,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_grouped(const __grid_constant__
     tc_after_sync();
 
     [[maybe_unused]] long long gt_acc[16] = {};  // phase cycle counters (trace builds)
-    if (warp < kConvWarps) role_convert(sh, a, smem, gt_acc);
-    else if (warp < kWeightWarp) role_epilogue<kMode>(sh, a, gt_acc);
-    else if (warp == kWeightWarp) role_weights(sh, a, smem, gt_acc);
-    else if (warp == kTokenWarp) role_tokens(sh, a, smem, &bmap, gt_acc);
-    else role_mma(sh, a, smem, gt_acc);
+    if (kMX) {
+        if (warp < kConvWarps) role_unpack(sh, a, smem);
+        else if (warp < kWeightWarp) role_epilogue<kMode, true>(sh, a, gt_acc);
+        else if (warp == kWeightWarp) role_weights(sh, a, smem, gt_acc);
+        else if (warp == kTokenWarp) role_tokens_mx(sh, a, smem, &bmap);
+        else role_mma_mx(sh, a, smem);
+    } else {
+        if (warp < kConvWarps) role_convert(sh, a, smem, gt_acc);
+        else if (warp < kWeightWarp) role_epilogue<kMode, false>(sh, a, gt_acc);
+        else if (warp == kWeightWarp) role_weights(sh, a, smem, gt_acc);
+        else if (warp == kTokenWarp) role_tokens(sh, a, smem, &bmap, gt_acc);
+        else role_mma(sh, a, smem, gt_acc);
+    }
 
     tc_before_sync();
     __syncthreads();
@@ -707,6 +926,83 @@ __global__ void __launch_bounds__(256) k_gather(MoeDims d, MoeWork w, int H) {
     }
 }
 
+// One row of K values -> MXFP8: E4M3 codes q[K] and scale words sf[ceil(K/128)]
+// (byte b of word s = the E8M0 scale of block 4s + b).  One warp; lane l
+// takes values 4l..4l+3 of each 128-value stage, 8 lanes per 32-value block.
+// Scale = 2^(floor(log2 max|x|) - 8) (byte = the max's biased exponent - 8,
+// clamped to [0, 254]; 0 for an all-zero block); codes = x / scale rounded to
+// nearest-even E4M3, saturating.  oracle.quantize_mxfp8 restates this.
+template <typename In>
+__device__ __forceinline__ void quantize_row_mx(const In* __restrict__ src, int K, uint8_t* __restrict__ q,
+                                                uint32_t* __restrict__ sf) {
+    const int lane = threadIdx.x & 31;
+    const int nst = (K + 127) >> 7;
+    for (int s = 0; s < nst; ++s) {
+        const int c = s * 128 + lane * 4;
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        if (c < K) {
+            const uint2 raw = *reinterpret_cast<const uint2*>(src + c);
+            const uint32_t u[2] = {raw.x, raw.y};
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                if constexpr (sizeof(In) == 2 && std::is_same<In, __half>::value) {
+                    const __half2 h = *reinterpret_cast<const __half2*>(&u[j]);
+                    v[2 * j] = __low2float(h);
+                    v[2 * j + 1] = __high2float(h);
+                } else {  // bf16 bits
+                    v[2 * j] = __uint_as_float(u[j] << 16);
+                    v[2 * j + 1] = __uint_as_float(u[j] & 0xffff0000u);
+                }
+            }
+        }
+        float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+        const int eb = (int)((__float_as_uint(m) >> 23) & 0xffu);
+        const int byte = m > 0.f ? min(254, max(0, eb - 8)) : 0;
+        const int p = 127 - byte, p1 = p / 2;
+        const float f1 = pow2f(p1), f2 = pow2f(p - p1);
+        uint32_t lo, hi;
+        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(*reinterpret_cast<unsigned short*>(&lo)) : "f"(v[1] * f1 * f2), "f"(v[0] * f1 * f2));
+        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(*reinterpret_cast<unsigned short*>(&hi)) : "f"(v[3] * f1 * f2), "f"(v[2] * f1 * f2));
+        if (c < K) *reinterpret_cast<uint32_t*>(q + c) = (lo & 0xffffu) | ((hi & 0xffffu) << 16);
+        const uint32_t b0 = __shfl_sync(0xffffffffu, byte, 0), b1 = __shfl_sync(0xffffffffu, byte, 8);
+        const uint32_t b2 = __shfl_sync(0xffffffffu, byte, 16), b3 = __shfl_sync(0xffffffffu, byte, 24);
+        if (lane == 0) sf[s] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+    }
+}
+
+// Block-scaled mode's token rows: every (expert, token) slot's x row quantised
+// to MXFP8 in expert order (row epre[e] + i).  grid (E, 32), 8 warps.
+template <typename In>
+__global__ void __launch_bounds__(256) k_gather_mx(MoeDims d, MoeWork w, const In* __restrict__ x, int H) {
+    __shared__ int off;
+    const int e = blockIdx.x, warp = threadIdx.x >> 5;
+    if (threadIdx.x < 32) {
+        int s = 0;
+        for (int j = threadIdx.x; j < e; j += 32) s += min(w.counts[j], w.tcap);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (threadIdx.x == 0) off = s;
+    }
+    __syncthreads();
+    const int cnt = min(w.counts[e], w.tcap), nst = (H + 127) >> 7;
+    for (int i = blockIdx.y * 8 + warp; i < cnt; i += gridDim.y * 8) {
+        const int tok = w.lists[(int64_t)e * w.tcap + i] / d.k;
+        quantize_row_mx(x + (int64_t)tok * H, H, w.xq + (int64_t)(off + i) * H, w.xsf + (int64_t)(off + i) * nst);
+    }
+}
+
+// Block-scaled mode's activations: the f16 rows gate_up wrote (expert order)
+// quantised to MXFP8 for the down projection.  One warp per row.
+__global__ void __launch_bounds__(256) k_quant_act(MoeWork w, int rows, int F) {
+    const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (r >= rows) return;
+    const int nst = (F + 127) >> 7;
+    quantize_row_mx(w.act + (int64_t)r * F, F, w.aq + (int64_t)r * F, w.asf + (int64_t)r * nst);
+}
+
 // Largest E8M0 exponent of each row (bytes 1..254; 127 when the row has
 // none) of a row-major scale matrix.
 __global__ void k_rowexp(const uint8_t* __restrict__ scales, int rows, int nblk, uint8_t* __restrict__ out) {
@@ -736,12 +1032,11 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }  // namespace
 
 int configure_grouped() {
-    if (cudaFuncSetAttribute(k_grouped<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem) != cudaSuccess)
-        return -1;
-    if (cudaFuncSetAttribute(k_grouped<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem) != cudaSuccess)
-        return -1;
-    if (cudaFuncSetAttribute(k_grouped<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem) != cudaSuccess)
-        return -1;
+    const void* fns[6] = {(const void*)k_grouped<0, false>, (const void*)k_grouped<1, false>,
+                          (const void*)k_grouped<2, false>, (const void*)k_grouped<0, true>,
+                          (const void*)k_grouped<1, true>,  (const void*)k_grouped<2, true>};
+    for (const void* f : fns)
+        if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem) != cudaSuccess) return -1;
     return 0;
 }
 
@@ -753,46 +1048,67 @@ bool grouped_supported(const MoeDims& d, const MoeWork& w) {
 }
 
 int launch_grouped(const LayerView& L, const MoeDims& d, const MoeWork& w, int which, int sms,
-                   cudaStream_t s) {
+                   cudaStream_t s, const void* x, int x_dtype) {
+    const bool mx = w.block_scaled != 0;
+    if (mx && which == 0 && !x) return -1;  // the block-scaled gather quantises the layer input
     GroupedArgs a;
     a.L = L;
     a.d = d;
     a.w = w;
     const void* bsrc;
-    uint64_t brows;
+    uint64_t brows = (uint64_t)w.tcap * d.k;
     if (which == 0) {
         a.M = 2 * d.F; a.K = d.H;
         a.sec_packed = 0; a.sec_scales = 1; a.sec_bias = 4;
         a.rexp_off = 0;
-        bsrc = w.xg; brows = (uint64_t)w.tcap * d.k; a.bdiv = d.k;
+        bsrc = mx ? (const void*)w.xq : (const void*)w.xg;
+        a.bsf = w.xsf;
+        a.bdiv = d.k;
         a.mode = d.act == 0 ? 0 : 1;
     } else {
         a.M = d.H; a.K = d.F;
         a.sec_packed = 2; a.sec_scales = 3; a.sec_bias = 5;
         a.rexp_off = 2 * d.F;
-        bsrc = w.act; brows = (uint64_t)w.tcap * d.k; a.bdiv = 1;
+        bsrc = mx ? (const void*)w.aq : (const void*)w.act;
+        a.bsf = w.asf;
+        a.bdiv = 1;
         a.mode = 2;
     }
-    // expert-ordered token rows: [brows][K] f16, loaded 64 columns x 128 rows
-    // per box into 128-byte-swizzled shared rows
+    // expert-ordered token rows [brows][K] (f16, or E4M3 codes in the
+    // block-scaled mode), one 128-byte row slice x 128 rows per box, 128-byte
+    // swizzle
     CUtensorMap map;
-    const cuuint64_t gdim[2] = {(cuuint64_t)a.K, (cuuint64_t)brows};
-    const cuuint64_t gstride[1] = {(cuuint64_t)a.K * 2};
-    const cuuint32_t box[2] = {kBox, kNMax}, estride[2] = {1, 1};
+    const int esz = mx ? 1 : 2;
+    const cuuint64_t gdim[2] = {(cuuint64_t)a.K, brows};
+    const cuuint64_t gstride[1] = {(cuuint64_t)a.K * esz};
+    const cuuint32_t box[2] = {(cuuint32_t)(128 / esz), kNMax}, estride[2] = {1, 1};
     auto enc = tensor_map_encoder();
-    if (!enc || enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(bsrc), gdim, gstride, box,
-                    estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                    CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    if (!enc || enc(&map, mx ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                    const_cast<void*>(bsrc), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return -1;
     int launched = 0;
     if (which == 0) {
-        k_gather<<<dim3(d.E, 32), 256, 0, s>>>(d, w, d.H);
+        if (!mx) k_gather<<<dim3(d.E, 32), 256, 0, s>>>(d, w, d.H);
+        else if (x_dtype == kF16) k_gather_mx<__half><<<dim3(d.E, 32), 256, 0, s>>>(d, w, static_cast<const __half*>(x), d.H);
+        else k_gather_mx<uint16_t><<<dim3(d.E, 32), 256, 0, s>>>(d, w, static_cast<const uint16_t*>(x), d.H);
+        ++launched;
+    } else if (mx) {
+        const int rows = w.tcap * d.k;
+        k_quant_act<<<(rows + 7) / 8, 256, 0, s>>>(w, rows, d.F);
         ++launched;
     }
     const dim3 grid(sms), block(kThreads);
-    if (a.mode == 0) k_grouped<0><<<grid, block, kDynSmem, s>>>(map, a);
-    else if (a.mode == 1) k_grouped<1><<<grid, block, kDynSmem, s>>>(map, a);
-    else k_grouped<2><<<grid, block, kDynSmem, s>>>(map, a);
+    if (mx) {
+        if (a.mode == 0) k_grouped<0, true><<<grid, block, kDynSmem, s>>>(map, a);
+        else if (a.mode == 1) k_grouped<1, true><<<grid, block, kDynSmem, s>>>(map, a);
+        else k_grouped<2, true><<<grid, block, kDynSmem, s>>>(map, a);
+    } else {
+        if (a.mode == 0) k_grouped<0, false><<<grid, block, kDynSmem, s>>>(map, a);
+        else if (a.mode == 1) k_grouped<1, false><<<grid, block, kDynSmem, s>>>(map, a);
+        else k_grouped<2, false><<<grid, block, kDynSmem, s>>>(map, a);
+    }
     return cudaGetLastError() == cudaSuccess ? launched + 1 : -1;
 }
 

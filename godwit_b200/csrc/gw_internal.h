@@ -52,10 +52,15 @@ struct MoeWork {
     __half* act;       // [tcap*k][F]  activated gate_up output (f16, as the reference); slot
                        //              order on the GEMV path, expert order on the tensor-core path
     __half* xg;        // [tcap*k][H]  x16 rows gathered in expert order (tensor-core path)
+    uint8_t* xq;       // [tcap*k][H]  MXFP8 (E4M3) token rows in expert order (block-scaled mode)
+    uint32_t* xsf;     // [tcap*k][ceil(H/128)] their E8M0 scales, 4 blocks per word
+    uint8_t* aq;       // [tcap*k][F]  MXFP8 activations in expert order (block-scaled mode)
+    uint32_t* asf;     // [tcap*k][ceil(F/128)]
     float* ybuf;       // [tcap*k][H]  routing-weighted down output per slot
     unsigned* done;    // [tcap/8+1]   router completion counter per token chunk (self-resetting)
     unsigned* status;  // [1]          sticky error bits set by bounded waits (nullptr: none)
     int mma_min_avg;   // tensor-core expert path when T*k >= mma_min_avg * E (0: never)
+    int block_scaled;  // tensor-core path as block-scaled MXFP4 x MXFP8 MMAs (activations quantised)
 };
 
 // Host-side launchers; each returns the number of kernels it launched (or -1
@@ -90,7 +95,7 @@ size_t gemv_smem_bytes(int cols, int max_tok);
 // Tensor-core grouped expert GEMM (gw_grouped.cu): which 0 = gate_up + activation,
 // 1 = down + routing weight.  `sms` persistent CTAs.
 int launch_grouped(const LayerView& L, const MoeDims& d, const MoeWork& w, int which, int sms,
-                   cudaStream_t s);
+                   cudaStream_t s, const void* x = nullptr, int x_dtype = 0);
 bool grouped_supported(const MoeDims& d, const MoeWork& w);
 int configure_grouped();
 // Decode expert GEMVs with bulk-copied weights (gw_stream.cu): which 0 =

@@ -71,6 +71,11 @@ class Context:
     def sync(self) -> None:
         call("gw_sync", self.handle)
 
+    def set_block_scaled(self, enable: bool) -> None:
+        """Tensor-core expert layers as block-scaled MXFP4 x MXFP8 MMAs (the
+        expert inputs and activations quantised to MXFP8) instead of exact f16."""
+        call("gw_set_block_scaled", self.handle, 1 if enable else 0)
+
     def set_decode_streaming(self, enable: bool) -> None:
         """Decode-size layers stream the expert weights with bulk copies into a
         shared-memory ring, or (default) read them with per-thread loads; the

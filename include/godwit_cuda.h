@@ -130,6 +130,13 @@ GW_API gw_status gw_set_tensor_core_min_tokens(gw_ctx* ctx, int32_t min_avg);
  * GEMV tiles (k_stream); 0 (default, currently the faster) runs the same
  * tiles on per-thread loads.  The results agree to fp32 summation order. */
 GW_API gw_status gw_set_decode_streaming(gw_ctx* ctx, int32_t enable);
+/* Tensor-core expert path arithmetic: 0 (default) = exact f16 activations
+ * (the reference's numerics, fp32 accumulation); 1 = tcgen05 block-scaled
+ * MXFP4 x MXFP8 MMAs, the expert inputs and activations quantised to MXFP8
+ * (E4M3 codes, one E8M0 scale per 32 values along K, scale = 2^(floor(log2
+ * max|x|) - 8), nearest-even, saturating) — half the MMA instructions and no
+ * weight widening, at ~6% relative (rel-L2) deviation from the f16 result. */
+GW_API gw_status gw_set_block_scaled(gw_ctx* ctx, int32_t enable);
 
 /* ---- layout (ExpertLayout.init, Install/InstallLayout.swift:50-92) ------ */
 

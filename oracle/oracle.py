@@ -274,6 +274,66 @@ def moe_layer64(spec, strides: np.ndarray, x: np.ndarray, experts: np.ndarray,
     return out
 
 
+# ---- MXFP8 activations (config 4's block-scaled tensor-core mode) ----------
+#
+# Not part of the reference (which feeds f16 activations to every expert
+# GEMV); it restates the OCP MX recipe the device quantiser follows, so the
+# block-scaled path has an exact oracle: per 32-value block along K, shared
+# exponent X = floor(log2(max |x|)) - 8 (8 = E4M3's largest exponent), stored
+# as the E8M0 byte X + 127 clamped to [0, 254] (0 for an all-zero block);
+# elements = x / 2^X rounded to nearest-even E4M3, saturated to +-448.
+
+def quantize_mxfp8(x: np.ndarray):
+    """x [rows, K] (K % 32 == 0) -> (codes uint8 [rows, K] E4M3, scales
+    uint8 [rows, K/32] E8M0)."""
+    import ml_dtypes
+    x = np.asarray(x, np.float32)
+    rows, K = x.shape
+    xb = x.reshape(rows, K // 32, 32)
+    amax = np.abs(xb).max(-1)
+    _, ex = np.frexp(amax)                      # amax = m * 2^ex, m in [0.5, 1)
+    byte = np.where(amax > 0, np.clip(ex - 1 - 8 + 127, 0, 254), 0).astype(np.int64)
+    q = xb * np.exp2(127.0 - byte)[..., None]   # exact power-of-two scaling (float64)
+    q = np.clip(q, -448.0, 448.0).astype(np.float32).astype(ml_dtypes.float8_e4m3fn)
+    return q.view(np.uint8).reshape(rows, K), byte.astype(np.uint8)
+
+
+def dequantize_mxfp8(codes: np.ndarray, scales: np.ndarray) -> np.ndarray:
+    import ml_dtypes
+    rows, K = codes.shape
+    v = codes.view(ml_dtypes.float8_e4m3fn).astype(np.float64).reshape(rows, K // 32, 32)
+    return (v * np.exp2(scales.astype(np.float64) - 127.0)[..., None]).reshape(rows, K)
+
+
+def moe_layer64_mx(spec, strides: np.ndarray, x: np.ndarray, experts: np.ndarray,
+                   weights: np.ndarray) -> np.ndarray:
+    """moe_layer64 with the block-scaled mode's activation handling: the
+    expert inputs quantised to MXFP8, the activations rounded to f16 (as the
+    reference stores them) and then quantised to MXFP8 for the down
+    projection."""
+    T = x.shape[0]
+    xq = dequantize_mxfp8(*quantize_mxfp8(np.asarray(x, np.float32)))
+    out = np.zeros((T, spec.hidden), dtype=np.float64)
+    for e in np.unique(experts):
+        if e < 0:
+            continue
+        gu, gb, dn, db = expert_sections(spec, strides[int(e)])
+        tt, jj = np.nonzero(experts == e)
+        g = xq[tt] @ gu.T + gb
+        gate, up = g[:, 0::2], g[:, 1::2]
+        if spec.activation == 0:
+            gate = np.minimum(gate, spec.limit)
+            up = np.clip(up, -spec.limit, spec.limit)
+            a = (up + 1.0) * (gate / (1.0 + np.exp(-spec.alpha * gate)))
+        else:
+            a = (gate / (1.0 + np.exp(-gate))) * up
+        a = a.astype(np.float16).astype(np.float32)
+        a = dequantize_mxfp8(*quantize_mxfp8(a))
+        y = a @ dn.T + db
+        np.add.at(out, tt, y * np.asarray(weights, np.float64)[tt, jj][:, None])
+    return out
+
+
 def rel_l2(a, b) -> float:
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)

@@ -155,3 +155,44 @@ def test_default_policy_switches_on_tokens_per_expert(ctx, oss):
         out, ex, wt = MoEBlock(ctx, bank).forward(xb, 0, "bf16")
         ref = O.moe_layer64(spec, st, synth.as_f32(xb, "bf16"), ex, wt)
         assert O.rel_l2(out, ref) < 1e-3
+
+
+# ---- block-scaled mode (gw_set_block_scaled): MXFP4 x MXFP8 tcgen05 MMAs ----
+
+def block_scaled(ctx, bank, xb, routing=None):
+    blk = MoEBlock(ctx, bank)
+    try:
+        ctx.set_tensor_core_min_tokens(1)
+        ctx.set_block_scaled(True)
+        return blk.forward(xb, 0, "bf16", routing=routing)
+    finally:
+        ctx.set_block_scaled(False)
+        ctx.set_tensor_core_min_tokens(8)
+
+
+@pytest.mark.parametrize("T", [16, 200, 700])
+def test_block_scaled_matches_quantised_oracle(ctx, oss, T):
+    """Exact oracle: the fp64 layer with the same MXFP8 quantisation of the
+    expert inputs and of the f16 activations (oracle.moe_layer64_mx)."""
+    bank, st, _ = oss
+    spec = bank.spec
+    rng = np.random.default_rng(100 + T)
+    xb = synth.make_hidden(rng, T, spec.hidden, "bf16")
+    out, ex, wt = block_scaled(ctx, bank, xb)
+    x = synth.as_f32(xb, "bf16")
+    assert np.all(np.isfinite(out))
+    assert O.rel_l2(out, O.moe_layer64_mx(spec, st, x, ex, wt)) < 1e-3
+    # and the deviation from the reference's f16-activation numerics: two
+    # E4M3 quantisations (3 mantissa bits, ~3.6% RMS each) give ~5.7%
+    assert O.rel_l2(out, O.moe_layer64(spec, st, x, ex, wt)) < 8e-2
+
+
+def test_block_scaled_qwen3(ctx):
+    bank, st, _ = make_bank(ctx, SMALL_QWEN, 501)
+    try:
+        spec = bank.spec
+        xb = synth.make_hidden(np.random.default_rng(502), 96, spec.hidden, "bf16")
+        out, ex, wt = block_scaled(ctx, bank, xb)
+        assert O.rel_l2(out, O.moe_layer64_mx(spec, st, synth.as_f32(xb, "bf16"), ex, wt)) < 1e-3
+    finally:
+        bank.close()
