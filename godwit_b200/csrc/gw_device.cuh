@@ -67,6 +67,13 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
 
 __device__ __forceinline__ uint32_t ldg_u32(const uint32_t* p) { return __ldg(p); }
 
+// Starts an L2 fill of [p, p + bytes) (both 16-byte aligned, bytes a multiple
+// of 16) without holding registers or shared memory: the later loads of the
+// range then wait on L2, not on DRAM.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ uint32_t ldg_u8(const uint8_t* p) {
     return static_cast<uint32_t>(__ldg(p));
 }
@@ -120,7 +127,10 @@ constexpr int kXBlockHalves = 40;
 //     rows and packed / scales the matrix base.
 //   kTiled = true: the bank's tiled layout (see tile_layout_offset); rowA /
 //     rowB are rows 0..15 of the tile and packed / scales point at the tile.
-template <int kTok, int kSets, bool kTiled = false>
+//   kPrefetch: start an L2 fill of the warp's whole K-range up front (tiled
+//     layout only; measured on B200 it speeds up the gate_up GEMVs by ~10%
+//     at decode batch 64 and slows the down GEMVs and batch 1 slightly).
+template <int kTok, int kSets, bool kTiled = false, bool kPrefetch = false>
 __device__ __forceinline__ void mxfp4_tile_diag(const uint8_t* __restrict__ packed,
                                                 const uint8_t* __restrict__ scales, int cols,
                                                 int rowA, int rowB, const __half* xs,
@@ -141,6 +151,22 @@ __device__ __forceinline__ void mxfp4_tile_diag(const uint8_t* __restrict__ pack
     const uint8_t* sB = scales + (kTiled ? 0 : (size_t)rowB * row_blocks);
 #pragma unroll
     for (int j = 0; j < kTok * kSets; ++j) { accA[j] = 0.f; accB[j] = 0.f; }
+    // Put the warp's whole K-range in flight at once (the register loads below
+    // keep only one 8-block group ahead): in the tiled layout blocks
+    // [blk0, blk1) of the tile's 16 rows are one contiguous run of groups.
+    if (kPrefetch && kTiled && blk1 > blk0) {
+        {
+            if (lane == 0) {
+                const uint32_t lo = (uint32_t)(blk0 >> 3) * 2048u;
+                const uint32_t hi = min((uint32_t)((blk1 + 7) >> 3) * 2048u, (uint32_t)(16 * (cols >> 1)));
+                prefetch_l2_bulk(packed + lo, hi - lo);
+            } else if (lane == 1) {  // the groups' scale bytes (16 rows x w per group)
+                const uint32_t lo = (uint32_t)(blk0 >> 3) * 128u;
+                const uint32_t hi = min((uint32_t)((blk1 + 7) >> 3) * 128u, (uint32_t)(16 * (cols >> 5)));
+                prefetch_l2_bulk(scales + lo, hi - lo);
+            }
+        }
+    }
 
     // Per 8-block group: the group's first block of row A / row B, and its
     // width in the layout (the tiled layout stores a group's rows w blocks

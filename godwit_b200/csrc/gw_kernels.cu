@@ -385,8 +385,8 @@ __device__ __forceinline__ void split_range(int nblk, int ksplit, int sp, int& b
 // scales point at the tile, rowA / rowB are tile rows) split over `ksplit` warps
 // and calls emit(token, rowA total, rowB total) once per (row pair, token)
 // on the split-0 warp.  Every thread of the CTA must call this (it
-// synchronises when ksplit > 1).
-template <class Emit>
+// synchronises when ksplit > 1).  kPrefetch: see mxfp4_tile_diag.
+template <bool kPrefetch, class Emit>
 __device__ __forceinline__ void run_tile(int n, bool valid, const uint8_t* packed,
                                          const uint8_t* scales, int cols, int rowA, int rowB,
                                          const __half* xs, int ksplit, Emit&& emit) {
@@ -403,16 +403,16 @@ __device__ __forceinline__ void run_tile(int n, bool valid, const uint8_t* packe
         const int st = diag_stride(cols);
         if (n == 1) {
             float a1[1], bb1[1];
-            mxfp4_tile_diag<1, 1, true>(packed, scales, cols, rowA, rowB, xs, st, 1, b0, b1, a1, bb1);
+            mxfp4_tile_diag<1, 1, true, false>(packed, scales, cols, rowA, rowB, xs, st, 1, b0, b1, a1, bb1);
             a[0] = a1[0];
             b[0] = bb1[0];
         } else if (n == 2) {
             float a2[2], bb2[2];
-            mxfp4_tile_diag<2, 1, true>(packed, scales, cols, rowA, rowB, xs, st, 2, b0, b1, a2, bb2);
+            mxfp4_tile_diag<2, 1, true, kPrefetch>(packed, scales, cols, rowA, rowB, xs, st, 2, b0, b1, a2, bb2);
             a[0] = a2[0]; a[1] = a2[1];
             b[0] = bb2[0]; b[1] = bb2[1];
         } else {
-            mxfp4_tile_diag<2, 2, true>(packed, scales, cols, rowA, rowB, xs, st, n, b0, b1, a, b);
+            mxfp4_tile_diag<2, 2, true, kPrefetch>(packed, scales, cols, rowA, rowB, xs, st, n, b0, b1, a, b);
         }
     }
     if (ksplit > 1) {
@@ -484,7 +484,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 5) k_gateup(LayerView L, MoeD
         __syncthreads();
         stage_x16(xs, diag_stride(H), w.x16, rows, n, H);
         __syncthreads();
-        run_tile(n, valid, packed + (size_t)tile * 16 * (H >> 1), scales + (size_t)tile * 16 * (H >> 5),
+        run_tile<true>(n, valid, packed + (size_t)tile * 16 * (H >> 1), scales + (size_t)tile * 16 * (H >> 5),
                  H, 2 * g, 2 * g + 1, xs, ksplit,
                  [&](int col, float ga, float ub) {
                      const float v = activate<kAct>(ga * xm[col] + bA, ub * xm[col] + bB, d.limit, d.alpha);
@@ -531,7 +531,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 5) k_down(LayerView L, MoeDim
         __syncthreads();
         stage_x16(xs, diag_stride(F), w.act, slots, n, F);
         __syncthreads();
-        run_tile(n, valid, packed + (size_t)tile * 16 * (F >> 1), scales + (size_t)tile * 16 * (F >> 5),
+        run_tile<false>(n, valid, packed + (size_t)tile * 16 * (F >> 1), scales + (size_t)tile * 16 * (F >> 5),
                  F, g, g + 8, xs, ksplit,
                  [&](int col, float ya, float yb) {
                      float* y = w.ybuf + (int64_t)slots[col] * H;
