@@ -127,10 +127,11 @@ constexpr int kXBlockHalves = 40;
 //     rows and packed / scales the matrix base.
 //   kTiled = true: the bank's tiled layout (see tile_layout_offset); rowA /
 //     rowB are rows 0..15 of the tile and packed / scales point at the tile.
-//   kPrefetch: start an L2 fill of the warp's whole K-range up front (tiled
-//     layout only; measured on B200 it speeds up the gate_up GEMVs by ~10%
-//     at decode batch 64 and slows the down GEMVs and batch 1 slightly).
-template <int kTok, int kSets, bool kTiled = false, bool kPrefetch = false>
+//   kPrefetch (tiled layout only): 1 = start an L2 fill of the warp's whole
+//     K-range up front (measured on B200: ~10% faster gate_up GEMVs at decode
+//     batch 64, slightly slower down GEMVs and batch 1); D >= 2 = keep the L2
+//     fill D 8-block groups ahead of the loads; 0 = none.
+template <int kTok, int kSets, bool kTiled = false, int kPrefetch = 0>
 __device__ __forceinline__ void mxfp4_tile_diag(const uint8_t* __restrict__ packed,
                                                 const uint8_t* __restrict__ scales, int cols,
                                                 int rowA, int rowB, const __half* xs,
@@ -154,15 +155,17 @@ __device__ __forceinline__ void mxfp4_tile_diag(const uint8_t* __restrict__ pack
     // Put the warp's whole K-range in flight at once (the register loads below
     // keep only one 8-block group ahead): in the tiled layout blocks
     // [blk0, blk1) of the tile's 16 rows are one contiguous run of groups.
+    const uint32_t tile_pk = 16u * (uint32_t)(cols >> 1), tile_sc = 16u * (uint32_t)(cols >> 5);
     if (kPrefetch && kTiled && blk1 > blk0) {
         {
+            const int blk_end = kPrefetch == 1 ? blk1 : min(blk1, blk0 + 8 * (kPrefetch + 1));
             if (lane == 0) {
                 const uint32_t lo = (uint32_t)(blk0 >> 3) * 2048u;
-                const uint32_t hi = min((uint32_t)((blk1 + 7) >> 3) * 2048u, (uint32_t)(16 * (cols >> 1)));
+                const uint32_t hi = min((uint32_t)((blk_end + 7) >> 3) * 2048u, tile_pk);
                 prefetch_l2_bulk(packed + lo, hi - lo);
             } else if (lane == 1) {  // the groups' scale bytes (16 rows x w per group)
                 const uint32_t lo = (uint32_t)(blk0 >> 3) * 128u;
-                const uint32_t hi = min((uint32_t)((blk1 + 7) >> 3) * 128u, (uint32_t)(16 * (cols >> 5)));
+                const uint32_t hi = min((uint32_t)((blk_end + 7) >> 3) * 128u, tile_sc);
                 prefetch_l2_bulk(scales + lo, hi - lo);
             }
         }
@@ -215,6 +218,14 @@ __device__ __forceinline__ void mxfp4_tile_diag(const uint8_t* __restrict__ pack
 #pragma unroll
         for (int r = 0; r < 2; ++r) { ca[r] = wa[r]; cb[r] = wb[r]; }
         if (base + 8 < nblk) load(base + 8);  // next group's loads in flight
+        if (kPrefetch >= 2 && kTiled && lane < 2) {  // the group kPrefetch + 1 ahead, into L2
+            const int nb = base + 8 * (kPrefetch + 1);
+            if (nb < nblk) {
+                const uint32_t unit = lane == 0 ? 2048u : 128u, total = lane == 0 ? tile_pk : tile_sc;
+                const uint32_t lo = (uint32_t)(nb >> 3) * unit;
+                prefetch_l2_bulk((lane == 0 ? packed : scales) + lo, min(unit, total - lo));
+            }
+        }
         float d[kSets][4];
 #pragma unroll
         for (int s = 0; s < kSets; ++s) d[s][0] = d[s][1] = d[s][2] = d[s][3] = 0.f;

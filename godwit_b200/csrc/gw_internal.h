@@ -11,7 +11,10 @@ namespace gw {
 constexpr int kMaxTopK = 16;
 constexpr int kMaxExperts = 256;
 constexpr int kTokTile = 8;       // tokens per router CTA
-constexpr int kRouterMmaMinTokens = 128;  // bf16 batches from here on use k_router_mma
+#ifndef GW_ROUTER_MMA_MIN
+#define GW_ROUTER_MMA_MIN 128
+#endif
+constexpr int kRouterMmaMinTokens = GW_ROUTER_MMA_MIN;  // bf16 batches from here on use k_router_mma
 constexpr int kChunk = 4;         // tokens per weight pass of an expert GEMV tile
 constexpr int kGemvWarps = 4;     // warps per GEMV CTA (one 16-row tile each)
 

@@ -54,17 +54,23 @@ __device__ __forceinline__ void store_act(void* p, int dtype, int64_t i, float v
 // exactly as in the reference (by current array order, which the swaps
 // perturb — not simply by lowest expert id).  NaN logits are outside this
 // contract (the reference's own result then depends on scan order).
-__device__ void select_topk_warp(const float* __restrict__ logits, int E, int k, int* ord,
+// The token's E logits are first copied (coalesced) into the warp's shared
+// scratch `lg`, so the passes read shared memory, not L2.
+__device__ void select_topk_warp(const float* __restrict__ logits_g, int E, int k, int* ord, float* lg,
                                  int32_t* experts, float* weights) {
     const int lane = threadIdx.x & 31;
-    for (int p = lane; p < E; p += 32) ord[p] = p;
+    for (int p = lane; p < E; p += 32) {
+        ord[p] = p;
+        lg[p] = __ldcg(logits_g + p);
+    }
     __syncwarp();
+    const float* logits = lg;
     for (int pos = 0; pos < k; ++pos) {
         float bv = 0.f;
         int bp = 0x7fffffff;
         bool have = false;
         for (int p = pos + ((lane - pos) & 31); p < E; p += 32) {
-            const float v = __ldcg(logits + ord[p]);
+            const float v = logits[ord[p]];
             if (!have || v > bv) { bv = v; bp = p; have = true; }
         }
 #pragma unroll
@@ -87,7 +93,7 @@ __device__ void select_topk_warp(const float* __restrict__ logits, int E, int k,
         float sel[kMaxTopK];
         float peak = 0.f;
         for (int j = 0; j < k; ++j) {
-            sel[j] = __ldcg(logits + ord[j]);
+            sel[j] = logits[ord[j]];
             if (j == 0 || sel[j] > peak) peak = sel[j];
         }
         float total = 0.f;
@@ -195,6 +201,7 @@ __global__ void __launch_bounds__(128) k_router(LayerView L, MoeDims d, const vo
 
     __shared__ int last;
     __shared__ int ord[4][kMaxExperts];
+    __shared__ float lgc[4][kMaxExperts];
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
@@ -206,7 +213,7 @@ __global__ void __launch_bounds__(128) k_router(LayerView L, MoeDims d, const vo
     __threadfence();
     if (threadIdx.x == 0) w.done[blockIdx.y] = 0u;
     for (int t = t0 + warp; t < t1; t += 4) {
-        select_topk_warp(w.logits + (int64_t)t * d.E, d.E, d.k, ord[warp],
+        select_topk_warp(w.logits + (int64_t)t * d.E, d.E, d.k, ord[warp], lgc[warp],
                          w.experts + (int64_t)t * d.k, w.weights + (int64_t)t * d.k);
         if (lane < d.k) group_slot(d, w, __ldcg(w.experts + (int64_t)t * d.k + lane), t * d.k + lane);
     }
@@ -255,6 +262,7 @@ __global__ void __launch_bounds__(128) k_router_mma(LayerView L, MoeDims d, cons
     const int H = d.H, E = d.E;
     __shared__ int shift[16];
     __shared__ int ord[4][kMaxExperts];
+    __shared__ float lgc[4][kMaxExperts];
     // row maxima of the CTA's tokens: warp w takes tokens 4w .. 4w+3
     for (int q = 0; q < 4; ++q) {
         const int t = t0 + warp * 4 + q;
@@ -341,7 +349,7 @@ __global__ void __launch_bounds__(128) k_router_mma(LayerView L, MoeDims d, cons
     for (int q = warp; q < 16; q += 4) {
         const int t = t0 + q;
         if (t >= T) break;
-        select_topk_warp(w.logits + (int64_t)t * E, E, d.k, ord[warp], w.experts + (int64_t)t * d.k,
+        select_topk_warp(w.logits + (int64_t)t * E, E, d.k, ord[warp], lgc[warp], w.experts + (int64_t)t * d.k,
                          w.weights + (int64_t)t * d.k);
         if (lane < d.k) group_slot(d, w, __ldcg(w.experts + (int64_t)t * d.k + lane), t * d.k + lane);
     }
@@ -386,7 +394,13 @@ __device__ __forceinline__ void split_range(int nblk, int ksplit, int sp, int& b
 // and calls emit(token, rowA total, rowB total) once per (row pair, token)
 // on the split-0 warp.  Every thread of the CTA must call this (it
 // synchronises when ksplit > 1).  kPrefetch: see mxfp4_tile_diag.
-template <bool kPrefetch, class Emit>
+#ifndef GW_PF_GATEUP
+#define GW_PF_GATEUP 1
+#endif
+#ifndef GW_PF_DOWN
+#define GW_PF_DOWN 2
+#endif
+template <int kPrefetch, class Emit>
 __device__ __forceinline__ void run_tile(int n, bool valid, const uint8_t* packed,
                                          const uint8_t* scales, int cols, int rowA, int rowB,
                                          const __half* xs, int ksplit, Emit&& emit) {
@@ -484,7 +498,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 5) k_gateup(LayerView L, MoeD
         __syncthreads();
         stage_x16(xs, diag_stride(H), w.x16, rows, n, H);
         __syncthreads();
-        run_tile<true>(n, valid, packed + (size_t)tile * 16 * (H >> 1), scales + (size_t)tile * 16 * (H >> 5),
+        run_tile<GW_PF_GATEUP>(n, valid, packed + (size_t)tile * 16 * (H >> 1), scales + (size_t)tile * 16 * (H >> 5),
                  H, 2 * g, 2 * g + 1, xs, ksplit,
                  [&](int col, float ga, float ub) {
                      const float v = activate<kAct>(ga * xm[col] + bA, ub * xm[col] + bB, d.limit, d.alpha);
@@ -531,7 +545,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 5) k_down(LayerView L, MoeDim
         __syncthreads();
         stage_x16(xs, diag_stride(F), w.act, slots, n, F);
         __syncthreads();
-        run_tile<false>(n, valid, packed + (size_t)tile * 16 * (F >> 1), scales + (size_t)tile * 16 * (F >> 5),
+        run_tile<GW_PF_DOWN>(n, valid, packed + (size_t)tile * 16 * (F >> 1), scales + (size_t)tile * 16 * (F >> 5),
                  F, g, g + 8, xs, ksplit,
                  [&](int col, float ya, float yb) {
                      float* y = w.ybuf + (int64_t)slots[col] * H;
