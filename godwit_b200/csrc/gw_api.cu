@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -888,6 +889,85 @@ gw_status gw_residual_round_async(gw_ctx* c, float* stream_dev, const float* del
     CtxLock lk(c);
     if ((st = set_device(c))) return st;
     return count(c, gw::launch_residual_round(stream_dev, delta_dev, x_out_dev, x_dtype, n, c->cur));
+}
+
+// Argument checks shared by the RMSNorm entry points.
+static gw_status check_norm(const void* stream, const void* weight, float eps, int32_t T, int32_t H) {
+    if (!stream || !weight) return fail(GW_E_ARG, "null argument");
+    if (T <= 0) return fail(GW_E_ARG, "T must be positive");
+    if (H <= 0 || H % 4) return fail(GW_E_ARG, "H = %d must be a positive multiple of 4", H);
+    if (!(eps >= 0.f) || !std::isfinite(eps)) return fail(GW_E_ARG, "eps must be finite and >= 0");
+    if (reinterpret_cast<uintptr_t>(stream) % 16 || reinterpret_cast<uintptr_t>(weight) % 8)
+        return fail(GW_E_ARG, "stream must be 16-byte and weight 8-byte aligned");
+    return GW_OK;
+}
+
+gw_status gw_rmsnorm_async(gw_ctx* c, const float* stream_dev, const uint16_t* weight_dev, float eps,
+                           int32_t T, int32_t H, void* out_dev) {
+    gw_status st = check_norm(stream_dev, weight_dev, eps, T, H);
+    if (st) return st;
+    if (!c || !out_dev) return fail(GW_E_ARG, "null argument");
+    if (reinterpret_cast<uintptr_t>(out_dev) % 8) return fail(GW_E_ARG, "out must be 8-byte aligned");
+    CtxLock lk(c);
+    if ((st = set_device(c))) return st;
+    return count(c, gw::launch_rmsnorm(stream_dev, weight_dev, eps, T, H, static_cast<__half*>(out_dev),
+                                       c->cur));
+}
+
+// The MoE half of TransformerLayer.forward on device memory: RMSNorm of the
+// residual stream into the workspace's x buffer (f16), router + experts on
+// it, and the combine adding the weighted expert sum into the stream.
+static gw_status moe_block_device(gw_ctx* c, gw_bank* b, int layer, float* stream, const uint16_t* norm_w,
+                                  float eps, int T) {
+    gw_status st = ensure_work(c, b, T);
+    if (st) return st;
+    __half* xn = static_cast<__half*>(c->w.xr);
+    if ((st = count(c, gw::launch_rmsnorm(stream, norm_w, eps, T, b->d.hidden, xn, c->cur)))) return st;
+    return moe_layer_device(c, b, layer, xn, GW_DTYPE_F16, T, nullptr, nullptr, stream, 1, nullptr);
+}
+
+gw_status gw_moe_block_async(gw_ctx* c, gw_bank* b, int32_t layer, float* stream_dev,
+                             const uint16_t* norm_w_dev, float eps, int32_t T, int32_t* experts_dev,
+                             float* weights_dev) {
+    if (!c) return fail(GW_E_ARG, "null argument");
+    gw_status st = check_bank(b, layer);
+    if (st || (st = check_norm(stream_dev, norm_w_dev, eps, T, b->d.hidden))) return st;
+    CtxLock lk(c);
+    if ((st = set_device(c))) return st;
+    if ((st = moe_block_device(c, b, layer, stream_dev, norm_w_dev, eps, T))) return st;
+    const size_t nk = (size_t)T * b->d.top_k;
+    if (experts_dev)
+        GW_CUDA(cudaMemcpyAsync(experts_dev, c->w.experts, nk * 4, cudaMemcpyDeviceToDevice, c->cur));
+    if (weights_dev)
+        GW_CUDA(cudaMemcpyAsync(weights_dev, c->w.weights, nk * 4, cudaMemcpyDeviceToDevice, c->cur));
+    return GW_OK;
+}
+
+gw_status gw_moe_block(gw_ctx* c, gw_bank* b, int32_t layer, float* stream, const uint16_t* norm_w,
+                       float eps, int32_t T, int32_t* experts_out, float* weights_out) {
+    if (!c || !stream || !norm_w) return fail(GW_E_ARG, "null argument");
+    gw_status st = check_bank(b, layer);
+    if (st) return st;
+    const int H = b->d.hidden;
+    if (T <= 0) return fail(GW_E_ARG, "T must be positive");
+    if (!(eps >= 0.f) || !std::isfinite(eps)) return fail(GW_E_ARG, "eps must be finite and >= 0");
+    CtxLock lk(c);
+    if ((st = set_device(c))) return st;
+    const size_t ns = (size_t)T * H * 4, nw = (size_t)H * 2, nk = (size_t)T * b->d.top_k;
+    Stage sg(c);
+    const size_t os = sg.add(ns), ow = sg.add(nw);
+    cudaError_t e = sg.alloc();
+    if (e != cudaSuccess) return cuda_fail(e, "staging allocation");
+    GW_CUDA(cudaMemcpyAsync(sg.at<float>(os), stream, ns, cudaMemcpyHostToDevice, c->cur));
+    GW_CUDA(cudaMemcpyAsync(sg.at<uint16_t>(ow), norm_w, nw, cudaMemcpyHostToDevice, c->cur));
+    if ((st = moe_block_device(c, b, layer, sg.at<float>(os), sg.at<uint16_t>(ow), eps, T))) return st;
+    GW_CUDA(cudaMemcpyAsync(stream, sg.at<float>(os), ns, cudaMemcpyDeviceToHost, c->cur));
+    if (experts_out)
+        GW_CUDA(cudaMemcpyAsync(experts_out, c->w.experts, nk * 4, cudaMemcpyDeviceToHost, c->cur));
+    if (weights_out)
+        GW_CUDA(cudaMemcpyAsync(weights_out, c->w.weights, nk * 4, cudaMemcpyDeviceToHost, c->cur));
+    GW_CUDA(cudaStreamSynchronize(c->cur));
+    return GW_OK;
 }
 
 // GEMV over `count` matrices (device pointers).

@@ -89,6 +89,10 @@ int launch_residual_round(float* stream, const float* delta, void* x_out, int x_
                           int64_t n, cudaStream_t s);
 int launch_xprep(const void* x, int x_dtype, int T, int H, __half* x16, float* xmul,
                  cudaStream_t s);
+// out[T][H] f16 = RMSNorm(stream[T][H] fp32) with bf16 weight[H]; H % 4 == 0,
+// 16-byte aligned rows.
+int launch_rmsnorm(const float* stream, const uint16_t* weight, float eps, int T, int H, __half* out,
+                   cudaStream_t s);
 // Reference row-major <-> tiled bank layout of one MXFP4 matrix's packed
 // blocks (scales = 0) or scale bytes (scales = 1).
 int launch_tile_layout(const uint8_t* src, uint8_t* dst, int rows, int cols, int scales,

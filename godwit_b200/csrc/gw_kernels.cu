@@ -219,6 +219,53 @@ __global__ void __launch_bounds__(128) k_router(LayerView L, MoeDims d, const vo
     }
 }
 
+// k_rmsnorm: the post-attention RMSNorm ahead of the router,
+// out[t][i] = f16((stream[t][i] * inv) * w[i]), inv = 1 / sqrt(sum_i stream[t][i]^2 / H + eps),
+// as TransformerLayer.normalise (Runtime/TransformerLayer.swift:265-285) and
+// the Metal `rmsnorm` (Metal/MoE/router.metal:41-60) compute it: fp32 squares
+// and sums, a plain multiplicative bf16 weight, IEEE division and square
+// root, f16 output rounded to nearest even.  The reference sums the squares
+// in index order; this kernel sums them as a tree (per-thread runs, then the
+// warps), so `inv` can differ in its last bit and an output by one f16 ulp.
+// grid T, 256 threads; H a multiple of 4.
+__global__ void __launch_bounds__(256) k_rmsnorm(const float* __restrict__ stream,
+                                                 const uint16_t* __restrict__ weight, float eps, int H,
+                                                 __half* __restrict__ out) {
+    const float* row = stream + (int64_t)blockIdx.x * H;
+    __half* orow = out + (int64_t)blockIdx.x * H;
+    float ss = 0.f;
+    for (int i = threadIdx.x * 4; i < H; i += blockDim.x * 4) {
+        const float4 v = *reinterpret_cast<const float4*>(row + i);
+        ss = __fadd_rn(ss, __fmul_rn(v.x, v.x));
+        ss = __fadd_rn(ss, __fmul_rn(v.y, v.y));
+        ss = __fadd_rn(ss, __fmul_rn(v.z, v.z));
+        ss = __fadd_rn(ss, __fmul_rn(v.w, v.w));
+    }
+    ss = warp_sum(ss);
+    __shared__ float part[8];
+    __shared__ float inv;
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float tot = 0.f;
+        for (int j = 0; j < (int)(blockDim.x >> 5); ++j) tot = __fadd_rn(tot, part[j]);
+        inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)H), eps)));
+    }
+    __syncthreads();
+    const float r = inv;
+    for (int i = threadIdx.x * 4; i < H; i += blockDim.x * 4) {
+        const float4 v = *reinterpret_cast<const float4*>(row + i);
+        const uint2 wb = *reinterpret_cast<const uint2*>(weight + i);
+        const float w0 = __uint_as_float(wb.x << 16), w1 = __uint_as_float(wb.x & 0xffff0000u);
+        const float w2 = __uint_as_float(wb.y << 16), w3 = __uint_as_float(wb.y & 0xffff0000u);
+        __half2* o = reinterpret_cast<__half2*>(orow + i);
+        o[0] = __halves2half2(__float2half_rn(__fmul_rn(__fmul_rn(v.x, r), w0)),
+                              __float2half_rn(__fmul_rn(__fmul_rn(v.y, r), w1)));
+        o[1] = __halves2half2(__float2half_rn(__fmul_rn(__fmul_rn(v.z, r), w2)),
+                              __float2half_rn(__fmul_rn(__fmul_rn(v.w, r), w3)));
+    }
+}
+
 // k_xprep: x row -> f16 with the row's shift (see row_exponent_shift);
 // grid (rows), one CTA per row, row m at x + m * x_stride elements.
 __global__ void k_xprep(const void* __restrict__ x, int64_t x_stride, int x_dtype, int cols,
@@ -780,6 +827,12 @@ int launch_combine(const MoeDims& d, int T, const MoeWork& w, float* out, int ac
                    void* x_next, int x_dtype, cudaStream_t s) {
     dim3 grid((d.H / 4 + 255) / 256, T);
     k_combine<<<grid, 256, 0, s>>>(d, w, out, accumulate, x_next, x_dtype);
+    return ok_or_fail();
+}
+
+int launch_rmsnorm(const float* stream, const uint16_t* weight, float eps, int T, int H, __half* out,
+                  cudaStream_t s) {
+    k_rmsnorm<<<T, 256, 0, s>>>(stream, weight, eps, H, out);
     return ok_or_fail();
 }
 

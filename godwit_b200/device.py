@@ -88,3 +88,18 @@ def residual_round(ctx: Context, stream: torch.Tensor, delta: torch.Tensor | Non
                    x_out: torch.Tensor | None) -> None:
     call("gw_residual_round_async", ctx.handle, _p(stream), _p(delta), _p(x_out),
          GW_DTYPE_BF16 if x_out is None else dtype_code(x_out), stream.numel())
+
+
+def rmsnorm(ctx: Context, stream: torch.Tensor, weight_bits: torch.Tensor, eps: float,
+            out: torch.Tensor) -> None:
+    """out [T, H] f16 = RMSNorm(stream [T, H] fp32) with the bf16 weight (int16/uint16 bits or bfloat16)."""
+    T, H = stream.shape
+    call("gw_rmsnorm_async", ctx.handle, _p(stream), _p(weight_bits), float(eps), T, H, _p(out))
+
+
+def moe_block(ctx: Context, bank: ExpertBank, layer: int, stream: torch.Tensor, norm_weight: torch.Tensor,
+              eps: float, experts: torch.Tensor | None = None, weights: torch.Tensor | None = None) -> None:
+    """The MoE half of a transformer layer on device tensors: stream [T, H] fp32
+    += MoE(RMSNorm(stream)) in place (norm_weight: bf16 bits [H])."""
+    call("gw_moe_block_async", ctx.handle, bank.handle, layer, _p(stream), _p(norm_weight), float(eps),
+         stream.shape[0], _p(experts), _p(weights))

@@ -318,3 +318,21 @@ class MoEBlock:
         call("gw_moe_forward", self.ctx.handle, self.bank.handle, layer, _ptr(xb),
              _dtype_code(dtype), T, _ptr(ein), _ptr(win), _ptr(out), _ptr(ex), _ptr(wt))
         return out, ex, wt
+
+    def block(self, stream: np.ndarray, layer: int, norm_weight_bits: np.ndarray, eps: float):
+        """The MoE half of TransformerLayer.forward (Runtime/TransformerLayer.swift:140-238):
+        RMSNorm of the fp32 residual `stream` [T, H] with the layer's bf16 post-attention
+        norm weight (raw uint16 bits, [H]), routing and experts on the f16 result, and
+        the weighted expert sum added into the stream.  Returns (new stream, experts,
+        weights); the argument is not modified."""
+        H, k = self.bank.spec.hidden, self.bank.spec.top_k
+        st = np.array(stream, dtype=np.float32, order="C", copy=True).reshape(-1, H)
+        nw = np.ascontiguousarray(norm_weight_bits, dtype=np.uint16)
+        if nw.size != H:
+            raise GodwitCUDAError(_abi.GW_E_ARG, f"norm weight has {nw.size} values, expected {H}")
+        T = st.shape[0]
+        ex = np.empty((T, k), dtype=np.int32)
+        wt = np.empty((T, k), dtype=np.float32)
+        call("gw_moe_block", self.ctx.handle, self.bank.handle, layer, _ptr(st), _ptr(nw),
+             float(eps), T, _ptr(ex), _ptr(wt))
+        return st, ex, wt

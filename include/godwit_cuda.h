@@ -242,6 +242,29 @@ GW_API gw_status gw_moe_apply_async(gw_ctx* ctx, gw_bank* bank, int32_t layer,
  * residual add of TransformerLayer.forward (Runtime/TransformerLayer.swift:232-238). */
 GW_API gw_status gw_residual_round_async(gw_ctx* ctx, float* stream_dev, const float* delta_dev,
                                   void* x_out_dev, int32_t x_dtype, int64_t n);
+/* RMSNorm ahead of the router (TransformerLayer.normalise,
+ * Runtime/TransformerLayer.swift:265-285; Metal `rmsnorm`, Metal/MoE/router.metal:41-60):
+ * out_dev[T, H] f16 = stream_dev[t, i] * (1 / sqrt(mean_i(stream_dev[t, i]^2) + eps)) * w[i],
+ * fp32 arithmetic, bf16 weight [H].  The squares are summed as a tree, not in
+ * index order, so an output can differ from the reference's by one f16 ulp.
+ * H % 4 == 0; stream_dev 16-byte, weight_dev and out_dev 8-byte aligned. */
+GW_API gw_status gw_rmsnorm_async(gw_ctx* ctx, const float* stream_dev, const uint16_t* weight_dev,
+                                  float eps, int32_t T, int32_t H, void* out_dev);
+/* The MoE half of TransformerLayer.forward (Runtime/TransformerLayer.swift:140-238)
+ * on the device, with no host round trip between its steps: normed =
+ * RMSNorm(stream, norm_w, eps) (the post-attention norm, :141-143), routing
+ * and the experts on normed (as gw_moe_forward), then stream += the weighted
+ * expert sum (:232-238).  stream [T, H] fp32 is updated in place; norm_w is
+ * the layer's bf16 post-attention norm weight [H].  experts/weights: optional
+ * [T, k] routing outputs.  gw_moe_block takes host pointers and returns when
+ * done; gw_moe_block_async takes device pointers (stream 16-byte, norm_w
+ * 8-byte aligned) and is ordered on the context's stream. */
+GW_API gw_status gw_moe_block(gw_ctx* ctx, gw_bank* bank, int32_t layer, float* stream,
+                              const uint16_t* norm_w, float eps, int32_t T, int32_t* experts_out,
+                              float* weights_out);
+GW_API gw_status gw_moe_block_async(gw_ctx* ctx, gw_bank* bank, int32_t layer, float* stream_dev,
+                                    const uint16_t* norm_w_dev, float eps, int32_t T,
+                                    int32_t* experts_dev, float* weights_dev);
 /* One MoE layer that allocates no device memory, for callers that cannot
  * allocate while serving (memory planned up front, a hard memory cap, or no
  * tolerance for a first-call allocation).  No counterpart in the reference.

@@ -334,6 +334,29 @@ def moe_layer64_mx(spec, strides: np.ndarray, x: np.ndarray, experts: np.ndarray
     return out
 
 
+def rmsnorm(stream: np.ndarray, weight_bits: np.ndarray, eps: float) -> np.ndarray:
+    """TransformerLayer.normalise (Runtime/TransformerLayer.swift:265-285): per token,
+    sumSquares accumulated in index order in fp32 (value * value, then +=),
+    inverse = 1 / sqrt(sumSquares / width + eps) in fp32, out = Float16(value *
+    inverse * bf16(weight)).  stream fp32 [T, H], weight_bits uint16 [H] -> f16 [T, H]."""
+    x = np.asarray(stream, dtype=np.float32)
+    x = x.reshape(-1, x.shape[-1])
+    H = x.shape[1]
+    w = (np.asarray(weight_bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+    # np.cumsum over float32 adds strictly left to right (no pairwise blocking)
+    ss = np.cumsum(x * x, axis=1, dtype=np.float32)[:, -1]
+    inv = np.float32(1) / np.sqrt(ss / np.float32(H) + np.float32(eps))
+    return ((x * inv[:, None]) * w[None, :]).astype(np.float16)
+
+
+def moe_block64(spec, strides: np.ndarray, stream: np.ndarray, normed: np.ndarray,
+                experts: np.ndarray, weights: np.ndarray) -> np.ndarray:
+    """The MoE half of TransformerLayer.forward (:140-238) in fp64 given the
+    normed f16 input and the routing: stream + moe_layer64(normed)."""
+    return np.asarray(stream, dtype=np.float64) + moe_layer64(spec, strides, normed.astype(np.float64),
+                                                              experts, weights)
+
+
 def rel_l2(a, b) -> float:
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
