@@ -92,6 +92,7 @@ SIGNATURES = {
     "gw_residual_round_async": (ST, [P, P, P, P, I32, I64]),
     "gw_last_launch_count": (ST, [P, C.POINTER(I64)]),
     "gw_rmsnorm_async": (ST, [P, P, P, C.c_float, I32, I32, P]),
+    "gw_route_async": (ST, [P, P, I32, P, I32, I32, P, P]),
     "gw_moe_block": (ST, [P, P, I32, P, P, C.c_float, I32, P, P]),
     "gw_moe_block_async": (ST, [P, P, I32, P, P, C.c_float, I32, P, P]),
 }

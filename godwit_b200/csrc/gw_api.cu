@@ -1090,6 +1090,30 @@ gw_status gw_router_logits(gw_ctx* c, gw_bank* b, int32_t layer, const void* x, 
     return GW_OK;
 }
 
+gw_status gw_route_async(gw_ctx* c, gw_bank* b, int32_t layer, const void* x_dev, int32_t x_dtype,
+                         int32_t T, int32_t* experts_dev, float* weights_dev) {
+    if (!c || !x_dev || !experts_dev || !weights_dev) return fail(GW_E_ARG, "null argument");
+    gw_status st = check_bank(b, layer);
+    if (st || (st = check_dtype(x_dtype))) return st;
+    if (T <= 0) return fail(GW_E_ARG, "T must be positive");
+    CtxLock lk(c);
+    if ((st = set_device(c))) return st;
+    if ((st = ensure_work(c, b, T))) return st;
+    const gw::MoeDims d = dims_of(b);
+    if ((st = timed_launch(c, 3, 0, [&] {
+             return gw::launch_router(layer_of(b, layer), d, x_dev, x_dtype, T, c->w, c->cur);
+         })))
+        return st;
+    // the router also grouped the slots for the expert kernels: leave the
+    // counts at zero for the next layer call, as the combine would
+    GW_CUDA(cudaMemsetAsync(c->w.counts, 0, (size_t)d.E * 4, c->cur));
+    GW_CUDA(cudaMemsetAsync(c->w.nactive, 0, 4, c->cur));
+    const size_t nk = (size_t)T * d.k;
+    GW_CUDA(cudaMemcpyAsync(experts_dev, c->w.experts, nk * 4, cudaMemcpyDeviceToDevice, c->cur));
+    GW_CUDA(cudaMemcpyAsync(weights_dev, c->w.weights, nk * 4, cudaMemcpyDeviceToDevice, c->cur));
+    return GW_OK;
+}
+
 gw_status gw_route(gw_ctx* c, gw_bank* b, int32_t layer, const void* x, int32_t x_dtype, int32_t T,
                    int32_t* experts_out, float* weights_out) {
     if (!c || !x || !experts_out || !weights_out) return fail(GW_E_ARG, "null argument");

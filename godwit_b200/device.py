@@ -103,3 +103,10 @@ def moe_block(ctx: Context, bank: ExpertBank, layer: int, stream: torch.Tensor, 
     += MoE(RMSNorm(stream)) in place (norm_weight: bf16 bits [H])."""
     call("gw_moe_block_async", ctx.handle, bank.handle, layer, _p(stream), _p(norm_weight), float(eps),
          stream.shape[0], _p(experts), _p(weights))
+
+
+def route(ctx: Context, bank: ExpertBank, layer: int, x: torch.Tensor, experts: torch.Tensor,
+          weights: torch.Tensor) -> None:
+    """experts [T, k] int32, weights [T, k] fp32 = the router's decision for x [T, H]."""
+    call("gw_route_async", ctx.handle, bank.handle, layer, _p(x), dtype_code(x), x.shape[0], _p(experts),
+         _p(weights))

@@ -218,6 +218,12 @@ GW_API gw_status gw_mxfp4_gemv_batched_async(gw_ctx* ctx, int32_t count,
                                       const void* x, int64_t x_stride, int32_t x_dtype,
                                       float* y, int64_t y_stride,
                                       int32_t rows, int32_t cols);
+/* Router.route (Runtime/Router.swift:100-104) on device memory: x_dev [T, H]
+ * -> experts_dev [T, k] int32, weights_dev [T, k] fp32, ordered on the
+ * context's stream (gw_route's device twin; used by the all-to-all expert
+ * parallelism to route a rank's own tokens before dispatching them). */
+GW_API gw_status gw_route_async(gw_ctx* ctx, gw_bank* bank, int32_t layer, const void* x_dev,
+                                int32_t x_dtype, int32_t T, int32_t* experts_dev, float* weights_dev);
 /* One MoE layer on device memory: x_dev [T, H] (x_dtype), out_dev [T, H] fp32.
  * experts_dev/weights_dev: optional [T, k] outputs of the routing decision. */
 GW_API gw_status gw_moe_forward_async(gw_ctx* ctx, gw_bank* bank, int32_t layer,

@@ -1,0 +1,100 @@
+"""All-to-all expert parallelism (godwit_b200/ep.py AllToAllEP) on CPU gloo
+ranks: each rank holds a slice of the tokens, routes them, sends every
+(token, slot) row to the owner of the slot's expert (e % world), applies the
+experts there and returns the weighted outputs, which are summed in slot
+order.  The per-rank compute is an elementwise stand-in (router = top-k of
+the first E features, expert e = w * tanh((e + 1 + layer) x)), so the
+multi-rank stack must equal the one-rank stack exactly; the stand-in also
+checks that every row arrives at the rank owning its expert."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+H, E, K, LAYERS = 48, 10, 3, 3
+T_TOTAL = 13
+
+
+class ToyOps:
+    def __init__(self, rank, world):
+        self.rank, self.world = rank, world
+
+    def widen(self, x, stream):
+        stream.copy_(x.float())
+
+    def residual(self, stream, delta, x_out):
+        stream.add_(delta)
+        x_out.copy_(stream.to(torch.bfloat16))
+
+    def route(self, layer, x):
+        logits = x.float()[:, :E]
+        top = torch.topk(logits, K, dim=1)
+        return top.indices.to(torch.int32), torch.softmax(top.values, dim=1).to(torch.float32)
+
+    def apply_rows(self, layer, rows, experts, weights, out):
+        assert bool(((experts.to(torch.int64) % self.world) == self.rank).all()), "row sent to a non-owner"
+        out.copy_(weights[:, None] * torch.tanh(rows.float() * (experts[:, None].float() + 1 + layer)))
+
+
+def make_x():
+    g = torch.Generator().manual_seed(11)
+    return torch.randn(T_TOTAL, H, generator=g).to(torch.bfloat16)
+
+
+def slice_of(rank, world):
+    per = -(-T_TOTAL // world)
+    return slice(rank * per, min(T_TOTAL, (rank + 1) * per))
+
+
+def run(rank, world):
+    from godwit_b200.ep import AllToAllEP
+    x = make_x()[slice_of(rank, world)].contiguous()
+    stream = torch.empty(x.shape[0], H)
+    x_work = torch.empty_like(x)
+    return AllToAllEP(ToyOps(rank, world), LAYERS, K).forward(x, stream, x_work).numpy()
+
+
+def _worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        np.save(os.path.join(out_dir, f"r{rank}.npy"), run(rank, world))
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_alltoall_ranks_match_one_rank(tmp_path, world):
+    ref = run(0, 1)
+    mp.spawn(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    got = np.concatenate([np.load(tmp_path / f"r{r}.npy") for r in range(world)])
+    assert got.shape == ref.shape
+    assert np.array_equal(got, ref)
+
+
+def test_one_rank_matches_direct_sum():
+    """The single-rank path (no process group) against the layer written out
+    directly: stream += sum_j w_j expert_{e_j}(round(stream)) in slot order."""
+    ops = ToyOps(0, 1)
+    x = make_x()
+    stream = x.float().clone()
+    xw = x.clone()
+    for layer in range(LAYERS):
+        ex, wt = ops.route(layer, xw)
+        acc = None
+        for j in range(K):
+            y = wt[:, j:j + 1] * torch.tanh(xw.float() * (ex[:, j:j + 1].float() + 1 + layer))
+            acc = y if acc is None else acc + y
+        stream += acc
+        xw = stream.to(torch.bfloat16)
+    assert np.array_equal(run(0, 1), stream.numpy())
