@@ -177,6 +177,17 @@ class CpuReference:
                 f"scaled to the stack; {dt:.2f} s on {self.threads} threads")
 
 
+def profiled_traffic(workload: str):
+    """`profiles/traffic.json`'s entry for the workload (DRAM bytes per launch
+    of its dominant kernel, read off an ncu capture), or None."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f).get(workload)
+    except (OSError, ValueError):
+        return None
+
+
 def cpu_reference_sample(spec, threads: int, budget_s: float = 12.0):
     ref = CpuReference(spec, threads)
     ref.calibrate(budget_s)
@@ -462,6 +473,11 @@ def run_decode(args):
                     "achieved": achieved, "peak": peak, "unit": "GB/s",
                     "frac": (achieved / peak) if achieved else None,
                     "peak_kind": peak_kind, "traffic": None}
+        tr = profiled_traffic(args.workload) if not args.layers else None
+        if tr:  # DRAM bytes of one launch of the dominant kernel, from a committed ncu capture
+            roofline.update({"traffic": tr["dram_bytes_per_launch"], "traffic_kernel": tr["kernel"],
+                             "traffic_alg_bytes": tr["alg_bytes_per_launch_approx"],
+                             "traffic_source": tr["source"]})
     roofline.update({"alg_bytes_per_step": step_bytes_total,
                      "expert_passes_per_step": prof["expert_passes"] / prof_steps,
                      "expert_ms_per_step": expert_ms / prof_steps,
