@@ -131,28 +131,29 @@ __device__ __forceinline__ void prep_block(const void* x, int x_dtype, int H, in
     else x16[i] = __float2half_rn(bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(x)[i]) * pow2f(p));
 }
 
-// k_router: grid (ceil(E/4), ceil(T/8)), 4 warps; warp w scores expert
-// 4*blockIdx.x + w against the CTA's (up to) 8 tokens, and the CTA converts
-// its share of those tokens' x blocks for the expert GEMVs.  Each CTA then
-// counts itself done on its token chunk's counter; the last CTA of a chunk
-// selects the top-k of the chunk's tokens and adds their slots to the expert
-// lists (whose counts the previous combine left at zero).
+// k_router: grid (E, ceil(T/8)), 4 warps; CTA (e, y) scores expert e against
+// the chunk's (up to) 8 tokens, warp w taking the w-th quarter of the hidden
+// dimension (three 16-byte rounds per lane at H = 2880), and the four partial
+// sums meet in a fixed order.  The CTA also converts its share of those
+// tokens' x blocks for the expert GEMVs.  Each CTA then counts itself done on
+// its token chunk's counter; the last CTA of a chunk selects the top-k of the
+// chunk's tokens and adds their slots to the expert lists (whose counts the
+// previous combine left at zero).
 __global__ void __launch_bounds__(128) k_router(LayerView L, MoeDims d, const void* __restrict__ xr,
                                                 int x_dtype, int T, MoeWork w) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int e = blockIdx.x * 4 + warp;
+    const int e = blockIdx.x;
     const int t0 = blockIdx.y * kTokTile;
     const int t1 = min(T, t0 + kTokTile);
-    // every warp streams the chunk's x rows (for its expert's dot products,
-    // or only for the row maxima when the CTA has fewer than 4 experts left)
-    const bool has_e = e < d.E;
-    const uint4* wrow = reinterpret_cast<const uint4*>(L.router_w + (int64_t)(has_e ? e : 0) * d.H);
+    const uint4* wrow = reinterpret_cast<const uint4*>(L.router_w + (int64_t)e * d.H);
     const int nchunk = d.H >> 3;
+    const int per = (nchunk + 3) >> 2;
+    const int c0 = warp * per, c1 = min(nchunk, c0 + per);
     float acc[kTokTile], mx[kTokTile];
 #pragma unroll
     for (int q = 0; q < kTokTile; ++q) acc[q] = mx[q] = 0.f;
-    for (int c = lane; c < nchunk; c += 32) {
-        const uint4 wv = has_e ? __ldg(wrow + c) : make_uint4(0u, 0u, 0u, 0u);
+    for (int c = c0 + lane; c < c1; c += 32) {
+        const uint4 wv = __ldg(wrow + c);
         const uint32_t wr[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
         for (int q = 0; q < kTokTile; ++q) {
@@ -177,21 +178,24 @@ __global__ void __launch_bounds__(128) k_router(LayerView L, MoeDims d, const vo
             }
         }
     }
+    __shared__ float racc[4][kTokTile], rmx[4][kTokTile];
     __shared__ int shift[kTokTile];
-    {
-        const float bias = (has_e && L.router_b) ? bf16_bits_to_f32(L.router_b[e]) : 0.f;
 #pragma unroll
-        for (int q = 0; q < kTokTile; ++q) {
-            if (t0 + q >= t1) break;
-            const float v = warp_sum(acc[q]);
-            const float m = warp_max(mx[q]);
-            if (lane == 0 && has_e) w.logits[(int64_t)(t0 + q) * d.E + e] = v + bias;
-            if (lane == 0 && warp == 0) {
-                const int p = x_dtype == kBF16 ? row_exponent_shift(m) : 0;
-                shift[q] = p;
-                if (blockIdx.x == 0) w.xmul[t0 + q] = pow2f(-p);
-            }
-        }
+    for (int q = 0; q < kTokTile; ++q) {
+        const float v = warp_sum(acc[q]);
+        const float m = warp_max(mx[q]);
+        if (lane == 0) { racc[warp][q] = v; rmx[warp][q] = m; }
+    }
+    __syncthreads();
+    if (warp == 0 && lane < kTokTile && t0 + lane < t1) {
+        const int q = lane;
+        const float bias = L.router_b ? bf16_bits_to_f32(L.router_b[e]) : 0.f;
+        const float v = ((racc[0][q] + racc[1][q]) + racc[2][q]) + racc[3][q];
+        const float m = fmaxf(fmaxf(rmx[0][q], rmx[1][q]), fmaxf(rmx[2][q], rmx[3][q]));
+        w.logits[(int64_t)(t0 + q) * d.E + e] = v + bias;
+        const int p = x_dtype == kBF16 ? row_exponent_shift(m) : 0;
+        shift[q] = p;
+        if (blockIdx.x == 0) w.xmul[t0 + q] = pow2f(-p);
     }
     __syncthreads();
     // this CTA's share of the chunk's x blocks
@@ -787,7 +791,7 @@ int launch_router(const LayerView& L, const MoeDims& d, const void* x, int x_dty
         k_router_mma<<<(T + 15) / 16, 128, 0, s>>>(L, d, static_cast<const uint16_t*>(x), T, w);
         return ok_or_fail();
     }
-    dim3 grid((d.E + 3) / 4, (T + kTokTile - 1) / kTokTile);
+    dim3 grid(d.E, (T + kTokTile - 1) / kTokTile);
     k_router<<<grid, 128, 0, s>>>(L, d, x, x_dtype, T, w);
     return ok_or_fail();
 }
