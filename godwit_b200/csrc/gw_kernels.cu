@@ -131,15 +131,17 @@ __device__ __forceinline__ void prep_block(const void* x, int x_dtype, int H, in
     else x16[i] = __float2half_rn(bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(x)[i]) * pow2f(p));
 }
 
-// k_router: grid (E, ceil(T/8)), 4 warps; CTA (e, y) scores expert e against
-// the chunk's (up to) 8 tokens, warp w taking the w-th quarter of the hidden
-// dimension (three 16-byte rounds per lane at H = 2880), and the four partial
-// sums meet in a fixed order.  The CTA also converts its share of those
+// k_router: grid (E, ceil(T/8)), kRouterWarps warps (16 for a single token
+// chunk, where the grid is only E CTAs; 4 otherwise — both measured best on
+// B200); CTA (e, y) scores expert e against the chunk's (up to) 8 tokens,
+// warp w taking the w-th 1/kRouterWarps of the hidden dimension, and the
+// partial sums meet in a fixed order.  The CTA also converts its share of those
 // tokens' x blocks for the expert GEMVs.  Each CTA then counts itself done on
 // its token chunk's counter; the last CTA of a chunk selects the top-k of the
 // chunk's tokens and adds their slots to the expert lists (whose counts the
 // previous combine left at zero).
-__global__ void __launch_bounds__(128) k_router(LayerView L, MoeDims d, const void* __restrict__ xr,
+template <int kRouterWarps>
+__global__ void __launch_bounds__(kRouterWarps * 32) k_router(LayerView L, MoeDims d, const void* __restrict__ xr,
                                                 int x_dtype, int T, MoeWork w) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int e = blockIdx.x;
@@ -147,7 +149,7 @@ __global__ void __launch_bounds__(128) k_router(LayerView L, MoeDims d, const vo
     const int t1 = min(T, t0 + kTokTile);
     const uint4* wrow = reinterpret_cast<const uint4*>(L.router_w + (int64_t)e * d.H);
     const int nchunk = d.H >> 3;
-    const int per = (nchunk + 3) >> 2;
+    const int per = (nchunk + kRouterWarps - 1) / kRouterWarps;
     const int c0 = warp * per, c1 = min(nchunk, c0 + per);
     float acc[kTokTile], mx[kTokTile];
 #pragma unroll
@@ -178,7 +180,7 @@ __global__ void __launch_bounds__(128) k_router(LayerView L, MoeDims d, const vo
             }
         }
     }
-    __shared__ float racc[4][kTokTile], rmx[4][kTokTile];
+    __shared__ float racc[kRouterWarps][kTokTile], rmx[kRouterWarps][kTokTile];
     __shared__ int shift[kTokTile];
 #pragma unroll
     for (int q = 0; q < kTokTile; ++q) {
@@ -190,8 +192,12 @@ __global__ void __launch_bounds__(128) k_router(LayerView L, MoeDims d, const vo
     if (warp == 0 && lane < kTokTile && t0 + lane < t1) {
         const int q = lane;
         const float bias = L.router_b ? bf16_bits_to_f32(L.router_b[e]) : 0.f;
-        const float v = ((racc[0][q] + racc[1][q]) + racc[2][q]) + racc[3][q];
-        const float m = fmaxf(fmaxf(rmx[0][q], rmx[1][q]), fmaxf(rmx[2][q], rmx[3][q]));
+        float v = racc[0][q], m = rmx[0][q];
+#pragma unroll
+        for (int j = 1; j < kRouterWarps; ++j) {
+            v += racc[j][q];
+            m = fmaxf(m, rmx[j][q]);
+        }
         w.logits[(int64_t)(t0 + q) * d.E + e] = v + bias;
         const int p = x_dtype == kBF16 ? row_exponent_shift(m) : 0;
         shift[q] = p;
@@ -200,12 +206,12 @@ __global__ void __launch_bounds__(128) k_router(LayerView L, MoeDims d, const vo
     __syncthreads();
     // this CTA's share of the chunk's x blocks
     const int nblk = d.H >> 5;
-    for (int task = blockIdx.x * 4 + warp; task < (t1 - t0) * nblk; task += gridDim.x * 4)
+    for (int task = blockIdx.x * kRouterWarps + warp; task < (t1 - t0) * nblk; task += gridDim.x * kRouterWarps)
         prep_block(xr, x_dtype, d.H, t0 + task / nblk, task % nblk, shift[task / nblk], w.x16);
 
     __shared__ int last;
-    __shared__ int ord[4][kMaxExperts];
-    __shared__ float lgc[4][kMaxExperts];
+    __shared__ int ord[kRouterWarps][kMaxExperts];
+    __shared__ float lgc[kRouterWarps][kMaxExperts];
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
@@ -216,7 +222,7 @@ __global__ void __launch_bounds__(128) k_router(LayerView L, MoeDims d, const vo
     if (!last) return;
     __threadfence();
     if (threadIdx.x == 0) w.done[blockIdx.y] = 0u;
-    for (int t = t0 + warp; t < t1; t += 4) {
+    for (int t = t0 + warp; t < t1; t += kRouterWarps) {
         select_topk_warp(w.logits + (int64_t)t * d.E, d.E, d.k, ord[warp], lgc[warp],
                          w.experts + (int64_t)t * d.k, w.weights + (int64_t)t * d.k);
         if (lane < d.k) group_slot(d, w, __ldcg(w.experts + (int64_t)t * d.k + lane), t * d.k + lane);
@@ -792,7 +798,8 @@ int launch_router(const LayerView& L, const MoeDims& d, const void* x, int x_dty
         return ok_or_fail();
     }
     dim3 grid(d.E, (T + kTokTile - 1) / kTokTile);
-    k_router<<<grid, 128, 0, s>>>(L, d, x, x_dtype, T, w);
+    if (T <= kTokTile) k_router<16><<<grid, 16 * 32, 0, s>>>(L, d, x, x_dtype, T, w);
+    else k_router<4><<<grid, 4 * 32, 0, s>>>(L, d, x, x_dtype, T, w);
     return ok_or_fail();
 }
 
