@@ -73,9 +73,14 @@ constexpr int kGroupPk = 8 * kTileRun;    // 16 KB of MXFP4 blocks per group
 constexpr int kGroupSc = 8 * 16 * 8;      // 1 KB of scale bytes per group
 constexpr int kRingBytes = kStages * kBSlot;
 constexpr int kGroupOff = kRingBytes;
-constexpr int kTsfOff = kGroupOff + kGroups * (kGroupPk + kGroupSc);  // block-scaled: token scale words
-constexpr int kTsfSlot = kNMax * 4;                                   // 128 tokens x one word per stage
-constexpr int kDynSmem = kTsfOff + kStages * kTsfSlot + 1024;         // + alignment slack
+// Block-scaled scale words staged for tcgen05.cp, per stage: the tokens' as
+// 32 rows x 16 bytes (row r = tokens r, 32 + r, 64 + r, 96 + r), the weight
+// rows' as 128 rows x 16 bytes (the row's word four times).
+constexpr int kTsfOff = kGroupOff + kGroups * (kGroupPk + kGroupSc);
+constexpr int kTsfSlot = kNMax * 4;
+constexpr int kSfaOff = kTsfOff + kStages * kTsfSlot;
+constexpr int kSfaSlot = kM * 16;
+constexpr int kDynSmem = kSfaOff + kStages * kSfaSlot + 1024;         // + alignment slack
 constexpr int kThreads = 15 * 32;
 constexpr int kTmemCols = 512;            // accumulators 2 x kNMax, then the weight ring
 constexpr int kAColBase = 2 * kNMax;
@@ -173,13 +178,15 @@ __device__ __forceinline__ void tc_mma_mx(uint32_t tmem, uint64_t ad, uint64_t b
         "l"(ad), "l"(bd), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
         : "memory");
 }
-__device__ __forceinline__ void tmem_st1(uint32_t taddr, uint32_t v) {
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(v) : "memory");
+// Shared -> TMEM copies of the block-scaled mode's scale words, issued by the
+// MMA thread ahead of the stage's MMAs (the tensor pipe keeps them in order):
+// 128 rows x 16 bytes to lanes 0-127, and 32 rows x 16 bytes to lanes 0-31 of
+// every lane quarter.
+__device__ __forceinline__ void tc_cp_128x128b(uint32_t taddr, uint64_t sdesc) {
+    asm volatile("tcgen05.cp.cta_group::1.128x128b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
 }
-__device__ __forceinline__ void tmem_st4(uint32_t taddr, uint32_t v0, uint32_t v1, uint32_t v2, uint32_t v3) {
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr), "r"(v0), "r"(v1),
-                 "r"(v2), "r"(v3)
-                 : "memory");
+__device__ __forceinline__ void tc_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
+    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
 }
 // 32 consecutive 32-bit TMEM columns of this thread's lane.
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
@@ -245,7 +252,6 @@ __device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
 
 struct Shared {
     uint64_t full[kStages], empty[kStages], gfull[kGroups], gempty[kGroups], tfull[2], tempty[2], fin;
-    uint64_t tsf[kStages];  // block-scaled: the stage's token scale words are in shared memory
     uint32_t tmem;
     int abort;
     int nact, nitems, chunks, mt;
@@ -548,19 +554,16 @@ __device__ __forceinline__ void role_mma(Shared& sh, const GroupedArgs& a, char*
 // r = m0 + (c & 127) and blocks 2h, 2h + 1 of each stage (h = c >> 7).  It
 // copies them from the group ring into the MMA's unpacked e2m1 layout (each
 // 16-value half block = 8 bytes of codes + 8 bytes of zeros, canonical
-// K-major core matrices of 8 rows x 16 bytes); the h = 0 threads write the
-// row's four block scales as one TMEM word (lane r, column sfa + r / 32), and
-// the h = 1 warps — one per TMEM lane quarter — copy the chunk's token scale
-// words into their quarter (lane n % 32, column sfb + n / 32: every quarter
-// holds the whole token scale vector).
+// K-major core matrices of 8 rows x 16 bytes); the h = 0 threads stage the
+// row's four block scales (one word) in the stage's scale slot, which the MMA
+// thread copies into TMEM (lane r, column sfa + r / 32) with tcgen05.cp.
 __device__ __forceinline__ void role_unpack(Shared& sh, const GroupedArgs& a, char* smem) {
     const int c = threadIdx.x;
-    const int r = c & (kM - 1), h = c >> 7, lane = c & 31, warp = c >> 5;
+    const int r = c & (kM - 1), h = c >> 7, lane = c & 31;
     const int lr = r & 15, tile = r >> 4;
     const int nblk = a.K >> 5, ngrp = (nblk + 7) >> 3;
     unsigned* status = a.w.status;
     const char* ring = smem + kGroupOff;
-    const uint32_t tlane = (uint32_t)((warp & 3) * 32) << 16;
     int g = 0, gq = 0;
     bool ok = true;
     for (int it = blockIdx.x; ok && it < sh.nitems; it += gridDim.x) {
@@ -603,15 +606,9 @@ __device__ __forceinline__ void role_unpack(Shared& sh, const GroupedArgs& a, ch
                     fence_async_smem();
                 }
                 if (h == 0) {
-                    tmem_st1(sh.tmem + tlane + kMxSfa + slot * 4 + (warp & 3), sfw);
-                } else {  // token scale words of the stage (tokens 32j + lane), staged by the token warp
-                    if (!warp_wait(&sh.abort, &sh.tsf[slot], (g / kStages) & 1, status, 4u)) { ok = false; break; }
-                    const uint32_t* tsf = reinterpret_cast<const uint32_t*>(smem + kTsfOff + slot * kTsfSlot);
-                    tmem_st4(sh.tmem + tlane + kMxSfb + slot * 4, tsf[lane], tsf[32 + lane], tsf[64 + lane],
-                             tsf[96 + lane]);
+                    *reinterpret_cast<uint4*>(smem + kSfaOff + slot * kSfaSlot + r * 16) = make_uint4(sfw, sfw, sfw, sfw);
+                    fence_async_smem();
                 }
-                tmem_st_wait();
-                tc_before_sync();
                 __syncwarp();
                 if (lane == 0) bar_arrive(&sh.full[slot]);
             }
@@ -621,7 +618,8 @@ __device__ __forceinline__ void role_unpack(Shared& sh, const GroupedArgs& a, ch
 
 // Token producer of the block-scaled mode: one TMA (128 rows x 128 E4M3
 // codes, 128B swizzle) per stage, and the stage's token scale words (one per
-// token) into shared memory for the unpackers, up to a ring ahead of them.
+// token) into the stage's shared slot for the MMA thread's tcgen05.cp; its
+// one arrival on the stage's full barrier carries the TMA's byte count.
 __device__ __forceinline__ void role_tokens_mx(Shared& sh, const GroupedArgs& a, char* smem,
                                                const CUtensorMap* map) {
     const int nblk = a.K >> 5, ngrp = (nblk + 7) >> 3, nst = (a.K + 127) >> 7;
@@ -643,12 +641,11 @@ __device__ __forceinline__ void role_tokens_mx(Shared& sh, const GroupedArgs& a,
                                 ? __ldg(a.bsf + (int64_t)(item.g0 + 32 * j + lane) * nst + 2 * grp + sub)
                                 : 0u;
                 if (!warp_wait(&sh.abort, &sh.empty[slot], ((g / kStages) & 1) ^ 1, status, 8u)) return;
-                uint32_t* tsf = reinterpret_cast<uint32_t*>(smem + kTsfOff + slot * kTsfSlot);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) tsf[32 * j + lane] = tw[j];
+                *reinterpret_cast<uint4*>(smem + kTsfOff + slot * kTsfSlot + lane * 16) =
+                    make_uint4(tw[0], tw[1], tw[2], tw[3]);
+                fence_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                    bar_arrive(&sh.tsf[slot]);
                     char* B = smem + slot * (kMxASlot + kMxBSlot) + kMxASlot;
                     bar_arrive_tx(&sh.full[slot], kMxBSlot);
                     tma_2d(B, map, (8 * grp + 4 * sub) * 32, item.g0, &sh.full[slot]);
@@ -689,6 +686,8 @@ __device__ __forceinline__ void role_mma_mx(Shared& sh, const GroupedArgs& a, ch
                 if (lane == 0) {
                     const uint32_t A = base + slot * (kMxASlot + kMxBSlot), B = A + kMxASlot;
                     const uint32_t sfa = sh.tmem + kMxSfa + slot * 4, sfb = sh.tmem + kMxSfb + slot * 4;
+                    tc_cp_128x128b(sfa, smem_desc(base + kSfaOff + slot * kSfaSlot, 128, 128, 0));
+                    tc_cp_32x128b_x4(sfb, smem_desc(base + kTsfOff + slot * kTsfSlot, 128, 128, 0));
                     for (int k = 0; k < kb; ++k) {
                         const uint32_t idesc = idesc0 | ((uint32_t)k << 29) | ((uint32_t)k << 4);
                         tc_mma_mx(dtm, smem_desc(A + k * 256, 128, 1024, 0), smem_desc(B + k * 32, 16, 1024, 2),
@@ -809,7 +808,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_grouped(const __grid_constant__
         for (int i = 0; i < kStages; ++i) { bar_init(&sh.full[i], kConvWarps + 1); bar_init(&sh.empty[i], 1); }
         for (int i = 0; i < kGroups; ++i) { bar_init(&sh.gfull[i], 1); bar_init(&sh.gempty[i], kConvWarps); }
         for (int i = 0; i < 2; ++i) { bar_init(&sh.tfull[i], 1); bar_init(&sh.tempty[i], 128); }
-        for (int i = 0; i < kStages; ++i) bar_init(&sh.tsf[i], 1);
         bar_init(&sh.fin, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
