@@ -85,6 +85,9 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t0 = time.time()  # the first sample, so the timed region is covered from its start
+            while not self.lines and self.proc.poll() is None and time.time() - t0 < 3.0:
+                time.sleep(0.01)
         except Exception:
             self.proc = None
 
@@ -266,7 +269,9 @@ def metric_unit(workload):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default: about a second of work — 60 for decode, 150 for "
+                         "the prefill layer, 200 for the GEMV, 3 for --impl reference)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -276,6 +281,9 @@ def main():
     ap.add_argument("--layers", type=int, default=None,
                     help="profiling only: hold and run this many layers instead of the model's")
     args = ap.parse_args()
+    if args.steps is None:  # about a second of timed work, so the clock sampler sees it
+        args.steps = (3 if args.impl == "reference" else 150 if args.workload == "oss120-prefill"
+                      else 200 if args.workload == "gemv" else 60)
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args, args.workload)
@@ -362,8 +370,6 @@ def run_decode(args):
     prefill = args.workload == "oss120-prefill"
     if prefill:
         spec = spec.with_(layers=1)
-        # one layer is ~2 ms: time enough steps for the clock sampler to see them
-        args.steps = max(args.steps, 150)
     if args.layers:
         spec = spec.with_(layers=args.layers)
     ctx = Context(local)
