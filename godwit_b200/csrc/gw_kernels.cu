@@ -768,10 +768,12 @@ inline int ok_or_fail() { return cudaPeekAtLastError() == cudaSuccess ? 1 : -1; 
 // Warps per tile: split K when the expert work alone cannot fill the GPU
 // (batch-1 decode runs only top_k experts per layer).
 int pick_ksplit(int tiles_total) {
-    const int target = 148 * 32;  // warps in flight
-    if (tiles_total >= target) return 1;
-    if (tiles_total * 2 >= target) return 2;
-    return 4;
+    // Measured on B200 at batch 1 (GPT-OSS and Qwen3 shapes): the best split is
+    // the largest that keeps the launch under ~3072 warps (~20 per SM) — more
+    // warps only add partial-sum reductions and per-CTA x staging.
+    int ks = 1;
+    while (ks < kGemvWarps && tiles_total * ks * 2 < 3072) ks *= 2;
+    return ks;
 }
 
 }  // namespace
