@@ -51,6 +51,9 @@ WORKLOADS = {
     "gemv": (None, 1, "MXFP4 GEMV 2880x2880 (GPT-OSS down_proj shape), batched over copies"),
 }
 DEFAULT_WORKLOAD = "oss120-decode64"
+# timed steps when --steps is not given: about a second of work each
+DEFAULT_STEPS = {"oss120-decode64": 60, "oss120-decode1": 600, "oss20-decode1": 1000,
+                 "qwen3-decode1": 600, "qwen3-decode32": 200, "oss120-prefill": 150, "gemv": 200}
 SEED = 0
 
 
@@ -282,8 +285,7 @@ def main():
                     help="profiling only: hold and run this many layers instead of the model's")
     args = ap.parse_args()
     if args.steps is None:  # about a second of timed work, so the clock sampler sees it
-        args.steps = (3 if args.impl == "reference" else 150 if args.workload == "oss120-prefill"
-                      else 200 if args.workload == "gemv" else 60)
+        args.steps = 3 if args.impl == "reference" else DEFAULT_STEPS.get(args.workload, 60)
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args, args.workload)
