@@ -46,7 +46,8 @@ class CudaOps:
         self.D.moe_forward(self.ctx, self.bank, layer, x, out)
 
     def residual(self, stream: torch.Tensor, delta: torch.Tensor, x_out: torch.Tensor) -> None:
-        self.D.residual_round(self.ctx, stream, delta, x_out)
+        if stream.numel():  # a rank may hold no tokens
+            self.D.residual_round(self.ctx, stream, delta, x_out)
 
     def route(self, layer: int, x: torch.Tensor):
         k = self.bank.spec.top_k
@@ -114,7 +115,11 @@ class AllToAllEP:
         world = dist.get_world_size(self.group) if dist.is_initialized() else 1
         T, H = x.shape
         k = self.k
-        experts, weights = self.ops.route(layer, x)
+        if T > 0:
+            experts, weights = self.ops.route(layer, x)
+        else:  # a rank without tokens still takes part in every exchange
+            experts = torch.empty((0, k), dtype=torch.int32, device=x.device)
+            weights = torch.empty((0, k), dtype=torch.float32, device=x.device)
         flat_e = experts.reshape(-1).to(torch.int64)
         dest = torch.remainder(flat_e, world)
         order = torch.sort(dest, stable=True).indices                  # slots grouped by owner
@@ -139,6 +144,8 @@ class AllToAllEP:
         y = torch.empty_like(back)
         y.index_copy_(0, order, back)
         y = y.view(T, k, H)
+        if T == 0:
+            return torch.empty((0, H), dtype=torch.float32, device=x.device)
         partial = y[:, 0].clone()
         for j in range(1, k):                                          # slot order, as the combine
             partial += y[:, j]

@@ -45,24 +45,20 @@ def make_x():
     return torch.randn(T_TOTAL, H, generator=g).to(torch.bfloat16)
 
 
-def slice_of(rank, world):
-    per = -(-T_TOTAL // world)
-    return slice(rank * per, min(T_TOTAL, (rank + 1) * per))
-
-
-def run(rank, world):
+def run(rank, world, total=T_TOTAL):
     from godwit_b200.ep import AllToAllEP
-    x = make_x()[slice_of(rank, world)].contiguous()
+    per = -(-total // world)
+    x = make_x()[:total][rank * per:min(total, (rank + 1) * per)].contiguous()
     stream = torch.empty(x.shape[0], H)
     x_work = torch.empty_like(x)
     return AllToAllEP(ToyOps(rank, world), LAYERS, K).forward(x, stream, x_work).numpy()
 
 
-def _worker(rank, world, port, out_dir):
+def _worker(rank, world, port, out_dir, total=T_TOTAL):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        np.save(os.path.join(out_dir, f"r{rank}.npy"), run(rank, world))
+        np.save(os.path.join(out_dir, f"r{rank}.npy"), run(rank, world, total))
     finally:
         dist.destroy_process_group()
 
@@ -80,6 +76,16 @@ def test_alltoall_ranks_match_one_rank(tmp_path, world):
     got = np.concatenate([np.load(tmp_path / f"r{r}.npy") for r in range(world)])
     assert got.shape == ref.shape
     assert np.array_equal(got, ref)
+
+
+def test_rank_without_tokens(tmp_path):
+    """Two tokens over three ranks: the last rank holds none but still takes
+    part in every exchange (and serves the experts it owns)."""
+    ref = run(0, 1, 2)
+    mp.spawn(_worker, args=(3, _free_port(), str(tmp_path), 2), nprocs=3, join=True)
+    parts = [np.load(tmp_path / f"r{r}.npy") for r in range(3)]
+    assert parts[2].shape == (0, H)
+    assert np.array_equal(np.concatenate(parts), ref)
 
 
 def test_one_rank_matches_direct_sum():
