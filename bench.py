@@ -481,11 +481,12 @@ def run_decode(args):
                     "achieved": achieved, "peak": peak, "unit": "GB/s",
                     "frac": (achieved / peak) if achieved else None,
                     "peak_kind": peak_kind, "traffic": None}
-        tr = profiled_traffic(args.workload) if not args.layers else None
-        if tr:  # DRAM bytes of one launch of the dominant kernel, from a committed ncu capture
-            roofline.update({"traffic": tr["dram_bytes_per_launch"], "traffic_kernel": tr["kernel"],
-                             "traffic_alg_bytes": tr["alg_bytes_per_launch_approx"],
-                             "traffic_source": tr["source"]})
+
+    tr = profiled_traffic(args.workload) if not args.layers else None
+    if tr and not (prefill and not block_scaled):  # captured on the default mode's dominant kernel
+        roofline.update({"traffic": tr["dram_bytes_per_launch"], "traffic_kernel": tr["kernel"],
+                         "traffic_alg_bytes": tr["alg_bytes_per_launch_approx"],
+                         "traffic_source": tr["source"]})
     roofline.update({"alg_bytes_per_step": step_bytes_total,
                      "expert_passes_per_step": prof["expert_passes"] / prof_steps,
                      "expert_ms_per_step": expert_ms / prof_steps,
