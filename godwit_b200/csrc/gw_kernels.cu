@@ -1,9 +1,13 @@
 // gw_kernels.cu — sm_100a kernels of the MoE expert hot path.
 //
-//   k_router        bf16 router GEMV + bias (Metal/MoE/router.metal:18-34); the
-//                   last CTA to finish runs the top-k selection and softmax of
-//                   Router.select (Runtime/Router.swift:78-98) for every token
-//                   and builds the expert -> token lists
+//   k_router        bf16 router GEMV + bias (Metal/MoE/router.metal:18-34), one
+//                   expert x 8 tokens per CTA; the last CTA of a token chunk
+//                   runs the top-k selection and softmax of Router.select
+//                   (Runtime/Router.swift:78-98) for its tokens and builds the
+//                   expert -> token lists
+//   k_router_mma    the same for bf16 batches of >= 128 tokens, logits on mma.sync
+//   k_rmsnorm       post-attention RMSNorm into the router input
+//                   (Runtime/TransformerLayer.swift:265-285, router.metal:41-60)
 //   k_group         the same grouping for a routing decision supplied by the
 //                   caller (ExpertRunner.applyAssignments' assignment set)
 //   k_gateup        grouped MXFP4 gate_up GEMV + bias + activation epilogue
@@ -18,6 +22,8 @@
 //   k_fill          seeded synthetic bank bytes
 //   k_residual      stream += delta and the rounded next-layer input
 //   k_widen         stream = x
+//   k_xprep         x -> f16 with a per-row power-of-two shift (GEMV inputs)
+//   k_tile_layout   reference row-major <-> tiled bank layout of one matrix
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
