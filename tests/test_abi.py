@@ -109,3 +109,12 @@ def test_make_expert_stride_fills_the_layout():
         assert sc.min() >= 118 and sc.max() <= 124
         bias = buf[lay.offsets["down_bias"]:lay.offsets["down_bias"] + lay.sizes["down_bias"]]
         assert bool(np.any(bias)) == spec.expert_bias
+
+
+def test_bindings_match_header_argument_counts():
+    """Every ctypes signature has as many arguments as its declaration."""
+    text = open(HEADER).read()
+    for m in re.finditer(r"^GW_API\s+[\w\s\*]+?\b(gw_\w+)\s*\(([^;]*?)\)\s*;", text, flags=re.M | re.S):
+        name, params = m.group(1), " ".join(m.group(2).split())
+        n = 0 if params in ("", "void") else params.count(",") + 1
+        assert len(_abi.SIGNATURES[name][1]) == n, (name, n, len(_abi.SIGNATURES[name][1]))
