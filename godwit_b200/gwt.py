@@ -14,8 +14,10 @@ Format (restated from the reference, paths inside rayl15/Godwit):
                  [E, H]) and "layer{l}.router_b" (bf16 [E], only when the spec
                  has a router bias) (Runtime/TransformerLayer.swift:55-60).
 
-Each owned expert stride is read with one positional read into a host buffer and uploaded with gw_bank_upload_expert, which copies it to HBM
-and lays it out for the kernels.  A missing or inconsistent manifest is an
+Each owned expert stride is read with one positional read into one of two
+page-locked host buffers by a read-ahead thread while the other is uploaded
+with gw_bank_upload_expert (a DMA copy from page-locked memory, then the
+device re-layout), so the disk reads overlap the uploads.  A missing or inconsistent manifest is an
 incomplete install and is rejected, as the reference does
 (GodwitManifest.validate, ModelReader.swift:34-37).
 """
@@ -23,6 +25,8 @@ from __future__ import annotations
 
 import json
 import os
+import queue
+import threading
 
 import numpy as np
 
@@ -104,22 +108,72 @@ def load_bank(ctx, root: str, *, shard_rank: int = 0, shard_count: int = 1, laye
     _desc_from_manifest(desc, m)
     bank = ExpertBank(ctx, spec, shard_rank=shard_rank, shard_count=shard_count, desc=desc)
     stride = int(m["expertStride"])
-    buf = np.empty(stride, np.uint8)
+    bufs = staging_buffers(stride)
     trunk = _Trunk(root, m)
     for layer in range(nl):
-        fd = os.open(layer_path(root, layer), os.O_RDONLY)
-        try:
-            for e in range(shard_rank, spec.experts, shard_count):
-                n = os.preadv(fd, [memoryview(buf)], e * stride)
-                if n != stride:
-                    raise InstallError(f"short read: layer {layer} expert {e} got {n} of {stride}")
-                bank.upload_expert(layer, e, buf)
-        finally:
-            os.close(fd)
+        for e, buf in stream_strides(root, layer, range(shard_rank, spec.experts, shard_count), stride, bufs):
+            bank.upload_expert(layer, e, buf)
         w = trunk.u16(f"layer{layer}.router_w", spec.experts * spec.hidden)
         b = trunk.u16(f"layer{layer}.router_b", spec.experts) if spec.router_bias else None
         bank.upload_router(layer, w, b)
     return bank, spec
+
+
+def staging_buffers(stride: int, count: int = 2):
+    """`count` host buffers of `stride` bytes, page-locked when a CUDA device
+    is present (the uploads then DMA straight from them)."""
+    try:
+        import torch
+        if torch.cuda.is_available():
+            return [torch.empty(stride, dtype=torch.uint8, pin_memory=True).numpy() for _ in range(count)]
+    except Exception:
+        pass
+    return [np.empty(stride, np.uint8) for _ in range(count)]
+
+
+def stream_strides(root: str, layer: int, experts, stride: int, bufs):
+    """Yields (expert, buffer) for each expert's stride of layer `layer`, read
+    ahead by a thread into the buffers in turn (ModelReader.loadExpertStride,
+    Runtime/ModelReader.swift:73-76).  A buffer is refilled only after the
+    consumer has asked for the next stride, i.e. finished with it."""
+    experts = list(experts)
+    free: queue.Queue = queue.Queue()
+    full: queue.Queue = queue.Queue()
+    for i in range(len(bufs)):
+        free.put(i)
+    stop = threading.Event()
+
+    def reader():
+        fd = os.open(layer_path(root, layer), os.O_RDONLY)
+        try:
+            for e in experts:
+                i = free.get()
+                if stop.is_set():
+                    return
+                n = os.preadv(fd, [memoryview(bufs[i])], e * stride)
+                if n != stride:
+                    full.put(InstallError(f"short read: layer {layer} expert {e} got {n} of {stride}"))
+                    return
+                full.put((e, i))
+        except OSError as err:
+            full.put(InstallError(f"layer {layer}: {err}"))
+        finally:
+            os.close(fd)
+
+    t = threading.Thread(target=reader, daemon=True)
+    t.start()
+    try:
+        for _ in experts:
+            item = full.get()
+            if isinstance(item, Exception):
+                raise item
+            e, i = item
+            yield e, bufs[i]
+            free.put(i)
+    finally:
+        stop.set()
+        free.put(0)  # wakes a reader blocked on a buffer
+        t.join()
 
 
 class _Trunk:

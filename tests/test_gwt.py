@@ -74,3 +74,35 @@ def test_loaded_bank_matches_oracle(ctx, tmp_path):
         assert O.rel_l2(out, O.moe_layer64(spec, strides[1], x, ex, wt)) < 1e-3
     finally:
         bank.close()
+
+
+def test_streamed_strides_are_the_install_bytes(tmp_path):
+    """The read-ahead loader yields every owned expert's stride in order, byte
+    for byte, through two alternating buffers."""
+    from godwit_b200 import gwt
+    spec = GPT_OSS_20B.with_(hidden=64, intermediate=32, experts=5, layers=2)
+    rng = np.random.default_rng(2)
+    strides = [np.stack([synth.make_expert_stride(spec, rng) for _ in range(spec.experts)])
+               for _ in range(spec.layers)]
+    routers = [synth.make_router(spec, rng) for _ in range(spec.layers)]
+    gwt.write_install(str(tmp_path), spec, strides, routers)
+    m = gwt.read_manifest(str(tmp_path))
+    stride = int(m["expertStride"])
+    bufs = [np.empty(stride, np.uint8) for _ in range(2)]
+    for layer in range(spec.layers):
+        got = [(e, b.copy()) for e, b in gwt.stream_strides(str(tmp_path), layer, [1, 3, 4], stride, bufs)]
+        assert [e for e, _ in got] == [1, 3, 4]
+        for e, b in got:
+            assert np.array_equal(b, strides[layer][e])
+
+
+def test_streamed_read_past_the_file_is_an_install_error(tmp_path):
+    from godwit_b200 import gwt
+    spec = GPT_OSS_20B.with_(hidden=64, intermediate=32, experts=2, layers=1)
+    rng = np.random.default_rng(3)
+    strides = [np.stack([synth.make_expert_stride(spec, rng) for _ in range(spec.experts)])]
+    gwt.write_install(str(tmp_path), spec, strides, [synth.make_router(spec, rng)])
+    stride = int(gwt.read_manifest(str(tmp_path))["expertStride"])
+    bufs = [np.empty(stride, np.uint8) for _ in range(2)]
+    with pytest.raises(gwt.InstallError):
+        list(gwt.stream_strides(str(tmp_path), 0, [0, 5], stride, bufs))
