@@ -66,6 +66,7 @@ SIGNATURES = {
     "gw_shutdown": (ST, [P]),
     "gw_ctx_set_stream": (ST, [P, P]),
     "gw_sync": (ST, [P]),
+    "gw_selftest_wait_timeout": (ST, [P, I64]),
     "gw_set_tensor_core_min_tokens": (ST, [P, I32]),
     "gw_set_decode_streaming": (ST, [P, I32]),
     "gw_set_block_scaled": (ST, [P, I32]),

@@ -50,14 +50,18 @@ def build_cuda(force: bool = False, verbose: bool = False) -> str:
     nvcc = _nvcc()
     objdir = os.path.join(ROOT, "_build")
     os.makedirs(objdir, exist_ok=True)
-    objs = []
-    for s in CU_SOURCES:
+    from concurrent.futures import ThreadPoolExecutor
+
+    def compile_one(s: str) -> str:
         obj = os.path.join(objdir, s.replace(".cu", ".o"))
         cmd = [nvcc, *ARCH, *NVCC_FLAGS, "-c", os.path.join(CSRC, s), "-o", obj]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
         subprocess.run(cmd, check=True)
-        objs.append(obj)
+        return obj
+
+    with ThreadPoolExecutor(max_workers=len(CU_SOURCES)) as pool:  # one nvcc per source file
+        objs = list(pool.map(compile_one, CU_SOURCES))
     tmp = LIB + ".tmp"
     subprocess.run([nvcc, *ARCH, "-shared", *objs, "-o", tmp], check=True)
     os.replace(tmp, LIB)

@@ -74,6 +74,7 @@ struct gw_ctx {
     DevBuf work;        // MoE scratch (MoeWork)
     DevBuf staging;     // inputs/outputs of the synchronous API
     DevBuf gemv_x;      // f16 x + block scales of GEMV calls
+    unsigned* status = nullptr;  // sticky bits of bounded device waits that gave up
     int work_tcap = 0, work_H = 0, work_F = 0, work_E = 0, work_k = 0;
     gw::MoeWork w{};
     int sms = 148;          // persistent grid of the tensor-core expert kernels
@@ -180,12 +181,10 @@ gw_status ensure_work(gw_ctx* c, const gw_bank* b, int T) {
     const size_t o_aq = take((size_t)tcap * kc * Fc);
     const size_t o_asf = take((size_t)tcap * kc * ((Fc + 127) / 128) * 4);
     const size_t o_done = take((size_t)(tcap / 8 + 1) * 4);
-    const size_t o_status = take(4);
     cudaError_t e = c->work.ensure(off);
     if (e != cudaSuccess) return cuda_fail(e, "workspace allocation");
     char* base = static_cast<char*>(c->work.p);
     GW_CUDA(cudaMemsetAsync(base + o_done, 0, (size_t)(tcap / 8 + 1) * 4, c->cur));
-    GW_CUDA(cudaMemsetAsync(base + o_status, 0, 4, c->cur));
     GW_CUDA(cudaMemsetAsync(base + o_nactive, 0, 4, c->cur));
     GW_CUDA(cudaMemsetAsync(base + o_counts, 0, (size_t)Ec * 4, c->cur));
     gw::MoeWork& w = c->w;
@@ -208,7 +207,7 @@ gw_status ensure_work(gw_ctx* c, const gw_bank* b, int T) {
     w.aq = reinterpret_cast<uint8_t*>(base + o_aq);
     w.asf = reinterpret_cast<uint32_t*>(base + o_asf);
     w.done = reinterpret_cast<unsigned*>(base + o_done);
-    w.status = reinterpret_cast<unsigned*>(base + o_status);
+    w.status = c->status;
     w.mma_min_avg = c->mma_min_avg;
     w.block_scaled = c->block_scaled;
     c->work_tcap = tcap;
@@ -229,6 +228,13 @@ gw_status check_bank(gw_bank* b, int layer) {
     if (!b || !b->ctx) return fail(GW_E_ARG, "null bank");
     if (layer < 0 || layer >= b->d.layers)
         return fail(GW_E_ARG, "layer %d out of range [0, %d)", layer, b->d.layers);
+    return GW_OK;
+}
+
+// The expert kernels read activations and write outputs 16 bytes at a time.
+gw_status check_align16(const void* p, const char* what) {
+    if (reinterpret_cast<uintptr_t>(p) % 16)
+        return fail(GW_E_ARG, "%s (%p) must be 16-byte aligned", what, p);
     return GW_OK;
 }
 
@@ -380,6 +386,14 @@ gw_status gw_init(int32_t device, gw_ctx** out) {
         delete c;
         return cuda_fail(e, "cudaStreamCreate");
     }
+    e = cudaMalloc(&c->status, 4);
+    if (e == cudaSuccess) e = cudaMemset(c->status, 0, 4);
+    if (e != cudaSuccess) {
+        cudaStreamDestroy(c->own);
+        if (c->status) cudaFree(c->status);
+        delete c;
+        return cuda_fail(e, "status word allocation");
+    }
     c->cur = c->own;
     *out = c;
     g_last_error.clear();
@@ -398,6 +412,7 @@ gw_status gw_shutdown(gw_ctx* c) {
         c->work.release();
         c->staging.release();
         c->gemv_x.release();
+        if (c->status) cudaFree(c->status);
         cudaStreamDestroy(c->own);
     }
     delete c;
@@ -416,15 +431,24 @@ gw_status gw_sync(gw_ctx* c) {
     CtxLock lk(c);
     GW_CUDA(cudaSetDevice(c->device));
     GW_CUDA(cudaStreamSynchronize(c->cur));
-    if (c->w.status) {  // a bounded wait in a tensor-core expert kernel ran out
-        unsigned bits = 0;
-        GW_CUDA(cudaMemcpy(&bits, c->w.status, 4, cudaMemcpyDeviceToHost));
-        if (bits) {
-            GW_CUDA(cudaMemset(c->w.status, 0, 4));
-            return fail(GW_E_CUDA, "tensor-core expert kernel gave up waiting (status bits 0x%x)", bits);
-        }
+    // a bounded wait inside one of the context's kernels ran out
+    unsigned bits = 0;
+    GW_CUDA(cudaMemcpy(&bits, c->status, 4, cudaMemcpyDeviceToHost));
+    if (bits) {
+        GW_CUDA(cudaMemset(c->status, 0, 4));
+        return fail(GW_E_TIMEOUT, "a device-side wait gave up (status bits 0x%x)", bits);
     }
     return GW_OK;
+}
+
+gw_status gw_selftest_wait_timeout(gw_ctx* c, int64_t wait_cycles) {
+    if (!c) return fail(GW_E_ARG, "null context");
+    if (wait_cycles < 0 || wait_cycles > 100000000)
+        return fail(GW_E_ARG, "wait_cycles %lld outside [0, 1e8]", (long long)wait_cycles);
+    CtxLock lk(c);
+    gw_status st = set_device(c);
+    if (st) return st;
+    return count(c, gw::launch_wait_probe(c->status, wait_cycles, c->cur));
 }
 
 gw_status gw_set_block_scaled(gw_ctx* c, int32_t enable) {
@@ -791,6 +815,7 @@ gw_status gw_moe_forward_async(gw_ctx* c, gw_bank* b, int32_t layer, const void*
     if (!c || !x_dev || !out_dev) return fail(GW_E_ARG, "null argument");
     gw_status st = check_bank(b, layer);
     if (st || (st = check_dtype(x_dtype))) return st;
+    if ((st = check_align16(x_dev, "x_dev")) || (st = check_align16(out_dev, "out_dev"))) return st;
     if (T <= 0) return fail(GW_E_ARG, "T must be positive");
     CtxLock lk(c);
     if ((st = set_device(c))) return st;
@@ -809,6 +834,7 @@ gw_status gw_moe_stack_forward_async(gw_ctx* c, gw_bank* b, const void* x_dev, i
     if (!c || !x_dev || !stream_dev) return fail(GW_E_ARG, "null argument");
     gw_status st = check_bank(b, 0);
     if (st || (st = check_dtype(x_dtype))) return st;
+    if ((st = check_align16(x_dev, "x_dev")) || (st = check_align16(stream_dev, "stream_dev"))) return st;
     if (T <= 0) return fail(GW_E_ARG, "T must be positive");
     CtxLock lk(c);
     if ((st = set_device(c))) return st;
@@ -874,6 +900,7 @@ gw_status gw_moe_apply_async(gw_ctx* c, gw_bank* b, int32_t layer, const void* x
     if (!c || !x_dev || !out_dev || !experts_dev || !weights_dev) return fail(GW_E_ARG, "null argument");
     gw_status st = check_bank(b, layer);
     if (st || (st = check_dtype(x_dtype))) return st;
+    if ((st = check_align16(x_dev, "x_dev")) || (st = check_align16(out_dev, "out_dev"))) return st;
     if (T <= 0) return fail(GW_E_ARG, "T must be positive");
     CtxLock lk(c);
     if ((st = set_device(c))) return st;
@@ -1095,6 +1122,7 @@ gw_status gw_route_async(gw_ctx* c, gw_bank* b, int32_t layer, const void* x_dev
     if (!c || !x_dev || !experts_dev || !weights_dev) return fail(GW_E_ARG, "null argument");
     gw_status st = check_bank(b, layer);
     if (st || (st = check_dtype(x_dtype))) return st;
+    if ((st = check_align16(x_dev, "x_dev"))) return st;
     if (T <= 0) return fail(GW_E_ARG, "T must be positive");
     CtxLock lk(c);
     if ((st = set_device(c))) return st;
@@ -1282,6 +1310,7 @@ extern "C" GW_API gw_status gw_moe_forward_noalloc_async(gw_ctx* c, gw_bank* b, 
     if (!c || !x_dev || !out_dev) return fail(GW_E_ARG, "null argument");
     gw_status st = check_bank(b, layer);
     if (st || (st = check_dtype(x_dtype))) return st;
+    if ((st = check_align16(x_dev, "x_dev")) || (st = check_align16(out_dev, "out_dev"))) return st;
     if (T <= 0) return fail(GW_E_ARG, "T must be positive");
     const int H = b->d.hidden, F = b->d.intermediate, E = b->d.experts, k = b->d.top_k;
     // the same scratch carve-up as the context workspace, sized for exactly T
@@ -1324,6 +1353,7 @@ extern "C" GW_API gw_status gw_moe_forward_noalloc_async(gw_ctx* c, gw_bank* b, 
     w.act = reinterpret_cast<__half*>(base + o_act);
     w.ybuf = reinterpret_cast<float*>(base + o_ybuf);
     w.done = reinterpret_cast<unsigned*>(base + o_done);
+    w.status = c->status;
     // The array keeps whatever the previous call left: clear the expert counts,
     // the active-expert count and the router completion counters.
     GW_CUDA(cudaMemsetAsync(base + o_counts, 0, (size_t)E * 4, c->cur));

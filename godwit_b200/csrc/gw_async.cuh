@@ -64,14 +64,14 @@ __device__ __forceinline__ void group_sync(int id, int n) {
 // Bounded wait; false when the CTA is winding down (this wait ran out, or
 // another role's did).
 static __device__ __noinline__ bool wait_slow(int* abort_flag, uint64_t* b, uint32_t parity, unsigned* status,
-                                       unsigned bit) {
+                                       unsigned bit, long long limit = kWaitCycles) {
     const long long t0 = clock64();
     volatile int* ab = abort_flag;
     for (uint32_t i = 1;; ++i) {
         if (bar_try(b, parity)) return true;
         if ((i & 63) == 0) {
             if (*ab) return false;
-            if (clock64() - t0 > kWaitCycles) {
+            if (clock64() - t0 > limit) {
                 *ab = 1;
                 if (status) atomicOr(status, bit);
                 return false;

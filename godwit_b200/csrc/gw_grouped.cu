@@ -98,33 +98,6 @@ static_assert(kStages * (kMxASlot + kMxBSlot) <= kRingBytes, "block-scaled ring 
 // Warp roles.
 constexpr int kConvWarps = 8, kEpiWarp0 = 8, kWeightWarp = 12, kTokenWarp = 13, kMmaWarp = 14;
 
-// Per-role cycle counters, compiled in with -DGW_GROUPED_TRACE: lane 0 of
-// the first warp of each role adds the cycles it spent in each phase to
-// g_grouped_trace[slot] (summed over CTAs); read with gw_grouped_trace().
-#ifdef GW_GROUPED_TRACE
-__device__ unsigned long long g_grouped_trace[16];
-#define GT_START(v) const long long v = clock64()
-#define GT_ADD(slot, v, lead) \
-    do { if (lead) gt_acc[slot] += clock64() - (v); } while (0)
-#define GT_COUNT(slot, lead) \
-    do { if (lead) gt_acc[slot] += 1; } while (0)
-#define GT_FLUSH(lead)                                                                           \
-    do {                                                                                         \
-        if (lead)                                                                                \
-            for (int i_ = 0; i_ < 16; ++i_)                                                      \
-                if (gt_acc[i_]) atomicAdd(&g_grouped_trace[i_], (unsigned long long)gt_acc[i_]); \
-    } while (0)
-#else
-#define GT_FLUSH(lead) \
-    do { } while (0)
-#define GT_START(v) \
-    do { } while (0)
-#define GT_ADD(slot, v, lead) \
-    do { } while (0)
-#define GT_COUNT(slot, lead) \
-    do { } while (0)
-#endif
-
 struct GroupedArgs {
     LayerView L;
     MoeDims d;
@@ -262,9 +235,6 @@ struct Shared {
     int epre[kMaxExperts];        // expert-ordered rows before expert e (all experts)
     int col_slot[kNMax];          // epilogue: slot of each token column
     float col_mul[kNMax];         // epilogue: xmul (gate_up) or routing weight (down)
-#ifdef GW_GROUPED_TRACE
-    long long tok_issued[kStages], conv_arrived[kStages];
-#endif
 };
 
 struct Item {
@@ -299,7 +269,7 @@ __device__ __forceinline__ Item decode(const Shared& sh, int it) {
 
 // Weight producer (one warp, converged): for every item, every 8-block group
 // of its 128-row tile, once the ring slot is free; lane t copies tile t.
-__device__ __forceinline__ void role_weights(Shared& sh, const GroupedArgs& a, char* smem, long long (&gt_acc)[16]) {
+__device__ __forceinline__ void role_weights(Shared& sh, const GroupedArgs& a, char* smem) {
     const int nblk = a.K >> 5, ngrp = (nblk + 7) >> 3;
     const int lane = threadIdx.x & 31;
     unsigned* status = a.w.status;
@@ -315,21 +285,14 @@ __device__ __forceinline__ void role_weights(Shared& sh, const GroupedArgs& a, c
         const int tiles = min(8, (a.M - item.m0) >> 4);
         for (int grp = 0; grp < ngrp; ++grp, ++gq) {
             const int slot = gq % kGroups;
-            GT_START(t0);
             if (!warp_wait(&sh.abort, &sh.gempty[slot], ((gq / kGroups) & 1) ^ 1, status, 1u)) return;
-            GT_ADD(0, t0, lane == 0);
             const int w = min(8, nblk - 8 * grp);
             const uint32_t run = 16 * w * 16, srun = 16 * w;  // bytes per tile: blocks, scales
             char* dpk = ring + slot * (kGroupPk + kGroupSc);
             char* dsc = dpk + kGroupPk;
-#ifdef GW_TRACE_SKIP_RAW
-            if (lane == 0) bar_arrive(&sh.gfull[slot]);
-            if (false) {
-#else
             if (lane == 0) bar_arrive_tx(&sh.gfull[slot], tiles * (run + srun));
             __syncwarp();
             if (lane < tiles) {
-#endif
                 const int t = lane;
                 bulk_g2s(dpk + t * kTileRun, pk + (int64_t)t * 16 * nblk * 16 + grp * 128 * 16, run,
                          &sh.gfull[slot]);
@@ -343,7 +306,7 @@ __device__ __forceinline__ void role_weights(Shared& sh, const GroupedArgs& a, c
 // of each stage's up-to-four blocks, blocks 2h and 2h + 1 (h = c >> 7),
 // which it widens to 64 f16 and stores as 32 TMEM columns.  Lane 0 of each
 // warp does the barrier work for its warp.
-__device__ __forceinline__ void role_convert(Shared& sh, const GroupedArgs& a, char* smem, long long (&gt_acc)[16]) {
+__device__ __forceinline__ void role_convert(Shared& sh, const GroupedArgs& a, char* smem) {
     const int c = threadIdx.x;
     const int r = c & (kM - 1), h = c >> 7, lane = c & 31, warp = c >> 5;
     const int lr = r & 15, tile = r >> 4;
@@ -369,22 +332,14 @@ __device__ __forceinline__ void role_convert(Shared& sh, const GroupedArgs& a, c
         for (int grp = 0; ok && grp < ngrp; ++grp, ++gq) {
             const int w = min(8, nblk - 8 * grp);
             const int gslot = gq % kGroups;
-            [[maybe_unused]] const bool lead = c == 0;
-            GT_START(t0);
             if (!warp_wait(&sh.abort, &sh.gfull[gslot], (gq / kGroups) & 1, status, 2u)) { ok = false; break; }
-            GT_ADD(1, t0, lead);
             const char* gb = ring + gslot * (kGroupPk + kGroupSc);
             for (int sub = 0; sub * 4 < w; ++sub, ++g) {
                 const int kb = min(4, w - 4 * sub);  // blocks in this stage (4 or 2)
                 const bool mine = 2 * h < kb;        // this thread's two blocks exist
                 const int bl = 4 * sub + 2 * h;      // its first block within the group
-                GT_START(t1);
                 uint32_t v[32];
-#ifdef GW_TRACE_SKIP_CONVERT
-                if (false) {
-#else
                 if (valid && mine) {
-#endif
                     const uint4* q = reinterpret_cast<const uint4*>(gb + tile * kTileRun + (lr * w + bl) * 16);
                     const uint8_t* sb = reinterpret_cast<const uint8_t*>(gb + kGroupPk + tile * 128 + lr * w + bl);
 #pragma unroll
@@ -408,11 +363,8 @@ __device__ __forceinline__ void role_convert(Shared& sh, const GroupedArgs& a, c
                     __syncwarp();
                     if (lane == 0) bar_arrive(&sh.gempty[gslot]);
                 }
-                GT_ADD(2, t1, lead);
                 const int slot = g % kStages;
-                GT_START(t2);
                 if (!warp_wait(&sh.abort, &sh.empty[slot], ((g / kStages) & 1) ^ 1, status, 4u)) { ok = false; break; }
-                GT_ADD(3, t2, lead);
                 // the warp's 32 rows, columns [32h, 32h + 32) of the stage's weight slot
                 if (2 * h < kb) {  // uniform over the warp
                     tmem_st32(sh.tmem + tlane + kAColBase + slot * kACols + 32 * h, v);
@@ -420,11 +372,7 @@ __device__ __forceinline__ void role_convert(Shared& sh, const GroupedArgs& a, c
                 }
                 tc_before_sync();
                 __syncwarp();
-#ifdef GW_GROUPED_TRACE
-                if (c == 224) *(volatile long long*)&sh.conv_arrived[slot] = clock64();  // last converter warp
-#endif
                 if (lane == 0) bar_arrive(&sh.full[slot]);
-                GT_COUNT(13, lead);
             }
         }
     }
@@ -436,7 +384,7 @@ __device__ __forceinline__ void role_convert(Shared& sh, const GroupedArgs& a, c
 // expert and only fill columns the epilogue ignores; rows past the matrix
 // read as zero).
 __device__ __forceinline__ void role_tokens(Shared& sh, const GroupedArgs& a, char* smem,
-                                            const CUtensorMap* map, long long (&gt_acc)[16]) {
+                                            const CUtensorMap* map) {
     const int nblk = a.K >> 5, ngrp = (nblk + 7) >> 3;
     const int lane = threadIdx.x & 31;
     unsigned* status = a.w.status;
@@ -448,23 +396,13 @@ __device__ __forceinline__ void role_tokens(Shared& sh, const GroupedArgs& a, ch
             for (int sub = 0; sub * 4 < w; ++sub, ++g) {
                 const int kb = min(4, w - 4 * sub);
                 const int slot = g % kStages;
-                GT_START(t0);
                 if (!warp_wait(&sh.abort, &sh.empty[slot], ((g / kStages) & 1) ^ 1, status, 8u)) return;
-                GT_ADD(4, t0, lane == 0);
                 if (lane == 0) {
                     char* B = smem + slot * kBSlot;
                     const int x0 = (8 * grp + 4 * sub) * 32;
-#ifdef GW_TRACE_SKIP_TOKENS
-                    bar_arrive(&sh.full[slot]);
-                    (void)B; (void)map; (void)x0; (void)kb;
-#else
                     bar_arrive_tx(&sh.full[slot], (uint32_t)(kb / 2) * kBBox);
                     for (int cb = 0; cb < kb / 2; ++cb)
                         tma_2d(B + cb * kBBox, map, x0 + cb * kBox, item.g0, &sh.full[slot]);
-#endif
-#ifdef GW_GROUPED_TRACE
-                    *(volatile long long*)&sh.tok_issued[slot] = clock64();
-#endif
                 }
                 __syncwarp();
             }
@@ -475,7 +413,7 @@ __device__ __forceinline__ void role_tokens(Shared& sh, const GroupedArgs& a, ch
 // MMA issuer: one warp, converged; lane 0 issues.  A stage of kb blocks is
 // 2 kb MMAs of K = 16: A from the stage's TMEM columns, B from its shared
 // slot (box cb = k / 4, 32 bytes per K step inside the swizzled row).
-__device__ __forceinline__ void role_mma(Shared& sh, const GroupedArgs& a, char* smem, long long (&gt_acc)[16]) {
+__device__ __forceinline__ void role_mma(Shared& sh, const GroupedArgs& a, char* smem) {
     const int nblk = a.K >> 5, ngrp = (nblk + 7) >> 3;
     const int lane = threadIdx.x & 31;
     unsigned* status = a.w.status;
@@ -487,9 +425,7 @@ __device__ __forceinline__ void role_mma(Shared& sh, const GroupedArgs& a, char*
         const int n = max(16, (item.n + 15) & ~15);
         const uint32_t idesc = (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kM >> 4) << 24);
         const int b = il & 1;
-        GT_START(t0);
         if (!warp_wait(&sh.abort, &sh.tempty[b], ((il >> 1) & 1) ^ 1, status, 16u)) break;
-        GT_ADD(7, t0, lane == 0);
         tc_after_sync();
         const uint32_t dtm = sh.tmem + b * kNMax;
         bool first = true;
@@ -498,36 +434,19 @@ __device__ __forceinline__ void role_mma(Shared& sh, const GroupedArgs& a, char*
             for (int sub = 0; sub * 4 < w; ++sub, ++g) {
                 const int kb = min(4, w - 4 * sub);
                 const int slot = g % kStages;
-                GT_START(t1);
                 if (!warp_wait(&sh.abort, &sh.full[slot], (g / kStages) & 1, status, 32u)) { ok = false; break; }
-                GT_ADD(6, t1, lane == 0);
-#ifdef GW_GROUPED_TRACE
-                {
-                    const long long now = clock64();
-                    if (lane == 0) {
-                        gt_acc[5] += now - *(volatile long long*)&sh.tok_issued[slot];
-                        gt_acc[15] += now - *(volatile long long*)&sh.conv_arrived[slot];
-                    }
-                }
-#endif
-                GT_START(t2);
                 tc_after_sync();
                 if (lane == 0) {
                     const uint32_t atm = sh.tmem + kAColBase + slot * kACols;
                     const uint32_t B = base + slot * kBSlot;
                     for (int k = 0; k < 2 * kb; ++k) {
-#ifndef GW_TRACE_SKIP_MMA
                         tc_mma_ta(dtm, atm + k * 8, smem_desc(B + (k >> 2) * kBBox + (k & 3) * 32, 16, 1024, 2),
                                   idesc, first ? 0u : 1u);
-#else
-                        (void)idesc; (void)atm; (void)B;
-#endif
                         first = false;
                     }
                     tc_commit(&sh.empty[slot]);
                 }
                 __syncwarp();
-                GT_ADD(8, t2, lane == 0);
             }
         }
         if (!ok) break;
@@ -718,13 +637,12 @@ __device__ __forceinline__ void role_mma_mx(Shared& sh, const GroupedArgs& a, ch
 
 // Epilogue: thread t (0..127) owns TMEM lane t = tile row m0 + t.
 template <int kMode, bool kMX>
-__device__ __forceinline__ void role_epilogue(Shared& sh, const GroupedArgs& a, long long (&gt_acc)[16]) {
+__device__ __forceinline__ void role_epilogue(Shared& sh, const GroupedArgs& a) {
     const int t = threadIdx.x - kEpiWarp0 * 32;
     const int ew = t >> 5, lane = t & 31;
     unsigned* status = a.w.status;
     int il = 0;
     for (int it = blockIdx.x; it < sh.nitems; it += gridDim.x, ++il) {
-        GT_START(t0);
         const Item item = decode(sh, it);
         const int R = item.m0 + t;
         const bool valid = R < a.M;
@@ -747,12 +665,8 @@ __device__ __forceinline__ void role_epilogue(Shared& sh, const GroupedArgs& a, 
         sh.col_mul[t] = cm;
         group_sync(1, 128);
         const int b = il & 1;
-        GT_ADD(11, t0, t == 0);
-        GT_START(t1);
         const bool got = wait_on(&sh.abort, &sh.tfull[b], (il >> 1) & 1, status, 128u);
         if (group_any(!got, 2, 128)) break;
-        GT_ADD(9, t1, t == 0);
-        GT_START(t2);
         tc_after_sync();
         const uint32_t taddr = sh.tmem + b * kNMax + ((uint32_t)(ew * 32) << 16);
         const float pbv = __shfl_xor_sync(0xffffffffu, bv, 1);
@@ -778,8 +692,6 @@ __device__ __forceinline__ void role_epilogue(Shared& sh, const GroupedArgs& a, 
         }
         tc_before_sync();
         bar_arrive(&sh.tempty[b]);
-        GT_ADD(10, t2, t == 0);
-        GT_COUNT(14, t == 0);
     }
 }
 
@@ -791,7 +703,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_grouped(const __grid_constant__
     char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(dyn_raw) + 1023) & ~uintptr_t(1023));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int mt = (a.M + kM - 1) / kM;
-    GT_START(tk);
 
     // active experts and their token chunks
     const int nact = min(*a.w.nactive, a.d.E);
@@ -869,20 +780,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_grouped(const __grid_constant__
     tc_before_sync();
     __syncthreads();
     tc_after_sync();
-
-    [[maybe_unused]] long long gt_acc[16] = {};  // phase cycle counters (trace builds)
     if (kMX) {
         if (warp < kConvWarps) role_unpack(sh, a, smem);
-        else if (warp < kWeightWarp) role_epilogue<kMode, true>(sh, a, gt_acc);
-        else if (warp == kWeightWarp) role_weights(sh, a, smem, gt_acc);
+        else if (warp < kWeightWarp) role_epilogue<kMode, true>(sh, a);
+        else if (warp == kWeightWarp) role_weights(sh, a, smem);
         else if (warp == kTokenWarp) role_tokens_mx(sh, a, smem, &bmap);
         else role_mma_mx(sh, a, smem);
     } else {
-        if (warp < kConvWarps) role_convert(sh, a, smem, gt_acc);
-        else if (warp < kWeightWarp) role_epilogue<kMode, false>(sh, a, gt_acc);
-        else if (warp == kWeightWarp) role_weights(sh, a, smem, gt_acc);
-        else if (warp == kTokenWarp) role_tokens(sh, a, smem, &bmap, gt_acc);
-        else role_mma(sh, a, smem, gt_acc);
+        if (warp < kConvWarps) role_convert(sh, a, smem);
+        else if (warp < kWeightWarp) role_epilogue<kMode, false>(sh, a);
+        else if (warp == kWeightWarp) role_weights(sh, a, smem);
+        else if (warp == kTokenWarp) role_tokens(sh, a, smem, &bmap);
+        else role_mma(sh, a, smem);
     }
 
     tc_before_sync();
@@ -894,8 +803,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_grouped(const __grid_constant__
         const long long t0 = clock64();
         while (clock64() - t0 < 2000000) {}
     }
-    GT_ADD(12, tk, tid == 0);
-    GT_FLUSH(true);
     if (warp == kMmaWarp)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(sh.tmem), "r"(kTmemCols)
                      : "memory");
@@ -1115,15 +1022,5 @@ int launch_rowexp(const uint8_t* scales, int rows, int cols, uint8_t* out, cudaS
     return cudaGetLastError() == cudaSuccess ? 1 : -1;
 }
 
-#ifdef GW_GROUPED_TRACE
-extern "C" __attribute__((visibility("default"))) int gw_grouped_trace(unsigned long long* out, int reset) {
-    if (cudaMemcpyFromSymbol(out, g_grouped_trace, sizeof(g_grouped_trace)) != cudaSuccess) return -1;
-    if (reset) {
-        static const unsigned long long zero[16] = {};
-        if (cudaMemcpyToSymbol(g_grouped_trace, zero, sizeof(zero)) != cudaSuccess) return -1;
-    }
-    return 0;
-}
-#endif
 
 }  // namespace gw

@@ -11,10 +11,7 @@ namespace gw {
 constexpr int kMaxTopK = 16;
 constexpr int kMaxExperts = 256;
 constexpr int kTokTile = 8;       // tokens per router CTA
-#ifndef GW_ROUTER_MMA_MIN
-#define GW_ROUTER_MMA_MIN 128
-#endif
-constexpr int kRouterMmaMinTokens = GW_ROUTER_MMA_MIN;  // bf16 batches from here on use k_router_mma
+constexpr int kRouterMmaMinTokens = 128;  // bf16 batches from here on use k_router_mma
 constexpr int kChunk = 4;         // tokens per weight pass of an expert GEMV tile
 constexpr int kGemvWarps = 4;     // warps per GEMV CTA (one 16-row tile each)
 
@@ -97,6 +94,9 @@ int launch_rmsnorm(const float* stream, const uint16_t* weight, float eps, int T
 // blocks (scales = 0) or scale bytes (scales = 1).
 int launch_tile_layout(const uint8_t* src, uint8_t* dst, int rows, int cols, int scales,
                        int to_tiled, cudaStream_t s);
+// Status-word bit set by k_wait_probe (the kernels' own waits use bits 0-7).
+constexpr unsigned kStatusProbe = 0x100u;
+int launch_wait_probe(unsigned* status, long long limit, cudaStream_t s);
 int launch_widen(const void* x, int x_dtype, float* stream, int64_t n, cudaStream_t s);
 size_t gemv_smem_bytes(int cols, int max_tok);
 // Tensor-core grouped expert GEMM (gw_grouped.cu): which 0 = gate_up + activation,

@@ -29,6 +29,7 @@
 
 #include <algorithm>
 
+#include "gw_async.cuh"
 #include "gw_device.cuh"
 #include "gw_internal.h"
 
@@ -457,12 +458,9 @@ __device__ __forceinline__ void split_range(int nblk, int ksplit, int sp, int& b
 // and calls emit(token, rowA total, rowB total) once per (row pair, token)
 // on the split-0 warp.  Every thread of the CTA must call this (it
 // synchronises when ksplit > 1).  kPrefetch: see mxfp4_tile_diag.
-#ifndef GW_PF_GATEUP
-#define GW_PF_GATEUP 1
-#endif
-#ifndef GW_PF_DOWN
-#define GW_PF_DOWN 2
-#endif
+// L2 prefetch policy of the two expert GEMVs (see mxfp4_tile_diag's
+// kPrefetch): whole K-range up front for gate_up, two groups ahead for down.
+constexpr int kPrefetchGateup = 1, kPrefetchDown = 2;
 template <int kPrefetch, class Emit>
 __device__ __forceinline__ void run_tile(int n, bool valid, const uint8_t* packed,
                                          const uint8_t* scales, int cols, int rowA, int rowB,
@@ -561,7 +559,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 5) k_gateup(LayerView L, MoeD
         __syncthreads();
         stage_x16(xs, diag_stride(H), w.x16, rows, n, H);
         __syncthreads();
-        run_tile<GW_PF_GATEUP>(n, valid, packed + (size_t)tile * 16 * (H >> 1), scales + (size_t)tile * 16 * (H >> 5),
+        run_tile<kPrefetchGateup>(n, valid, packed + (size_t)tile * 16 * (H >> 1), scales + (size_t)tile * 16 * (H >> 5),
                  H, 2 * g, 2 * g + 1, xs, ksplit,
                  [&](int col, float ga, float ub) {
                      const float v = activate<kAct>(ga * xm[col] + bA, ub * xm[col] + bB, d.limit, d.alpha);
@@ -608,7 +606,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 5) k_down(LayerView L, MoeDim
         __syncthreads();
         stage_x16(xs, diag_stride(F), w.act, slots, n, F);
         __syncthreads();
-        run_tile<GW_PF_DOWN>(n, valid, packed + (size_t)tile * 16 * (F >> 1), scales + (size_t)tile * 16 * (F >> 5),
+        run_tile<kPrefetchDown>(n, valid, packed + (size_t)tile * 16 * (F >> 1), scales + (size_t)tile * 16 * (F >> 5),
                  F, g, g + 8, xs, ksplit,
                  [&](int col, float ya, float yb) {
                      float* y = w.ybuf + (int64_t)slots[col] * H;
@@ -769,6 +767,23 @@ __global__ void k_widen(const void* __restrict__ x, int x_dtype, float* __restri
         stream[i] = load_act(x, x_dtype, i);
 }
 
+// k_wait_probe: one CTA waits on an mbarrier that nothing ever completes,
+// through the same bounded wait the warp-specialised kernels use, with a
+// short limit; the wait gives up, sets kStatusProbe in the status word and
+// the kernel returns.  Lets the host check its timeout reporting without a
+// GPU fault.
+__global__ void k_wait_probe(unsigned* status, long long limit) {
+    __shared__ uint64_t never;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        bar_init(&never, 1);
+        abort_flag = 0;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) (void)wait_slow(&abort_flag, &never, 0, status, kStatusProbe, limit);
+    __syncthreads();
+}
+
 inline int ok_or_fail() { return cudaPeekAtLastError() == cudaSuccess ? 1 : -1; }
 
 // Warps per tile: split K when the expert work alone cannot fill the GPU
@@ -909,6 +924,11 @@ int launch_tile_layout(const uint8_t* src, uint8_t* dst, int rows, int cols, int
     int64_t blocks = ((int64_t)rows * nblk + 255) / 256;
     if (blocks > 148 * 32) blocks = 148 * 32;
     k_tile_layout<<<(unsigned)blocks, 256, 0, s>>>(src, dst, rows, nblk, scales ? 1 : 16, to_tiled);
+    return ok_or_fail();
+}
+
+int launch_wait_probe(unsigned* status, long long limit, cudaStream_t s) {
+    k_wait_probe<<<1, 32, 0, s>>>(status, limit);
     return ok_or_fail();
 }
 

@@ -15,7 +15,7 @@
 //               tokens are staged once per (expert, chunk) in the padded x
 //               layout the tile expects.
 // This is the reference's per-token expert GEMV pair (mxfp4_gemv_bias ->
-// activation -> mxfp4_gemv_bias, Shaders/expert.metal:46-102, 311-368, driven
+// activation -> mxfp4_gemv_bias, Metal/MoE/expert.metal:46-102, 311-368, driven
 // by ExpertRunner.applyAssignments, Runtime/ExpertRunner.swift:108-183) for
 // all of an expert's decode tokens at once.  Every wait is bounded; a wait
 // that runs out sets a status bit and the CTA winds down.

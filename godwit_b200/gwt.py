@@ -144,8 +144,11 @@ def stream_strides(root: str, layer: int, experts, stride: int, bufs):
     stop = threading.Event()
 
     def reader():
-        fd = os.open(layer_path(root, layer), os.O_RDONLY)
+        # Every way out of this thread leaves the consumer something to take
+        # from `full`: a stride, or the error that ended the reads.
+        fd = None
         try:
+            fd = os.open(layer_path(root, layer), os.O_RDONLY)
             for e in experts:
                 i = free.get()
                 if stop.is_set():
@@ -157,8 +160,11 @@ def stream_strides(root: str, layer: int, experts, stride: int, bufs):
                 full.put((e, i))
         except OSError as err:
             full.put(InstallError(f"layer {layer}: {err}"))
+        except BaseException as err:  # noqa: BLE001 — reported to the consumer, not swallowed
+            full.put(InstallError(f"layer {layer}: reader failed: {err!r}"))
         finally:
-            os.close(fd)
+            if fd is not None:
+                os.close(fd)
 
     t = threading.Thread(target=reader, daemon=True)
     t.start()

@@ -31,6 +31,10 @@
  *   - A gw_ctx is internally locked: calls on one context are serialised.
  *   - Shape misuse that the reference catches with `precondition` is
  *     reported as GW_E_ARG before any kernel launches.
+ *   - Device activation and output buffers of the MoE `_async` calls
+ *     (x_dev, out_dev, stream_dev) must be 16-byte aligned (any cudaMalloc
+ *     or torch allocation is); an offset pointer that is not is rejected with
+ *     GW_E_ARG before any launch.
  */
 #ifndef GODWIT_CUDA_H
 #define GODWIT_CUDA_H
@@ -116,9 +120,18 @@ GW_API gw_status gw_shutdown(gw_ctx* ctx);
 /* Orders subsequent `_async` work on `cuda_stream` (a cudaStream_t; NULL =
  * the context's own stream). */
 GW_API gw_status gw_ctx_set_stream(gw_ctx* ctx, void* cuda_stream);
-/* Waits for all work queued on the context's stream.  Also reports (and
- * clears) a bounded wait that ran out inside a tensor-core expert kernel. */
+/* Waits for all work queued on the context's stream.  Returns GW_E_TIMEOUT
+ * (and clears the record) when a bounded device-side wait inside one of the
+ * context's kernels gave up since the last gw_sync; the kernel that gave up
+ * wound down without faulting, so the context stays usable, but the results
+ * of the work since the last gw_sync are not valid. */
 GW_API gw_status gw_sync(gw_ctx* ctx);
+/* Launches one kernel whose bounded wait, on a barrier that nothing ever
+ * completes, gives up after `wait_cycles` SM clock cycles (0..1e8) and
+ * records that the way the expert kernels do; the next gw_sync then returns
+ * GW_E_TIMEOUT.  Lets a caller check its timeout handling end to end without
+ * a GPU fault.  No counterpart in the reference. */
+GW_API gw_status gw_selftest_wait_timeout(gw_ctx* ctx, int64_t wait_cycles);
 /* Expert-path policy (no reference counterpart: the reference runs every
  * (expert, token) assignment as GEMVs, ExpertRunner.applyAssignments,
  * Runtime/ExpertRunner.swift:108-183).  A layer with T tokens runs its experts as tensor-core grouped GEMMs when
@@ -280,9 +293,15 @@ GW_API gw_status gw_moe_block_async(gw_ctx* ctx, gw_bank* bank, int32_t layer, f
  * (up to T=55 at GPT-OSS shapes, 50 at Qwen3-30B-A3B shapes); larger T is
  * rejected with GW_E_ARG.  The first
  * call on a device resolves the array's address (cudaGetSymbolAddress); make
- * that first call before any stream capture.  All calls share the array:
- * calls that overlap on the GPU (other streams, other contexts of the same
- * device) race. */
+ * that first call before any stream capture.  The resolved address belongs
+ * to the device's primary context: after a cudaDeviceReset of that device
+ * this entry point must not be called again in the process.  All calls share
+ * the array: calls that overlap on the GPU (other streams, other contexts of
+ * the same device) race.  The experts always run on the MXFP4 GEMV tiles:
+ * the context's expert-path switches (gw_set_tensor_core_min_tokens,
+ * gw_set_block_scaled, gw_set_decode_streaming) do not apply here, so its
+ * results equal gw_moe_forward_async's whenever that call runs the GEMV
+ * tiles too (always at decode sizes under the default policy). */
 GW_API gw_status gw_moe_forward_noalloc_async(gw_ctx* ctx, gw_bank* bank, int32_t layer,
                                               const void* x_dev, int32_t x_dtype, int32_t T,
                                               float* out_dev, int32_t* experts_dev,

@@ -370,3 +370,51 @@ GWO_API void gwo_moe_layer_mt(const uint8_t* strides, int64_t stride_bytes,
     for (int t = 0; t < started; ++t)
         if (tid[t]) pthread_join(tid[t], NULL);
 }
+
+/* fp64 decode for the fp64 parity oracle: codebook x 2^(byte-127) (the
+ * MXFP4.decode arithmetic of MXFP4.swift:48-92, carried out in double, where
+ * every byte including 0xFF is a finite power of two), rows of a
+ * [rows][cols] matrix, row-parallel over `threads`. */
+typedef struct {
+    const uint8_t* packed; const uint8_t* scales; int64_t r0, r1, cols; double* out;
+} dq64_job;
+
+static void* dq64_worker(void* p) {
+    dq64_job* j = (dq64_job*)p;
+    const int64_t nb = j->cols / 32;
+    for (int64_t r = j->r0; r < j->r1; ++r) {
+        for (int64_t b = 0; b < nb; ++b) {
+            const uint8_t sb = j->scales[r * nb + b];
+            const double s = ldexp(1.0, (int)sb - 127);
+            const uint8_t* q = j->packed + (r * nb + b) * 16;
+            double* o = j->out + r * j->cols + b * 32;
+            for (int i = 0; i < 16; ++i) {
+                o[2 * i] = (double)kCodebook[q[i] & 0x0F] * s;
+                o[2 * i + 1] = (double)kCodebook[q[i] >> 4] * s;
+            }
+        }
+    }
+    return NULL;
+}
+
+GWO_API void gwo_dequant64_mt(const uint8_t* packed, const uint8_t* scales, int64_t rows,
+                              int64_t cols, double* out, int threads) {
+    if (threads < 1) threads = 1;
+    if (threads > 256) threads = 256;
+    pthread_t tid[256];
+    dq64_job jobs[256];
+    const int64_t per = (rows + threads - 1) / threads;
+    int started = 0;
+    for (int t = 0; t < threads; ++t) {
+        const int64_t r0 = t * per, r1 = (t + 1) * per < rows ? (t + 1) * per : rows;
+        if (r0 >= r1) break;
+        jobs[t] = (dq64_job){packed, scales, r0, r1, cols, out};
+        if (threads == 1 || pthread_create(&tid[t], NULL, dq64_worker, &jobs[t]) != 0) {
+            dq64_worker(&jobs[t]);
+            tid[t] = 0;
+        }
+        started = t + 1;
+    }
+    for (int t = 0; t < started; ++t)
+        if (tid[t]) pthread_join(tid[t], NULL);
+}

@@ -54,6 +54,7 @@ def lib() -> C.CDLL:
                                     I64, P, P, P, P, P]
         L.gwo_moe_layer_mt.argtypes = [P, I64, P, I64, I64, I64, C.c_int, C.c_int, F, F, P, P,
                                        P, I64, P, P, P, C.c_int]
+        L.gwo_dequant64_mt.argtypes = [P, P, I64, I64, P, C.c_int]
         _lib = L
     return _lib
 
@@ -216,6 +217,16 @@ def dequant64(packed: np.ndarray, scales: np.ndarray) -> np.ndarray:
     return out.reshape(rows, nb * 32)
 
 
+def dequant64_fast(packed: np.ndarray, scales: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """dequant64 through the C restatement, row-parallel on all host threads
+    (same values: every code x 2^(scale-127) is exact in fp64)."""
+    out = np.empty((rows, cols), dtype=np.float64)
+    lib().gwo_dequant64_mt(_p(np.ascontiguousarray(packed, dtype=np.uint8)),
+                           _p(np.ascontiguousarray(scales, dtype=np.uint8)), rows, cols, _p(out),
+                           os.cpu_count() or 1)
+    return out
+
+
 def expert_sections(spec, stride: np.ndarray):
     from godwit_b200.synth import bf16_bits_to_f32
     lay = spec.layout()
@@ -225,8 +236,8 @@ def expert_sections(spec, stride: np.ndarray):
         o = lay.offsets[name]
         return stride[o:o + lay.sizes[name]]
 
-    gu = dequant64(sec("gate_up_blocks").reshape(2 * F, H // 2), sec("gate_up_scales").reshape(2 * F, H // 32))
-    dn = dequant64(sec("down_blocks").reshape(H, F // 2), sec("down_scales").reshape(H, F // 32))
+    gu = dequant64_fast(sec("gate_up_blocks"), sec("gate_up_scales"), 2 * F, H)
+    dn = dequant64_fast(sec("down_blocks"), sec("down_scales"), H, F)
     gb = bf16_bits_to_f32(sec("gate_up_bias").view(np.uint16)).astype(np.float64)
     db = bf16_bits_to_f32(sec("down_bias").view(np.uint16)).astype(np.float64)
     return gu, gb, dn, db

@@ -106,3 +106,21 @@ def test_streamed_read_past_the_file_is_an_install_error(tmp_path):
     bufs = [np.empty(stride, np.uint8) for _ in range(2)]
     with pytest.raises(gwt.InstallError):
         list(gwt.stream_strides(str(tmp_path), 0, [0, 5], stride, bufs))
+
+
+@pytest.mark.timeout(60)
+def test_layer_file_that_cannot_be_opened_is_an_install_error(tmp_path):
+    """A layer file that disappears (or cannot be opened) after the manifest
+    check ends the read-ahead thread with an InstallError the consumer sees,
+    instead of leaving the consumer waiting for a stride forever."""
+    import os
+    from godwit_b200 import gwt
+    spec = GPT_OSS_20B.with_(hidden=64, intermediate=32, experts=2, layers=1)
+    rng = np.random.default_rng(4)
+    strides = [np.stack([synth.make_expert_stride(spec, rng) for _ in range(spec.experts)])]
+    gwt.write_install(str(tmp_path), spec, strides, [synth.make_router(spec, rng)])
+    stride = int(gwt.read_manifest(str(tmp_path))["expertStride"])
+    os.remove(gwt.layer_path(str(tmp_path), 0))
+    bufs = [np.empty(stride, np.uint8) for _ in range(2)]
+    with pytest.raises(gwt.InstallError):
+        list(gwt.stream_strides(str(tmp_path), 0, [0, 1], stride, bufs))
