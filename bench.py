@@ -53,7 +53,7 @@ WORKLOADS = {
 DEFAULT_WORKLOAD = "oss120-decode64"
 # timed steps when --steps is not given: about a second of work each
 DEFAULT_STEPS = {"oss120-decode64": 60, "oss120-decode1": 600, "oss20-decode1": 1000,
-                 "qwen3-decode1": 600, "qwen3-decode32": 200, "oss120-prefill": 150, "gemv": 200}
+                 "qwen3-decode1": 600, "qwen3-decode32": 200, "oss120-prefill": 150, "gemv": 2000}
 SEED = 0
 
 
@@ -89,7 +89,7 @@ class ClockSampler:
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
             t0 = time.time()  # the first sample, so the timed region is covered from its start
-            while not self.lines and self.proc.poll() is None and time.time() - t0 < 3.0:
+            while not self.lines and self.proc.poll() is None and time.time() - t0 < 10.0:
                 time.sleep(0.01)
         except Exception:
             self.proc = None
@@ -486,7 +486,8 @@ def run_decode(args):
     if tr and not (prefill and not block_scaled):  # captured on the default mode's dominant kernel
         roofline.update({"traffic": tr["dram_bytes_per_launch"], "traffic_kernel": tr["kernel"],
                          "traffic_alg_bytes": tr["alg_bytes_per_launch_approx"],
-                         "traffic_source": tr["source"]})
+                         "traffic_source": tr["source"],
+                         "traffic_measured_in_this_run": False})
     roofline.update({"alg_bytes_per_step": step_bytes_total,
                      "expert_passes_per_step": prof["expert_passes"] / prof_steps,
                      "expert_ms_per_step": expert_ms / prof_steps,
@@ -521,8 +522,14 @@ def run_decode(args):
         if not args.no_cpu_baseline and world == 1:
             threads = os.cpu_count() or 1
             v, sample = cpu_reference_sample(spec, threads)
+            v1, sample1 = cpu_reference_sample(spec, 1, budget_s=6.0)
             line["cpu_baseline"] = {"value": v, "unit": unit, "cores": threads, "kind": "port",
-                                    "sample": sample}
+                                    "sample": sample,
+                                    "single_thread": {"value": v1, "cores": 1, "sample": sample1}}
+        if world == 1 and args.workload == DEFAULT_WORKLOAD and not args.layers:
+            # config 0 (the metric's GEMV half), measured in the same run
+            line["gemv_config0"] = measure_gemv(ctx, cur, local, 1500, 3, 1,
+                                                cpu_baseline=not args.no_cpu_baseline)
         print(json.dumps(line), flush=True)
     bank.close()
     ctx.close()
@@ -532,17 +539,21 @@ def run_decode(args):
     return 0
 
 
-def run_gemv(args):
+GEMV_ROUNDS = 7  # DequantGEMVBenchmark.swift:290-336: one warm-up, then the median of 7 rounds
+
+
+def measure_gemv(ctx, cur, local: int, steps: int, warmup: int, world: int = 1,
+                 cpu_baseline: bool = True) -> dict:
+    """Config 0 (2880x2880 MXFP4 GEMV, GPT-OSS down_proj shape) batched over
+    R distinct copies (> 4x L2), timed the reference's way: warm-up, then
+    GEMV_ROUNDS rounds of `steps` batched launches each, median round.
+    Returns the JSON fields of its line."""
     import numpy as np
     import torch
 
     from godwit_b200 import device as D
     from godwit_b200 import synth
-    from godwit_b200.runtime import Context
 
-    world, rank, local = _dist_setup(args)
-    ctx = Context(local)
-    cur = D.bind_stream(ctx)
     rows = cols = 2880
     alg = 4_429_440  # packed + scales + x + bias + y (config 0)
     l2 = torch.cuda.get_device_properties(local).L2_cache_size
@@ -565,29 +576,32 @@ def run_gemv(args):
     def step():
         D.gemv_batched(ctx, packed, scales, bias, x, y)
 
-    for _ in range(args.warmup):
+    for _ in range(max(warmup, 1)):
         step()
     torch.cuda.synchronize()
     sampler = ClockSampler(local)
     sampler.start()
     launches0 = ctx.launch_count()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record(cur)
-    for _ in range(args.steps):
-        step()
-    ev1.record(cur)
-    torch.cuda.synchronize()
+    rounds = []
+    for _ in range(GEMV_ROUNDS):
+        ev0.record(cur)
+        for _ in range(steps):
+            step()
+        ev1.record(cur)
+        torch.cuda.synchronize()
+        rounds.append(ev0.elapsed_time(ev1) / steps)
     launches = ctx.launch_count() - launches0
-    ms = _max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
+    ms = _max_over_ranks(statistics.median(rounds), world)
     ev0.record(cur)
-    for _ in range(args.steps):
+    for _ in range(steps):
         x.copy_(x_host, non_blocking=True)
         step()
         y_host.copy_(y, non_blocking=True)
     ev1.record(cur)
     torch.cuda.synchronize()
     clocks = sampler.stop()
-    e2e_ms = ev0.elapsed_time(ev1) / args.steps
+    e2e_ms = _max_over_ranks(ev0.elapsed_time(ev1) / steps, world)
     ctx.profile_enable(True)
     for _ in range(3):
         step()
@@ -596,28 +610,46 @@ def run_gemv(args):
     k_ms = prof["gemv_ms"] / max(prof["gemv_launches"], 1)
     achieved = R * alg / (k_ms / 1e3) / 1e9
     peak, peak_kind = peaks()
+    gbs = R * alg * world / (ms / 1e3) / 1e9
+    out = {
+        "metric": "MXFP4 expert GEMV HBM GB/s", "value": gbs, "unit": "GB/s",
+        "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": ms,
+        "rounds": GEMV_ROUNDS, "round_ms": [round(r, 4) for r in rounds],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "mxfp4 weights x bf16 x, fp32 accumulate", "data": "synthetic",
+        "config": {"workload": "gemv", "rows": rows, "cols": cols, "copies": R,
+                   "l2": f"{R} distinct copies = {R * alg / 1e9:.2f} GB > 4x L2 per launch",
+                   "protocol": f"warm-up, then median of {GEMV_ROUNDS} rounds of {steps} launches"},
+        "e2e": {"value": R * alg * world / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
+                "h2d_bytes_per_step": R * cols * 2, "d2h_bytes_per_step": R * rows * 4},
+        "gpu_launches": launches,
+        "roofline": {"bound": "hbm", "kernel": "k_gemv", "achieved": achieved, "peak": peak,
+                     "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
+                     "alg_bytes_per_launch": R * alg, "traffic": None},
+        "clocks": clocks,
+    }
+    if cpu_baseline and world == 1:
+        threads = os.cpu_count() or 1
+        v, sample = cpu_gemv_sample(threads)
+        v1, sample1 = cpu_gemv_sample(1, budget_s=5.0)
+        out["cpu_baseline"] = {"value": v, "unit": "GB/s", "cores": threads, "kind": "port",
+                               "sample": sample,
+                               "single_thread": {"value": v1, "cores": 1, "sample": sample1}}
+    del packed, scales, bias, x, y
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_gemv(args):
+    from godwit_b200 import device as D
+    from godwit_b200.runtime import Context
+
+    world, rank, local = _dist_setup(args)
+    ctx = Context(local)
+    cur = D.bind_stream(ctx)
+    line = measure_gemv(ctx, cur, local, args.steps, args.warmup, world,
+                        cpu_baseline=not args.no_cpu_baseline)
     if rank == 0:
-        gbs = R * alg * world / (ms / 1e3) / 1e9
-        line = {
-            "metric": "MXFP4 expert GEMV HBM GB/s", "value": gbs, "unit": "GB/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "mxfp4 weights x bf16 x, fp32 accumulate", "data": "synthetic",
-            "config": {"workload": "gemv", "rows": rows, "cols": cols, "copies": R,
-                       "l2": f"{R} distinct copies = {R * alg / 1e9:.2f} GB > 4x L2"},
-            "e2e": {"value": R * alg * world / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
-                    "h2d_bytes_per_step": R * cols * 2, "d2h_bytes_per_step": R * rows * 4},
-            "gpu_launches": launches,
-            "roofline": {"bound": "hbm", "kernel": "k_gemv", "achieved": achieved, "peak": peak,
-                         "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
-                         "traffic": None},
-            "clocks": clocks,
-        }
-        if not args.no_cpu_baseline and world == 1:
-            threads = os.cpu_count() or 1
-            v, sample = cpu_gemv_sample(threads)
-            line["cpu_baseline"] = {"value": v, "unit": "GB/s", "cores": threads, "kind": "port",
-                                    "sample": sample}
         print(json.dumps(line), flush=True)
     ctx.close()
     return 0

@@ -68,7 +68,6 @@ SIGNATURES = {
     "gw_sync": (ST, [P]),
     "gw_selftest_wait_timeout": (ST, [P, I64]),
     "gw_set_tensor_core_min_tokens": (ST, [P, I32]),
-    "gw_set_decode_streaming": (ST, [P, I32]),
     "gw_set_block_scaled": (ST, [P, I32]),
     "gw_layout_default": (ST, [I32, I32, I32, I32, I32, I32, C.POINTER(BankDesc)]),
     "gw_bank_create": (ST, [P, C.POINTER(BankDesc), C.POINTER(P)]),

@@ -79,7 +79,6 @@ struct gw_ctx {
     gw::MoeWork w{};
     int sms = 148;          // persistent grid of the tensor-core expert kernels
     int mma_min_avg = 8;    // tensor-core expert path when T*k >= mma_min_avg * E
-    bool streamed = false;  // decode GEMVs with bulk-copied weights (k_stream) vs per-thread loads
     int block_scaled = 0;   // tensor-core path: block-scaled MXFP4 x MXFP8 instead of exact f16
     int64_t launches = 0;
     // profiling (gw_profile_enable): event pairs per timed launch
@@ -306,17 +305,14 @@ gw_status moe_layer_device(gw_ctx* c, gw_bank* b, int layer, const void* x_dev, 
     // Many tokens per expert: the tensor-core grouped GEMMs; few: the GEMV tiles.
     const bool mma = w.mma_min_avg > 0 && (int64_t)T * d.k >= (int64_t)w.mma_min_avg * d.E &&
                      gw::grouped_supported(d, w);
-    const bool streamed = !mma && c->streamed && gw::stream_supported(d, w);
     if ((st = timed_launch(c, 0, 0, [&] {
-             return mma        ? gw::launch_grouped(L, d, w, 0, c->sms, c->cur, x_dev, x_dtype)
-                    : streamed ? gw::launch_stream(L, d, w, 0, c->sms, c->cur)
-                               : gw::launch_gateup(L, d, x_dev, x_dtype, T, w, c->cur);
+             return mma ? gw::launch_grouped(L, d, w, 0, c->sms, c->cur, x_dev, x_dtype)
+                        : gw::launch_expert_gemv(L, d, w, T, 0, c->cur);
          })))
         return st;
     if ((st = timed_launch(c, 1, 0, [&] {
-             return mma        ? gw::launch_grouped(L, d, w, 1, c->sms, c->cur)
-                    : streamed ? gw::launch_stream(L, d, w, 1, c->sms, c->cur)
-                               : gw::launch_down(L, d, T, w, c->cur);
+             return mma ? gw::launch_grouped(L, d, w, 1, c->sms, c->cur)
+                        : gw::launch_expert_gemv(L, d, w, T, 1, c->cur);
          })))
         return st;
     if (c->prof && (st = log_nactive(c))) return st;
@@ -361,7 +357,7 @@ extern "C" {
 
 const char* gw_last_error(void) { return g_last_error.c_str(); }
 
-int32_t gw_version(void) { return 100; }
+int32_t gw_version(void) { return 200; }
 
 gw_status gw_init(int32_t device, gw_ctx** out) {
     if (!out) return fail(GW_E_ARG, "null output pointer");
@@ -375,8 +371,7 @@ gw_status gw_init(int32_t device, gw_ctx** out) {
     if (prop.major != 10)
         return fail(GW_E_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a",
                     device, prop.major, prop.minor);
-    if (gw::configure_kernels() != 0 || gw::configure_grouped() != 0 ||
-        gw::configure_stream(gw::kStreamMaxCols) != 0)
+    if (gw::configure_kernels() != 0 || gw::configure_grouped() != 0 || gw::configure_expert_gemv() != 0)
         return cuda_fail(cudaGetLastError(), "kernel attributes");
     gw_ctx* c = new gw_ctx();
     c->device = device;
@@ -456,17 +451,6 @@ gw_status gw_set_block_scaled(gw_ctx* c, int32_t enable) {
     CtxLock lk(c);
     c->block_scaled = enable != 0;
     c->w.block_scaled = c->block_scaled;
-    if (c->graph.exec) {  // a captured stack forward baked the old choice in
-        cudaGraphExecDestroy(c->graph.exec);
-        c->graph = gw_ctx::StackGraph{};
-    }
-    return GW_OK;
-}
-
-gw_status gw_set_decode_streaming(gw_ctx* c, int32_t enable) {
-    if (!c) return fail(GW_E_ARG, "null context");
-    CtxLock lk(c);
-    c->streamed = enable != 0;
     if (c->graph.exec) {  // a captured stack forward baked the old choice in
         cudaGraphExecDestroy(c->graph.exec);
         c->graph = gw_ctx::StackGraph{};
@@ -572,6 +556,9 @@ gw_status gw_bank_create(gw_ctx* c, const gw_bank_desc* d, gw_bank** out) {
     if (!c || !d || !out) return fail(GW_E_ARG, "null argument");
     if (d->hidden <= 0 || d->hidden % 32 || d->intermediate <= 0 || d->intermediate % 32)
         return fail(GW_E_ARG, "hidden and intermediate must be positive multiples of 32");
+    if (d->hidden > gw::kMaxGemvCols || d->intermediate > gw::kMaxGemvCols)
+        return fail(GW_E_UNSUPPORTED, "hidden (%d) and intermediate (%d) above %d are not supported",
+                    d->hidden, d->intermediate, gw::kMaxGemvCols);
     if (d->experts <= 0 || d->experts > gw::kMaxExperts)
         return fail(GW_E_ARG, "experts %d outside [1, %d]", d->experts, gw::kMaxExperts);
     if (d->top_k <= 0 || d->top_k > gw::kMaxTopK || d->top_k > d->experts)
@@ -1362,8 +1349,8 @@ extern "C" GW_API gw_status gw_moe_forward_noalloc_async(gw_ctx* c, gw_bank* b, 
     const gw::MoeDims d = dims_of(b);
     const gw::LayerView L = layer_of(b, layer);
     if ((st = count(c, gw::launch_router(L, d, x_dev, x_dtype, T, w, c->cur)))) return st;
-    if ((st = count(c, gw::launch_gateup(L, d, x_dev, x_dtype, T, w, c->cur)))) return st;
-    if ((st = count(c, gw::launch_down(L, d, T, w, c->cur)))) return st;
+    if ((st = count(c, gw::launch_expert_gemv(L, d, w, T, 0, c->cur)))) return st;
+    if ((st = count(c, gw::launch_expert_gemv(L, d, w, T, 1, c->cur)))) return st;
     if ((st = count(c, gw::launch_combine(d, T, w, out_dev, 0, nullptr, x_dtype, c->cur)))) return st;
     const size_t nk = (size_t)T * k;
     if (experts_dev)

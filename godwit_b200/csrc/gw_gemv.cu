@@ -1,0 +1,613 @@
+// gw_gemv.cu — decode expert GEMVs (gate_up + activation, down x routing
+// weight) over the HBM-resident bank.
+//
+// The reference evaluates each routed (expert, token) pair as
+// mxfp4_gemv_bias -> gptoss_expert_activation / expert_activation_swiglu ->
+// mxfp4_gemv_bias -> expert_accumulate (Metal/MoE/expert.metal:46-116,
+// :380-393; ExpertRunner.applyAssignments, Runtime/ExpertRunner.swift:108-183),
+// each block of 32 products summed in fp32 and then multiplied by the
+// block's E8M0 scale (Metal/Quant/dequant_gemv.metal:50-63).  This kernel does
+// the same arithmetic for every token routed to an expert from one pass over
+// the expert's weights.
+//
+// Layout and data movement.  The bank stores each MXFP4 matrix in 16-row
+// tiles, each tile in groups of eight 32-column blocks, a group's 16 rows x
+// 128 bytes row-major (2 KB; the last group of a row narrower when K/32 is not
+// a multiple of 8).  A CTA has kEW consumer warps, each owning one tile (or a
+// K-split share of one), and one producer warp.  Per stage the producer
+// issues one TMA box that holds the same group of all the CTA's tiles (16 KB,
+// 128-byte swizzle, so the consumers' reads are free of bank conflicts) and
+// one box of their scale bytes, into a kEStages-deep ring of stages guarded
+// by full / empty mbarriers; the consumers only wait, compute and release.
+// The tokens' f16 rows are staged once per pass of up to four tokens, laid
+// out as the MMA's B fragments.
+//
+// Arithmetic.  mma.sync.m16n8k16 (f16 x f16 -> fp32) with the 16 weight rows
+// as M.  Thread (g, t) feeds K-columns 8t..8t+7 of each 32-column block —
+// byte t*4..t*4+3 of each of its two rows, widened with cvt.rn.f16x2.e2m1x2 —
+// so one MMA pair covers exactly one block and the B fragment is one 16-byte
+// shared load.  The 8 N-columns hold (block slot, token): 8 blocks x 1
+// token, 4 x 2 or 2 x 4 (by the pass's token count), the B operand of a
+// column being zero outside its block slot; after each window of blocks the
+// fp32 partials are multiplied by their block's scale into fp32 accumulators
+// (the reference's `acc += partial * scale`).
+//
+// Every wait on an mbarrier is bounded (~2 s); a wait that runs out sets a
+// bit in the status word, the CTA stops computing but keeps its barrier
+// protocol, and the producer waits (bounded) for the copies it has in flight
+// before the CTA exits.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+#include "gw_async.cuh"
+#include "gw_device.cuh"
+#include "gw_internal.h"
+
+namespace gw {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();  // gw_grouped.cu
+
+namespace {
+
+constexpr int kEW = 24;                      // consumer warps per CTA (one CTA per SM)
+constexpr int kEThreads = (kEW + 1) * 32;    // + the producer warp
+constexpr int kEStages = 3;                  // stages in flight per CTA
+constexpr int kEPass = 4;                    // tokens per pass over the weights
+constexpr int kGrp = 2048;                   // one tile's full group: 16 rows x 128 bytes
+constexpr int kGrpSc = 128;                  // its scale bytes
+constexpr int kStageW = kEW * kGrp;          // 48 KB of weights per stage
+constexpr int kStageS = kEW * kGrpSc;        // 3 KB of scales per stage
+constexpr unsigned kStatusGemv = 0x200u;
+// try_wait suspends the waiting threads up to this long (they wake as soon as
+// the phase completes).
+constexpr uint32_t kSuspendNs = 100000;
+
+struct ExpertGemvArgs {
+    const uint8_t* base;   // local expert 0 of the layer
+    int64_t stride;        // bytes per expert
+    int64_t off_bias;
+    int M, K;              // matrix rows, columns
+    int ksplit;            // K-splits (tiles per split = kEW / ksplit)
+    int rounds;            // tile rounds per CTA: round r covers kEW / ksplit tiles
+    int k, shard_count;
+    int F, H;
+    float limit, alpha;
+    MoeWork w;
+};
+
+// The four TMA views of one matrix of the layer's bank (see launch_expert_gemv).
+struct GemvMaps {
+    CUtensorMap w_full, w_narrow, s_full, s_narrow;
+};
+
+// Shared-memory carve-up (dynamic; the base is aligned to 1024 for the
+// 128-byte swizzle).  The staged tokens are laid out for the MMA's B operand
+// directly: entry (group, block j, column g) is the 64 bytes lane group g
+// reads for block j — the block of x of the column's token when the column's
+// block slot is j's, else zeros — so no lane selects between x and zero.
+struct SmemPlan {
+    int ring, sc, xe, red, bars, total;
+};
+
+__host__ __device__ inline SmemPlan smem_plan(int K) {
+    const int ngrp = (K / 32 + 7) / 8;
+    SmemPlan p;
+    p.ring = 0;
+    p.sc = p.ring + kEStages * kStageW;
+    p.xe = p.sc + kEStages * kStageS;
+    p.red = p.xe + ngrp * 8 * 8 * 64;
+    p.bars = p.red + 2 * kEW * 2 * 8 * kEPass * 4;
+    p.total = p.bars + 2 * kEStages * 8 + 16 + 1024;  // + abort flag, alignment slack
+    return p;
+}
+
+// Shared-memory reads as plain C++ loads (the compiler schedules them; the
+// barrier waits' "memory" clobbers keep them after the data has landed).
+__device__ __forceinline__ uint32_t ld32(const unsigned char* p) { return *reinterpret_cast<const uint32_t*>(p); }
+__device__ __forceinline__ uint4 ld128(const unsigned char* p) { return *reinterpret_cast<const uint4*>(p); }
+
+// One 5-D tile of `map` at (0, 0, c2, c3, c4) -> shared, counted on `bar`.
+__device__ __forceinline__ void tma_5d(uint32_t dst, const CUtensorMap* map, int c2, int c3, int c4,
+                                       uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %2, "
+        "%3, %4, %5}], [%6];" ::"r"(dst),
+        "l"(map), "r"(0), "r"(c2), "r"(c3), "r"(c4), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void arrive_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool try_parity(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(kSuspendNs)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait on a phase; false once it ran out (status bit set).
+__device__ __forceinline__ bool wait_parity(uint32_t bar, uint32_t parity, unsigned* status) {
+    if (try_parity(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (uint32_t i = 1;; ++i) {
+        if (try_parity(bar, parity)) return true;
+        if ((i & 63) == 0 && clock64() - t0 > kWaitCycles) {
+            if (status) atomicOr(status, kStatusGemv);
+            return false;
+        }
+    }
+}
+
+
+// d = A B (the accumulator starts from zero)
+__device__ __forceinline__ void mma_f16_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%10, %10, %10, %10};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
+}
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ float e8m0(uint32_t byte) { return __uint_as_float(byte << 23); }  // gemv_scale
+
+// One group of one warp's tile: w blocks (w = 8 for a full, 128-byte-swizzled
+// group, else a narrow unswizzled one), rows rA / rB of the tile as the MMA's
+// rows g / g + 8, kTok tokens per MMA (8 / kTok block slots).  xg: this
+// lane's B entries of the group (entry (j, g), quarter t).  Accumulates
+// acc[row][column of the lane].
+template <int kTok, bool kFull>
+__device__ __forceinline__ void group_mma(const unsigned char* A, const unsigned char* Sc, int w, int rA, int rB,
+                                          const unsigned char* xg, int t, float (&acc)[2][2]) {
+    constexpr int kBlk = 8 / kTok;
+    const int wl = kFull ? 8 : w;
+    const int sw = kFull ? 8 : w;  // scale bytes per row
+    auto scale = [&](int r, int i) -> float {
+        return (kFull || i < wl) ? e8m0(Sc[r * sw + i]) : 0.f;
+    };
+    const unsigned char* rowA = A + (kFull ? rA * 128 : rA * 16 * w) + 4 * t;
+    const unsigned char* rowB = A + (kFull ? rB * 128 : rB * 16 * w) + 4 * t;
+    float d0[4], d1[4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        if (!kFull && j % kBlk == 0) {  // a narrow group may end before its window does
+#pragma unroll
+            for (int q = 0; q < 4; ++q) d0[q] = d1[q] = 0.f;
+        }
+        if (kFull || j < wl) {
+            const uint32_t wa = ld32(rowA + (kFull ? ((j ^ (rA & 7)) << 4) : j * 16));
+            const uint32_t wb = ld32(rowB + (kFull ? ((j ^ (rB & 7)) << 4) : j * 16));
+            const uint4 xv = ld128(xg + j * 512);
+            uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+            e2m1x8_to_f16x8(wa, a0, a1, a2, a3);
+            e2m1x8_to_f16x8(wb, b0, b1, b2, b3);
+            if (kFull && j % kBlk == 0) {  // the window's first block starts the accumulators
+                mma_f16_z(d0, a0, b0, a1, b1, xv.x, xv.y);
+                mma_f16_z(d1, a2, b2, a3, b3, xv.z, xv.w);
+            } else {
+                mma_f16(d0, a0, b0, a1, b1, xv.x, xv.y);
+                mma_f16(d1, a2, b2, a3, b3, xv.z, xv.w);
+            }
+        }
+        if (j % kBlk == kBlk - 1) {  // flush the window of blocks [j - kBlk + 1, j]
+            const int jb = j - kBlk + 1;
+            if (kTok == 1) {  // columns 2t, 2t + 1 = blocks 2t, 2t + 1
+                acc[0][0] = fmaf(d0[0] + d1[0], scale(rA, 2 * t), acc[0][0]);
+                acc[0][0] = fmaf(d0[1] + d1[1], scale(rA, 2 * t + 1), acc[0][0]);
+                acc[1][0] = fmaf(d0[2] + d1[2], scale(rB, 2 * t), acc[1][0]);
+                acc[1][0] = fmaf(d0[3] + d1[3], scale(rB, 2 * t + 1), acc[1][0]);
+            } else {  // columns 2t, 2t + 1 share one block
+                const int bi = jb + (kTok == 2 ? t : (t >> 1));
+                const float fa = scale(rA, bi), fb = scale(rB, bi);
+                acc[0][0] = fmaf(d0[0] + d1[0], fa, acc[0][0]);
+                acc[0][1] = fmaf(d0[1] + d1[1], fa, acc[0][1]);
+                acc[1][0] = fmaf(d0[2] + d1[2], fb, acc[1][0]);
+                acc[1][1] = fmaf(d0[3] + d1[3], fb, acc[1][1]);
+            }
+        }
+    }
+}
+
+// True on one lane of the (converged) warp.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred;
+    asm volatile(
+        "{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\tselp.u32 %0, 1, 0, P;\n\t}"
+        : "=r"(pred));
+    return pred != 0;
+}
+__device__ __forceinline__ void arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// the kEW consumer warps only
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kEW * 32) : "memory"); }
+
+__device__ __forceinline__ void tma_4d(uint32_t dst, const CUtensorMap* map, int c1, int c2, int c3, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+        "%4, %5}], [%6];" ::"r"(dst),
+        "l"(map), "r"(0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void tma_3d(uint32_t dst, const CUtensorMap* map, int c1, int c2, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+        "%4}], [%5];" ::"r"(dst),
+        "l"(map), "r"(0), "r"(c1), "r"(c2), "r"(bar)
+        : "memory");
+}
+
+// kMode 0 / 1: gate_up with the clamped GLU / SiLU epilogue (f16 activations
+// per slot); 2: down x routing weight (fp32 per slot).
+// grid (min(E, T*k), ceil(tiles / (kEW / ksplit))), kEThreads threads.
+template <int kMode>
+__global__ void __launch_bounds__(kEThreads, 1) k_expert_gemv(const __grid_constant__ GemvMaps maps,
+                                                              ExpertGemvArgs a) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int ai = blockIdx.x;
+    if (ai >= *a.w.nactive) return;
+    const int e = a.w.active[ai];
+    const SmemPlan P = smem_plan(a.K);
+    const uint32_t sbase = (saddr(smem_raw) + 1023u) & ~1023u;
+    unsigned char* sgen = smem_raw + (sbase - saddr(smem_raw));
+    __shared__ int meta_row[kEPass], meta_slot[kEPass];
+    __shared__ float meta_mul[kEPass];
+
+    // the warp index through a shuffle: the compiler then knows every value
+    // derived from it is warp-uniform
+    const int warp = __shfl_sync(0xffffffffu, (int)(threadIdx.x >> 5), 0);
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int nblk = a.K >> 5, nfull = nblk >> 3, ngrp = (nblk + 7) >> 3;
+    const int wlast = nblk - 8 * (ngrp - 1);
+    const int ntiles = a.M >> 4;
+    const int ks = a.ksplit, tb = kEW / ks;
+    const int per = (ngrp + ks - 1) / ks;           // stages per pass
+    const int cnt = min(a.w.counts[e], a.w.tcap);
+    const int npass = (cnt + kEPass - 1) / kEPass;
+    const int R = a.rounds;
+    const int total = per * R * npass;
+    const int le = e / a.shard_count;
+    const int tile0 = blockIdx.y * tb * R;
+    // Within a stage, split sp owns the region a full box would fill (tb
+    // tiles x 2 KB of weights, tb x 128 B of scales) whether its group is full
+    // or narrow: a stage can mix the two, and every TMA destination starts on a
+    // 128-byte boundary.
+    unsigned* status = a.w.status;
+    const uint32_t fullb = sbase + P.bars, emptyb = fullb + kEStages * 8;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(sgen + P.bars + 2 * kEStages * 8);
+
+    if (threadIdx.x < kEStages) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(fullb + threadIdx.x * 8) : "memory");
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(emptyb + threadIdx.x * 8), "n"(kEW) : "memory");
+    }
+    if (threadIdx.x == 0) *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    __syncthreads();
+
+    if (warp == kEW) {
+        // ---- producer: stage i = (pass, round r, step s) in that nesting;
+        // split sp's group sp * per + s of tiles tile0 + r * tb ...
+        if (elect_one()) {
+            int slot = 0, s = 0, r = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int i = 0; i < total; ++i) {
+                if (i >= kEStages && ok) {
+                    ok = wait_parity(emptyb + slot * 8, phase ^ 1, status);
+                    if (!ok) *abort_flag = 1;
+                }
+                if (ok && *abort_flag) ok = false;
+                if (!ok) break;
+                uint32_t bytes = 0;
+                for (int sp = 0; sp < ks; ++sp) {
+                    const int grp = sp * per + s;
+                    if (grp >= min(ngrp, (sp + 1) * per)) continue;
+                    bytes += grp < nfull ? (uint32_t)tb * (kGrp + kGrpSc) : (uint32_t)tb * 17u * 16u * wlast;
+                }
+                const uint32_t bar = fullb + slot * 8;
+                arrive_tx(bar, bytes);
+                for (int sp = 0; sp < ks; ++sp) {
+                    const int grp = sp * per + s;
+                    if (grp >= min(ngrp, (sp + 1) * per)) continue;
+                    const uint32_t wdst = sbase + P.ring + slot * kStageW;
+                    const uint32_t sdst = sbase + P.sc + slot * kStageS;
+                    if (grp < nfull) {
+                        tma_5d(wdst + sp * tb * kGrp, &maps.w_full, grp, tile0 + r * tb, le, bar);
+                        tma_4d(sdst + sp * tb * kGrpSc, &maps.s_full, grp, tile0 + r * tb, le, bar);
+                    } else {
+                        tma_4d(wdst + sp * tb * kGrp, &maps.w_narrow, 0, tile0 + r * tb, le, bar);
+                        tma_3d(sdst + sp * tb * kGrpSc, &maps.s_narrow, tile0 + r * tb, le, bar);
+                    }
+                }
+                if (++s == per) {
+                    s = 0;
+                    if (++r == R) r = 0;
+                }
+                if (++slot == kEStages) { slot = 0; phase ^= 1; }
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---- consumers
+        const int sp = warp / tb, tl = warp % tb;
+
+        const int g0 = min(ngrp, sp * per), g1 = min(ngrp, g0 + per);
+        const bool leader = elect_one();
+        // rows of the tile this lane feeds as MMA rows g and g + 8: down takes
+        // rows g, g + 8; gate_up takes feature g's gate and up rows (2g, 2g + 1),
+        // in the order that keeps the eight row-reads of a quad phase on
+        // distinct 128-byte-swizzle chunks.
+        int rA, rB;
+        if (kMode == 2) { rA = g; rB = g + 8; }
+        else if (g < 4) { rA = 2 * g; rB = 2 * g + 1; }
+        else { rA = 2 * g + 1; rB = 2 * g; }
+        const int* list = a.w.lists + (int64_t)e * a.w.tcap;
+        const __half* xsrc = kMode == 2 ? a.w.act : a.w.x16;
+        const unsigned char* xg0 = sgen + P.xe + g * 64 + 16 * t;
+        float* red0 = reinterpret_cast<float*>(sgen + P.red);
+        // this thread's fixed share of the B-entry staging: quarter q of
+        // column c of block j of every (kEW / 8)-th group from grp0
+        const int sq = threadIdx.x & 3, sc_ = (threadIdx.x >> 2) & 7, sj = (threadIdx.x >> 5) & 7;
+        const int sgrp0 = threadIdx.x >> 8;
+        bool ok = true;
+        int slot = 0;
+        uint32_t phase = 0;
+        for (int p = 0; p < npass; ++p) {
+            const int c0 = p * kEPass, n = min(kEPass, cnt - c0);
+            consumers_sync();  // the previous pass's staged x, results and metadata are consumed
+            if (threadIdx.x < n) {
+                const int sl = list[c0 + threadIdx.x];
+                const int row = kMode == 2 ? sl : sl / a.k;
+                meta_slot[threadIdx.x] = sl;
+                meta_row[threadIdx.x] = row;
+                meta_mul[threadIdx.x] = kMode == 2 ? a.w.weights[sl] : a.w.xmul[row];
+            }
+            consumers_sync();
+            {  // B entries: (group, block j, column c) <- x[token of c][block] or zeros
+                bool live;
+                int tok;
+                if (n == 1) { live = sj == sc_; tok = 0; }
+                else if (n == 2) { live = (sj & 3) == (sc_ >> 1); tok = sc_ & 1; }
+                else { live = (sj & 1) == (sc_ >> 2); tok = sc_ & 3; }
+                live = live && tok < n;
+                const uint4* src = reinterpret_cast<const uint4*>(xsrc + (int64_t)(live ? meta_row[tok] : 0) * a.K) +
+                                   sj * 4 + sq;
+                uint4* dst = reinterpret_cast<uint4*>(sgen + P.xe) + (threadIdx.x & 255);
+                for (int grp = sgrp0; grp < ngrp; grp += kEW / 8) {
+                    const bool in = live && grp * 8 + sj < nblk;
+                    dst[grp * 256] = in ? __ldg(src + grp * 32) : make_uint4(0u, 0u, 0u, 0u);
+                }
+            }
+            consumers_sync();
+          for (int r = 0; r < R; ++r) {
+            const int tile = tile0 + r * tb + tl;
+            const bool valid = tile < ntiles;
+            float* red = red0 + (r & 1) * (kEW * 2 * 8 * kEPass);  // double-buffered by round
+            float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+            for (int s = 0; s < per; ++s) {
+                if (ok) {
+                    ok = try_parity(fullb + slot * 8, phase) || wait_parity(fullb + slot * 8, phase, status);
+                    if (!ok) *abort_flag = 1;
+                }
+                ok = __all_sync(0xffffffffu, ok) && !*abort_flag;
+                const int grp = g0 + s;
+                if (ok && valid && grp < g1) {
+                    if (grp < nfull) {
+                        const unsigned char* A = sgen + P.ring + slot * kStageW + warp * kGrp;
+                        const unsigned char* Sc = sgen + P.sc + slot * kStageS + warp * kGrpSc;
+                        const unsigned char* xg = xg0 + grp * 4096;
+                        if (n == 1) group_mma<1, true>(A, Sc, 8, rA, rB, xg, t, acc);
+                        else if (n == 2) group_mma<2, true>(A, Sc, 8, rA, rB, xg, t, acc);
+                        else group_mma<4, true>(A, Sc, 8, rA, rB, xg, t, acc);
+                    } else {
+                        const unsigned char* A = sgen + P.ring + slot * kStageW + sp * tb * kGrp + tl * 256 * wlast;
+                        const unsigned char* Sc = sgen + P.sc + slot * kStageS + sp * tb * kGrpSc + tl * 16 * wlast;
+                        const unsigned char* xg = xg0 + grp * 4096;
+                        if (n == 1) group_mma<1, false>(A, Sc, wlast, rA, rB, xg, t, acc);
+                        else if (n == 2) group_mma<2, false>(A, Sc, wlast, rA, rB, xg, t, acc);
+                        else group_mma<4, false>(A, Sc, wlast, rA, rB, xg, t, acc);
+                    }
+                }
+                __syncwarp();
+                if (leader) arrive(emptyb + slot * 8);  // this warp is done with the stage
+                if (++slot == kEStages) { slot = 0; phase ^= 1; }
+            }
+            if (valid) {  // (a K-split warp left without groups contributes zeros)
+                // columns -> (row, token): sum the block slots held by the quad
+                float v[2][2];
+#pragma unroll
+                for (int r = 0; r < 2; ++r) {
+                    if (n == 1) {
+                        float x = acc[r][0];
+                        x += __shfl_xor_sync(0xffffffffu, x, 1);
+                        x += __shfl_xor_sync(0xffffffffu, x, 2);
+                        v[r][0] = x;
+                        v[r][1] = 0.f;
+                    } else if (n == 2) {
+#pragma unroll
+                        for (int c = 0; c < 2; ++c) {
+                            float x = acc[r][c];
+                            x += __shfl_xor_sync(0xffffffffu, x, 1);
+                            x += __shfl_xor_sync(0xffffffffu, x, 2);
+                            v[r][c] = x;
+                        }
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < 2; ++c) v[r][c] = acc[r][c] + __shfl_xor_sync(0xffffffffu, acc[r][c], 2);
+                    }
+                }
+                // red[warp][r][g][token]; gate_up rows in (gate, up) order
+                float* rw = red + warp * (2 * 8 * kEPass);
+                const bool swap = kMode != 2 && g >= 4;
+                const float r00 = swap ? v[1][0] : v[0][0], r01 = swap ? v[1][1] : v[0][1];
+                const float r10 = swap ? v[0][0] : v[1][0], r11 = swap ? v[0][1] : v[1][1];
+                const int tk = n <= 2 ? 0 : 2 * t;
+                if ((n <= 2 && t == 0) || (n > 2 && t < 2)) {
+                    rw[0 * 8 * kEPass + g * kEPass + tk] = r00;
+                    rw[1 * 8 * kEPass + g * kEPass + tk] = r10;
+                    rw[0 * 8 * kEPass + g * kEPass + tk + 1] = r01;
+                    rw[1 * 8 * kEPass + g * kEPass + tk + 1] = r11;
+                }
+            }
+            consumers_sync();
+            // split-0 warps emit: lane (g, t) -> token t (the splits of a tile
+            // are warps tl, tl + tb, ...)
+            if (valid && sp == 0 && t < n && ok) {
+                float y0 = 0.f, y1 = 0.f;
+                for (int q = 0; q < ks; ++q) {
+                    const float* rw = red + (warp + q * tb) * (2 * 8 * kEPass);
+                    y0 += rw[0 * 8 * kEPass + g * kEPass + t];
+                    y1 += rw[1 * 8 * kEPass + g * kEPass + t];
+                }
+                const int sl = meta_slot[t];
+                const float mul = meta_mul[t];
+                const uint16_t* bias = reinterpret_cast<const uint16_t*>(a.base + (int64_t)le * a.stride + a.off_bias);
+                if (kMode != 2) {
+                    const int f = tile * 8 + g;
+                    const float gate = y0 * mul + bf16_bits_to_f32(bias[2 * f]);
+                    const float up = y1 * mul + bf16_bits_to_f32(bias[2 * f + 1]);
+                    a.w.act[(int64_t)sl * a.F + f] = __float2half_rn(activate<kMode>(gate, up, a.limit, a.alpha));
+                } else {
+                    const int r0 = tile * 16 + g;
+                    float* y = a.w.ybuf + (int64_t)sl * a.H;
+                    y[r0] = (y0 + bf16_bits_to_f32(bias[r0])) * mul;
+                    y[r0 + 8] = (y1 + bf16_bits_to_f32(bias[r0 + 8])) * mul;
+                }
+            }
+          }
+        }
+    }
+    __syncthreads();
+    // after a wait ran out: let the copies still in flight land before exit
+    if (warp == kEW && *abort_flag && elect_one())
+        for (int j = 0; j < kEStages; ++j) (void)wait_parity(fullb + j * 8, 0, nullptr), (void)wait_parity(fullb + j * 8, 1, nullptr);
+}
+
+// Smallest K-split (1, 2, 4 or 8 warps per tile) that gives the launch
+// about one and a half waves of CTAs (one per SM).
+int pick_split(int experts, int ntiles) {
+    int ks = 1;
+    while (ks < 8 && (int64_t)experts * ((ntiles * ks + kEW - 1) / kEW) < 222) ks *= 2;
+    return ks;
+}
+
+}  // namespace
+
+int configure_expert_gemv() {
+    const int bytes = smem_plan(kMaxGemvCols).total;
+    for (auto fn : {k_expert_gemv<0>, k_expert_gemv<1>, k_expert_gemv<2>})
+        if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return -1;
+    return 0;
+}
+
+bool expert_gemv_supported(const MoeDims& d) {
+    return d.H <= kMaxGemvCols && d.F <= kMaxGemvCols && tensor_map_encoder() != nullptr;
+}
+
+int launch_expert_gemv(const LayerView& L, const MoeDims& d, const MoeWork& w, int T, int which,
+                       cudaStream_t s) {
+    ExpertGemvArgs a;
+    a.base = L.base;
+    a.stride = L.stride;
+    int64_t off_pk, off_sc;
+    if (which == 0) {
+        a.M = 2 * d.F; a.K = d.H;
+        off_pk = L.off[0]; off_sc = L.off[1]; a.off_bias = L.off[4];
+    } else {
+        a.M = d.H; a.K = d.F;
+        off_pk = L.off[2]; off_sc = L.off[3]; a.off_bias = L.off[5];
+    }
+    if (a.K > kMaxGemvCols || a.K % 32 || a.M % 16) return -1;
+    a.k = d.k;
+    a.shard_count = d.shard_count;
+    a.F = d.F;
+    a.H = d.H;
+    a.limit = d.limit;
+    a.alpha = d.alpha;
+    a.w = w;
+    const int nblk = a.K / 32, nfull = nblk / 8, ntiles = a.M / 16;
+    const int wlast = nblk - 8 * ((nblk + 7) / 8 - 1);
+    const int e_local = (d.E - d.shard_rank + d.shard_count - 1) / d.shard_count;
+    const int maxa = std::min(d.E, T * d.k);
+    a.ksplit = pick_split(maxa, ntiles);
+    const int tb = kEW / a.ksplit;
+    // Several rounds of tiles per CTA amortise its set-up and token staging;
+    // keep at least ~4 waves of CTAs.
+    a.rounds = 1;
+    while (a.rounds < 8 && (int64_t)maxa * ((ntiles + tb * a.rounds * 2 - 1) / (tb * a.rounds * 2)) >= 4 * 148)
+        a.rounds *= 2;
+    // TMA views of the bank (uint8 elements; a tile is 16 * nblk * 16 bytes
+    // of blocks and 16 * nblk bytes of scales; experts one stride apart):
+    //   w_full   (128 B, 16 rows, full groups, tiles, experts), box (128, 16, 1, tb, 1), 128-byte swizzle
+    //   w_narrow (16 w B, 16 rows, tiles, experts) at the last group, box (16 w, 16, tb, 1)
+    //   s_full   (128 B, full groups, tiles, experts), box (128, 1, tb, 1)
+    //   s_narrow (16 w B, tiles, experts) at the last group, box (16 w, tb, 1)
+    // A view whose groups do not exist (no full or no narrow group) is encoded
+    // over the first group and never used.
+    GemvMaps maps;
+    auto enc = tensor_map_encoder();
+    if (!enc) return -1;
+    const uint8_t* pk = L.base + off_pk;
+    const uint8_t* sc = L.base + off_sc;
+    const cuuint64_t tile_pk = (cuuint64_t)nblk * 256, tile_sc = (cuuint64_t)nblk * 16, es = (cuuint64_t)L.stride;
+    const int wn = wlast < 8 ? wlast : 8;
+    const cuuint64_t nf = nfull > 0 ? nfull : 1;
+    const cuuint32_t ones[5] = {1, 1, 1, 1, 1};
+    bool good = true;
+    {
+        const cuuint64_t gd[5] = {128, 16, nf, (cuuint64_t)ntiles, (cuuint64_t)e_local};
+        const cuuint64_t gs[4] = {128, 2048, tile_pk, es};
+        const cuuint32_t box[5] = {128, 16, 1, (cuuint32_t)tb, 1};
+        good = good && enc(&maps.w_full, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, const_cast<uint8_t*>(pk), gd, gs, box,
+                           ones, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    }
+    {
+        const cuuint64_t gd[4] = {(cuuint64_t)16 * wn, 16, (cuuint64_t)ntiles, (cuuint64_t)e_local};
+        const cuuint64_t gs[3] = {(cuuint64_t)16 * wn, tile_pk, es};
+        const cuuint32_t box[4] = {(cuuint32_t)(16 * wn), 16, (cuuint32_t)tb, 1};
+        good = good && enc(&maps.w_narrow, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4,
+                           const_cast<uint8_t*>(pk + (wlast < 8 ? (int64_t)nfull * 2048 : 0)), gd, gs, box, ones,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    }
+    {
+        const cuuint64_t gd[4] = {128, nf, (cuuint64_t)ntiles, (cuuint64_t)e_local};
+        const cuuint64_t gs[3] = {128, tile_sc, es};
+        const cuuint32_t box[4] = {128, 1, (cuuint32_t)tb, 1};
+        good = good && enc(&maps.s_full, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<uint8_t*>(sc), gd, gs, box,
+                           ones, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    }
+    {
+        const cuuint64_t gd[3] = {(cuuint64_t)16 * wn, (cuuint64_t)ntiles, (cuuint64_t)e_local};
+        const cuuint64_t gs[2] = {tile_sc, es};
+        const cuuint32_t box[3] = {(cuuint32_t)(16 * wn), (cuuint32_t)tb, 1};
+        good = good && enc(&maps.s_narrow, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3,
+                           const_cast<uint8_t*>(sc + (wlast < 8 ? (int64_t)nfull * 128 : 0)), gd, gs, box, ones,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    }
+    if (!good) return -1;
+    const dim3 grid(maxa, (ntiles + tb * a.rounds - 1) / (tb * a.rounds));
+    const int smem = smem_plan(a.K).total;
+    if (which == 1) k_expert_gemv<2><<<grid, kEThreads, smem, s>>>(maps, a);
+    else if (d.act == 0) k_expert_gemv<0><<<grid, kEThreads, smem, s>>>(maps, a);
+    else k_expert_gemv<1><<<grid, kEThreads, smem, s>>>(maps, a);
+    return cudaPeekAtLastError() == cudaSuccess ? 1 : -1;
+}
+
+}  // namespace gw

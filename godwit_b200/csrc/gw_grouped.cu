@@ -921,6 +921,9 @@ __global__ void k_rowexp(const uint8_t* __restrict__ scales, int rows, int nblk,
     out[r] = (uint8_t)(m == 0 ? 127 : m);
 }
 
+}  // namespace
+
+// cuTensorMapEncodeTiled from the driver, resolved once (nullptr if absent).
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;
@@ -934,7 +937,6 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-}  // namespace
 
 int configure_grouped() {
     const void* fns[6] = {(const void*)k_grouped<0, false>, (const void*)k_grouped<1, false>,

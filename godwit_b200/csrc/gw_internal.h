@@ -12,8 +12,7 @@ constexpr int kMaxTopK = 16;
 constexpr int kMaxExperts = 256;
 constexpr int kTokTile = 8;       // tokens per router CTA
 constexpr int kRouterMmaMinTokens = 128;  // bf16 batches from here on use k_router_mma
-constexpr int kChunk = 4;         // tokens per weight pass of an expert GEMV tile
-constexpr int kGemvWarps = 4;     // warps per GEMV CTA (one 16-row tile each)
+constexpr int kGemvWarps = 4;     // warps per k_gemv CTA (one 16-row tile each)
 
 // Element types of activation inputs.  F32 is internal: the residual stream
 // that the stack forward rounds to the configured input type.
@@ -69,9 +68,6 @@ int launch_router(const LayerView& L, const MoeDims& d, const void* x, int x_dty
                   const MoeWork& w, cudaStream_t s);
 int launch_group(const MoeDims& d, const int32_t* experts_in, const float* weights_in, int T,
                  const MoeWork& w, cudaStream_t s);
-int launch_gateup(const LayerView& L, const MoeDims& d, const void* x, int x_dtype, int T,
-                  const MoeWork& w, cudaStream_t s);
-int launch_down(const LayerView& L, const MoeDims& d, int T, const MoeWork& w, cudaStream_t s);
 int launch_combine(const MoeDims& d, int T, const MoeWork& w, float* out, int accumulate,
                    void* x_next, int x_dtype, cudaStream_t s);
 int launch_gemv_batched(int count, const uint8_t* packed, int64_t packed_stride,
@@ -98,20 +94,20 @@ int launch_tile_layout(const uint8_t* src, uint8_t* dst, int rows, int cols, int
 constexpr unsigned kStatusProbe = 0x100u;
 int launch_wait_probe(unsigned* status, long long limit, cudaStream_t s);
 int launch_widen(const void* x, int x_dtype, float* stream, int64_t n, cudaStream_t s);
-size_t gemv_smem_bytes(int cols, int max_tok);
+size_t gemv_smem_bytes(int cols);
 // Tensor-core grouped expert GEMM (gw_grouped.cu): which 0 = gate_up + activation,
 // 1 = down + routing weight.  `sms` persistent CTAs.
 int launch_grouped(const LayerView& L, const MoeDims& d, const MoeWork& w, int which, int sms,
                    cudaStream_t s, const void* x = nullptr, int x_dtype = 0);
 bool grouped_supported(const MoeDims& d, const MoeWork& w);
 int configure_grouped();
-// Decode expert GEMVs with bulk-copied weights (gw_stream.cu): which 0 =
-// gate_up + activation, 1 = down + routing weight; `sms` persistent CTAs.
-constexpr int kStreamMaxCols = 4096;
-int launch_stream(const LayerView& L, const MoeDims& d, const MoeWork& w, int which, int sms,
-                  cudaStream_t s);
-bool stream_supported(const MoeDims& d, const MoeWork& w);
-int configure_stream(int max_cols);
+// Decode expert GEMVs (gw_gemv.cu): which 0 = gate_up + activation, 1 =
+// down + routing weight, for layers of T tokens on the GEMV path.
+constexpr int kMaxGemvCols = 3072;  // the expert GEMV stages up to 12 groups of token blocks
+int launch_expert_gemv(const LayerView& L, const MoeDims& d, const MoeWork& w, int T, int which,
+                       cudaStream_t s);
+bool expert_gemv_supported(const MoeDims& d);
+int configure_expert_gemv();
 // Row-exponent table entries of a row-major scale matrix.
 int launch_rowexp(const uint8_t* scales, int rows, int cols, uint8_t* out, cudaStream_t s);
 int configure_kernels();

@@ -76,12 +76,6 @@ class Context:
         expert inputs and activations quantised to MXFP8) instead of exact f16."""
         call("gw_set_block_scaled", self.handle, 1 if enable else 0)
 
-    def set_decode_streaming(self, enable: bool) -> None:
-        """Decode-size layers stream the expert weights with bulk copies into a
-        shared-memory ring, or (default) read them with per-thread loads; the
-        results agree to fp32 summation order."""
-        call("gw_set_decode_streaming", self.handle, 1 if enable else 0)
-
     def set_tensor_core_min_tokens(self, min_avg: int) -> None:
         """Experts of a layer run as tensor-core grouped GEMMs when
         T * top_k >= min_avg * experts, else as MXFP4 GEMV tiles (0: always

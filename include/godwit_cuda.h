@@ -138,11 +138,6 @@ GW_API gw_status gw_selftest_wait_timeout(gw_ctx* ctx, int64_t wait_cycles);
  * T * top_k >= min_avg * experts, else as the MXFP4 GEMV tiles; 0 = always
  * the GEMV tiles.  Default 8. */
 GW_API gw_status gw_set_tensor_core_min_tokens(gw_ctx* ctx, int32_t min_avg);
-/* Decode-size layers (below the tensor-core threshold): 1 streams the expert
- * weights with bulk copies into a shared-memory ring consumed by the MXFP4
- * GEMV tiles (k_stream); 0 (default, currently the faster) runs the same
- * tiles on per-thread loads.  The results agree to fp32 summation order. */
-GW_API gw_status gw_set_decode_streaming(gw_ctx* ctx, int32_t enable);
 /* Tensor-core expert path arithmetic: 0 (default) = exact f16 activations
  * (the reference's numerics, fp32 accumulation); 1 = tcgen05 block-scaled
  * MXFP4 x MXFP8 MMAs, the expert inputs and activations quantised to MXFP8
@@ -299,7 +294,7 @@ GW_API gw_status gw_moe_block_async(gw_ctx* ctx, gw_bank* bank, int32_t layer, f
  * the array: calls that overlap on the GPU (other streams, other contexts of
  * the same device) race.  The experts always run on the MXFP4 GEMV tiles:
  * the context's expert-path switches (gw_set_tensor_core_min_tokens,
- * gw_set_block_scaled, gw_set_decode_streaming) do not apply here, so its
+ * gw_set_block_scaled) do not apply here, so its
  * results equal gw_moe_forward_async's whenever that call runs the GEMV
  * tiles too (always at decode sizes under the default policy). */
 GW_API gw_status gw_moe_forward_noalloc_async(gw_ctx* ctx, gw_bank* bank, int32_t layer,
