@@ -281,6 +281,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prefill-f16", action="store_true",
                     help="oss120-prefill: exact f16 activations instead of config 4's MXFP8 block-scaled MMAs")
+    ap.add_argument("--ep", default="alltoall", choices=["alltoall", "replicated"],
+                    help="expert parallelism at N > 1: token-sliced all-to-all (default) or replicated tokens")
     ap.add_argument("--layers", type=int, default=None,
                     help="profiling only: hold and run this many layers instead of the model's")
     args = ap.parse_args()
@@ -360,7 +362,7 @@ def run_decode(args):
     import torch
 
     from godwit_b200 import device as D
-    from godwit_b200.ep import CudaOps, ReplicatedTokensEP
+    from godwit_b200.ep import AllToAllEP, CudaOps, ReplicatedTokensEP
     from godwit_b200.layout import PRESETS
     from godwit_b200.runtime import Context, ExpertBank
     from godwit_b200 import synth
@@ -394,19 +396,35 @@ def run_decode(args):
         skew = {"hot_experts": list(HOT_EXPERTS), "delta": round(float(delta), 5),
                 "hot_mean_tokens": float(h[list(HOT_EXPERTS)].mean()),
                 "other_mean_tokens": float(np.delete(h, list(HOT_EXPERTS)).mean())}
-    x_host = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).pin_memory()
-    out_host = torch.empty(T, H, dtype=torch.float32).pin_memory()
+    # At N > 1 each rank holds a slice of the batch (token-sliced expert
+    # parallelism, AllToAllEP: the experts of slot rows are applied by their
+    # owner after an all-to-all, outputs return by a second one); with
+    # --ep replicated every rank holds all T tokens and the partial sums meet
+    # in an all-reduce per layer.
+    sliced = world > 1 and args.ep == "alltoall"
+    per = -(-T // world)
+    t0, t1 = (min(T, rank * per), min(T, (rank + 1) * per)) if sliced else (0, T)
+    Tr = t1 - t0
+    x_host = torch.from_numpy(np.ascontiguousarray(xb[t0:t1]).view(np.int16)).view(torch.bfloat16).pin_memory()
+    out_host = torch.empty(Tr, H, dtype=torch.float32).pin_memory()
     x = x_host.to("cuda")
-    stream_buf = torch.empty(T, H, dtype=torch.float32, device="cuda")
+    stream_buf = torch.empty(Tr, H, dtype=torch.float32, device="cuda")
     partial = torch.empty_like(stream_buf)
     x_work = torch.empty_like(x)
-    ep = ReplicatedTokensEP(CudaOps(ctx, bank), spec.layers)
+    if sliced:
+        ep = AllToAllEP(CudaOps(ctx, bank), spec.layers, spec.top_k,
+                        capacity_factor=2.0 if prefill else None)
+    else:
+        ep = ReplicatedTokensEP(CudaOps(ctx, bank), spec.layers)
 
     def step():
         if world == 1:
             D.moe_stack(ctx, bank, x, stream_buf)
         else:
-            ep.forward(x, stream_buf, partial, x_work)
+            if sliced:
+                ep.forward(x, stream_buf, x_work)
+            else:
+                ep.forward(x, stream_buf, partial, x_work)
 
     def step_e2e():
         x.copy_(x_host, non_blocking=True)
@@ -509,12 +527,13 @@ def run_decode(args):
                        f"{desc} (profiling run: {spec.layers} layers)", "model_shape": spec.name,
                        "layers": spec.layers, "experts": spec.experts, "top_k": spec.top_k,
                        "hidden": spec.hidden, "intermediate": spec.intermediate, "tokens": T,
-                       "parallelism": f"ep{world}" if world > 1 else "single",
+                       "parallelism": (f"ep{world} ({'all-to-all, tokens sliced ' + str(per) + ' per rank' if sliced else 'replicated tokens, all-reduce per layer'})"
+                                       if world > 1 else "single"),
                        "l2": "weights streamed per step >> 126 MB L2 (no flush needed)",
                        "bank_fill_s": round(fill_s, 2), "bank_bytes": bank.nbytes(),
                        **({"skew": skew} if skew else {})},
             "e2e": {"value": T / (e2e_ms / 1e3), "unit": unit, "ms_per_step": e2e_ms,
-                    "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 4},
+                    "h2d_bytes_per_step": Tr * H * 2, "d2h_bytes_per_step": Tr * H * 4},
             "gpu_launches": launches,
             "roofline": roofline,
             "clocks": clocks,

@@ -288,7 +288,7 @@ gw_status log_nactive(gw_ctx* c) {
 // if x_next is given it receives round(out) in x_dtype.
 gw_status moe_layer_device(gw_ctx* c, gw_bank* b, int layer, const void* x_dev, int x_dtype,
                            int T, const int32_t* experts_in, const float* weights_in, float* out,
-                           int accumulate, void* x_next) {
+                           int accumulate, void* x_next, int64_t slots_hint = -1) {
     const gw::MoeDims d = dims_of(b);
     const gw::LayerView L = layer_of(b, layer);
     gw_status st = ensure_work(c, b, T);
@@ -303,7 +303,9 @@ gw_status moe_layer_device(gw_ctx* c, gw_bank* b, int layer, const void* x_dev, 
         st = timed_launch(c, 3, 0, [&] { return gw::launch_router(L, d, x_dev, x_dtype, T, w, c->cur); });
     if (st) return st;
     // Many tokens per expert: the tensor-core grouped GEMMs; few: the GEMV tiles.
-    const bool mma = w.mma_min_avg > 0 && (int64_t)T * d.k >= (int64_t)w.mma_min_avg * d.E &&
+    // the slots the layer will compute, at most T * k
+    const int64_t slots = slots_hint >= 0 ? slots_hint : (int64_t)T * d.k;
+    const bool mma = w.mma_min_avg > 0 && slots >= (int64_t)w.mma_min_avg * d.E &&
                      gw::grouped_supported(d, w);
     if ((st = timed_launch(c, 0, 0, [&] {
              return mma ? gw::launch_grouped(L, d, w, 0, c->sms, c->cur, x_dev, x_dtype)
@@ -891,8 +893,11 @@ gw_status gw_moe_apply_async(gw_ctx* c, gw_bank* b, int32_t layer, const void* x
     if (T <= 0) return fail(GW_E_ARG, "T must be positive");
     CtxLock lk(c);
     if ((st = set_device(c))) return st;
+    // rows given to this entry point usually carry one expert each (the
+    // per-rank half of expert parallelism), so the expert path is chosen as
+    // for T slots rather than T * top_k
     return moe_layer_device(c, b, layer, x_dev, x_dtype, T, experts_dev, weights_dev, out_dev,
-                            accumulate ? 1 : 0, nullptr);
+                            accumulate ? 1 : 0, nullptr, (int64_t)T);
 }
 
 gw_status gw_residual_round_async(gw_ctx* c, float* stream_dev, const float* delta_dev,

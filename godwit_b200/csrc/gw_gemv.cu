@@ -13,9 +13,9 @@
 // Layout and data movement.  The bank stores each MXFP4 matrix in 16-row
 // tiles, each tile in groups of eight 32-column blocks, a group's 16 rows x
 // 128 bytes row-major (2 KB; the last group of a row narrower when K/32 is not
-// a multiple of 8).  A CTA has kEW consumer warps, each owning one tile (or a
-// K-split share of one), and one producer warp.  Per stage the producer
-// issues one TMA box that holds the same group of all the CTA's tiles (16 KB,
+// a multiple of 8).  A CTA has kEW consumer warps, each owning kNT tiles (or
+// a K-split share of them), and one producer warp.  Per stage the producer
+// issues one TMA box that holds the same group of all the CTA's tiles (48 KB,
 // 128-byte swizzle, so the consumers' reads are free of bank conflicts) and
 // one box of their scale bytes, into a kEStages-deep ring of stages guarded
 // by full / empty mbarriers; the consumers only wait, compute and release.
@@ -54,13 +54,16 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();  // gw_grouped.cu
 namespace {
 
 constexpr int kEW = 24;                      // consumer warps per CTA (one CTA per SM)
+constexpr int kNT = 1;                       // tiles per consumer warp
+constexpr int kCT = kEW * kNT;               // tiles per stage (per round)
+constexpr int kBoxT = 6;                     // tiles per TMA box of weights (divides kCT / 4)
 constexpr int kEThreads = (kEW + 1) * 32;    // + the producer warp
 constexpr int kEStages = 3;                  // stages in flight per CTA
 constexpr int kEPass = 4;                    // tokens per pass over the weights
 constexpr int kGrp = 2048;                   // one tile's full group: 16 rows x 128 bytes
 constexpr int kGrpSc = 128;                  // its scale bytes
-constexpr int kStageW = kEW * kGrp;          // 48 KB of weights per stage
-constexpr int kStageS = kEW * kGrpSc;        // 3 KB of scales per stage
+constexpr int kStageW = kCT * kGrp;          // 48 KB of weights per stage
+constexpr int kStageS = kCT * kGrpSc;        // 3 KB of scales per stage
 constexpr unsigned kStatusGemv = 0x200u;
 // try_wait suspends the waiting threads up to this long (they wake as soon as
 // the phase completes).
@@ -71,8 +74,8 @@ struct ExpertGemvArgs {
     int64_t stride;        // bytes per expert
     int64_t off_bias;
     int M, K;              // matrix rows, columns
-    int ksplit;            // K-splits (tiles per split = kEW / ksplit)
-    int rounds;            // tile rounds per CTA: round r covers kEW / ksplit tiles
+    int ksplit;            // K-splits (tiles per split = kCT / ksplit)
+    int rounds;            // tile rounds per CTA: round r covers kCT / ksplit tiles
     int k, shard_count;
     int F, H;
     float limit, alpha;
@@ -100,7 +103,7 @@ __host__ __device__ inline SmemPlan smem_plan(int K) {
     p.sc = p.ring + kEStages * kStageW;
     p.xe = p.sc + kEStages * kStageS;
     p.red = p.xe + ngrp * 8 * 8 * 64;
-    p.bars = p.red + 2 * kEW * 2 * 8 * kEPass * 4;
+    p.bars = p.red + 2 * kCT * 2 * 8 * kEPass * 4;
     p.total = p.bars + 2 * kEStages * 8 + 16 + 1024;  // + abort flag, alignment slack
     return p;
 }
@@ -164,58 +167,72 @@ __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1,
 
 __device__ __forceinline__ float e8m0(uint32_t byte) { return __uint_as_float(byte << 23); }  // gemv_scale
 
-// One group of one warp's tile: w blocks (w = 8 for a full, 128-byte-swizzled
-// group, else a narrow unswizzled one), rows rA / rB of the tile as the MMA's
-// rows g / g + 8, kTok tokens per MMA (8 / kTok block slots).  xg: this
-// lane's B entries of the group (entry (j, g), quarter t).  Accumulates
-// acc[row][column of the lane].
+// One group of kNT tiles of one warp: w blocks (w = 8 for full,
+// 128-byte-swizzled groups, else narrow unswizzled ones); tile rows g and
+// g + 8 as the MMA's rows g / g + 8, kTok tokens per MMA (8 / kTok block
+// slots).  A: the first tile's group in shared memory (the next tile's
+// follows `astep` bytes later), Sc: its 16 x w scale bytes (next tile's
+// `sstep` later); off[j] = (j ^ g) * 16, the swizzled position of block j in
+// rows g and g + 8 (both have row % 8 = g); xg: this lane's B entries of the
+// group (entry (j, g), quarter t), shared by the tiles.  Accumulates
+// acc[tile][row][column of the lane].
 template <int kTok, bool kFull>
-__device__ __forceinline__ void group_mma(const unsigned char* A, const unsigned char* Sc, int w, int rA, int rB,
-                                          const unsigned char* xg, int t, float (&acc)[2][2]) {
+__device__ __forceinline__ void group_mma(const unsigned char* A, int astep, const unsigned char* Sc, int sstep,
+                                          int w, int g, int t, const uint32_t (&off)[8], const unsigned char* xg,
+                                          float (&acc)[kNT][2][2]) {
     constexpr int kBlk = 8 / kTok;
     const int wl = kFull ? 8 : w;
     const int sw = kFull ? 8 : w;  // scale bytes per row
-    auto scale = [&](int r, int i) -> float {
-        return (kFull || i < wl) ? e8m0(Sc[r * sw + i]) : 0.f;
+    auto scale = [&](int ti, int row, int i) -> float {
+        return (kFull || i < wl) ? e8m0(Sc[ti * sstep + row * sw + i]) : 0.f;
     };
-    const unsigned char* rowA = A + (kFull ? rA * 128 : rA * 16 * w) + 4 * t;
-    const unsigned char* rowB = A + (kFull ? rB * 128 : rB * 16 * w) + 4 * t;
-    float d0[4], d1[4];
+    const unsigned char* rowA = A + (kFull ? g * 128 : g * 16 * w) + 4 * t;
+    const int rowB = kFull ? 8 * 128 : 8 * 16 * w;  // row g + 8, relative to row g
+    float d0[kNT][4], d1[kNT][4];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         if (!kFull && j % kBlk == 0) {  // a narrow group may end before its window does
 #pragma unroll
-            for (int q = 0; q < 4; ++q) d0[q] = d1[q] = 0.f;
+            for (int ti = 0; ti < kNT; ++ti)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) d0[ti][q] = d1[ti][q] = 0.f;
         }
         if (kFull || j < wl) {
-            const uint32_t wa = ld32(rowA + (kFull ? ((j ^ (rA & 7)) << 4) : j * 16));
-            const uint32_t wb = ld32(rowB + (kFull ? ((j ^ (rB & 7)) << 4) : j * 16));
             const uint4 xv = ld128(xg + j * 512);
-            uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-            e2m1x8_to_f16x8(wa, a0, a1, a2, a3);
-            e2m1x8_to_f16x8(wb, b0, b1, b2, b3);
-            if (kFull && j % kBlk == 0) {  // the window's first block starts the accumulators
-                mma_f16_z(d0, a0, b0, a1, b1, xv.x, xv.y);
-                mma_f16_z(d1, a2, b2, a3, b3, xv.z, xv.w);
-            } else {
-                mma_f16(d0, a0, b0, a1, b1, xv.x, xv.y);
-                mma_f16(d1, a2, b2, a3, b3, xv.z, xv.w);
+#pragma unroll
+            for (int ti = 0; ti < kNT; ++ti) {
+                const unsigned char* pa = rowA + ti * astep + (kFull ? off[j] : j * 16);
+                const uint32_t wa = ld32(pa);
+                const uint32_t wb = ld32(pa + rowB);
+                uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+                e2m1x8_to_f16x8(wa, a0, a1, a2, a3);
+                e2m1x8_to_f16x8(wb, b0, b1, b2, b3);
+                if (kFull && j % kBlk == 0) {  // the window's first block starts the accumulators
+                    mma_f16_z(d0[ti], a0, b0, a1, b1, xv.x, xv.y);
+                    mma_f16_z(d1[ti], a2, b2, a3, b3, xv.z, xv.w);
+                } else {
+                    mma_f16(d0[ti], a0, b0, a1, b1, xv.x, xv.y);
+                    mma_f16(d1[ti], a2, b2, a3, b3, xv.z, xv.w);
+                }
             }
         }
         if (j % kBlk == kBlk - 1) {  // flush the window of blocks [j - kBlk + 1, j]
             const int jb = j - kBlk + 1;
-            if (kTok == 1) {  // columns 2t, 2t + 1 = blocks 2t, 2t + 1
-                acc[0][0] = fmaf(d0[0] + d1[0], scale(rA, 2 * t), acc[0][0]);
-                acc[0][0] = fmaf(d0[1] + d1[1], scale(rA, 2 * t + 1), acc[0][0]);
-                acc[1][0] = fmaf(d0[2] + d1[2], scale(rB, 2 * t), acc[1][0]);
-                acc[1][0] = fmaf(d0[3] + d1[3], scale(rB, 2 * t + 1), acc[1][0]);
-            } else {  // columns 2t, 2t + 1 share one block
-                const int bi = jb + (kTok == 2 ? t : (t >> 1));
-                const float fa = scale(rA, bi), fb = scale(rB, bi);
-                acc[0][0] = fmaf(d0[0] + d1[0], fa, acc[0][0]);
-                acc[0][1] = fmaf(d0[1] + d1[1], fa, acc[0][1]);
-                acc[1][0] = fmaf(d0[2] + d1[2], fb, acc[1][0]);
-                acc[1][1] = fmaf(d0[3] + d1[3], fb, acc[1][1]);
+#pragma unroll
+            for (int ti = 0; ti < kNT; ++ti) {
+                if (kTok == 1) {  // columns 2t, 2t + 1 = blocks 2t, 2t + 1
+                    acc[ti][0][0] = fmaf(d0[ti][0] + d1[ti][0], scale(ti, g, 2 * t), acc[ti][0][0]);
+                    acc[ti][0][0] = fmaf(d0[ti][1] + d1[ti][1], scale(ti, g, 2 * t + 1), acc[ti][0][0]);
+                    acc[ti][1][0] = fmaf(d0[ti][2] + d1[ti][2], scale(ti, g + 8, 2 * t), acc[ti][1][0]);
+                    acc[ti][1][0] = fmaf(d0[ti][3] + d1[ti][3], scale(ti, g + 8, 2 * t + 1), acc[ti][1][0]);
+                } else {  // columns 2t, 2t + 1 share one block
+                    const int bi = jb + (kTok == 2 ? t : (t >> 1));
+                    const float fa = scale(ti, g, bi), fb = scale(ti, g + 8, bi);
+                    acc[ti][0][0] = fmaf(d0[ti][0] + d1[ti][0], fa, acc[ti][0][0]);
+                    acc[ti][0][1] = fmaf(d0[ti][1] + d1[ti][1], fa, acc[ti][0][1]);
+                    acc[ti][1][0] = fmaf(d0[ti][2] + d1[ti][2], fb, acc[ti][1][0]);
+                    acc[ti][1][1] = fmaf(d0[ti][3] + d1[ti][3], fb, acc[ti][1][1]);
+                }
             }
         }
     }
@@ -252,13 +269,16 @@ __device__ __forceinline__ void tma_3d(uint32_t dst, const CUtensorMap* map, int
 
 // kMode 0 / 1: gate_up with the clamped GLU / SiLU epilogue (f16 activations
 // per slot); 2: down x routing weight (fp32 per slot).
-// grid (min(E, T*k), ceil(tiles / (kEW / ksplit))), kEThreads threads.
+// grid (min(E, T*k), ceil(tiles / (rounds * kCT / ksplit))), kEThreads threads.
 template <int kMode>
 __global__ void __launch_bounds__(kEThreads, 1) k_expert_gemv(const __grid_constant__ GemvMaps maps,
                                                               ExpertGemvArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int ai = blockIdx.x;
     if (ai >= *a.w.nactive) return;
+    // a wait of this launch (or an earlier one since the last gw_sync) ran
+    // out: the results are already invalid, so do no more work
+    if (a.w.status && (*(volatile unsigned*)a.w.status & kStatusGemv)) return;
     const int e = a.w.active[ai];
     const SmemPlan P = smem_plan(a.K);
     const uint32_t sbase = (saddr(smem_raw) + 1023u) & ~1023u;
@@ -273,7 +293,7 @@ __global__ void __launch_bounds__(kEThreads, 1) k_expert_gemv(const __grid_const
     const int nblk = a.K >> 5, nfull = nblk >> 3, ngrp = (nblk + 7) >> 3;
     const int wlast = nblk - 8 * (ngrp - 1);
     const int ntiles = a.M >> 4;
-    const int ks = a.ksplit, tb = kEW / ks;
+    const int ks = a.ksplit, tb = kCT / ks;  // tiles per split and round
     const int per = (ngrp + ks - 1) / ks;           // stages per pass
     const int cnt = min(a.w.counts[e], a.w.tcap);
     const int npass = (cnt + kEPass - 1) / kEPass;
@@ -324,12 +344,15 @@ __global__ void __launch_bounds__(kEThreads, 1) k_expert_gemv(const __grid_const
                     if (grp >= min(ngrp, (sp + 1) * per)) continue;
                     const uint32_t wdst = sbase + P.ring + slot * kStageW;
                     const uint32_t sdst = sbase + P.sc + slot * kStageS;
+                    const int tt = tile0 + r * tb;
                     if (grp < nfull) {
-                        tma_5d(wdst + sp * tb * kGrp, &maps.w_full, grp, tile0 + r * tb, le, bar);
-                        tma_4d(sdst + sp * tb * kGrpSc, &maps.s_full, grp, tile0 + r * tb, le, bar);
+                        for (int b = 0; b < tb; b += kBoxT)
+                            tma_5d(wdst + (sp * tb + b) * kGrp, &maps.w_full, grp, tt + b, le, bar);
+                        tma_4d(sdst + sp * tb * kGrpSc, &maps.s_full, grp, tt, le, bar);
                     } else {
-                        tma_4d(wdst + sp * tb * kGrp, &maps.w_narrow, 0, tile0 + r * tb, le, bar);
-                        tma_3d(sdst + sp * tb * kGrpSc, &maps.s_narrow, tile0 + r * tb, le, bar);
+                        for (int b = 0; b < tb; b += kBoxT)
+                            tma_4d(wdst + sp * tb * kGrp + b * 256 * wlast, &maps.w_narrow, 0, tt + b, le, bar);
+                        tma_3d(sdst + sp * tb * kGrpSc, &maps.s_narrow, tt, le, bar);
                     }
                 }
                 if (++s == per) {
@@ -341,27 +364,22 @@ __global__ void __launch_bounds__(kEThreads, 1) k_expert_gemv(const __grid_const
         }
         __syncwarp();
     } else {
-        // ---- consumers
-        const int sp = warp / tb, tl = warp % tb;
-
+        // ---- consumers: warp = (split sp, position wl); its kNT tiles of a
+        // round are tiles wl * kNT .. + kNT - 1 of the split's tb
+        const int wps = kEW / ks;  // consumer warps per split
+        const int sp = warp / wps, wl = warp % wps;
         const int g0 = min(ngrp, sp * per), g1 = min(ngrp, g0 + per);
         const bool leader = elect_one();
-        // rows of the tile this lane feeds as MMA rows g and g + 8: down takes
-        // rows g, g + 8; gate_up takes feature g's gate and up rows (2g, 2g + 1),
-        // in the order that keeps the eight row-reads of a quad phase on
-        // distinct 128-byte-swizzle chunks.
-        int rA, rB;
-        if (kMode == 2) { rA = g; rB = g + 8; }
-        else if (g < 4) { rA = 2 * g; rB = 2 * g + 1; }
-        else { rA = 2 * g + 1; rB = 2 * g; }
+        // this lane reads tile rows g and g + 8 (the eight rows a quad phase
+        // reads sit on distinct 128-byte-swizzle chunks); block j of both is
+        // at 16 (j ^ g) in its row
+        uint32_t off[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) off[j] = (uint32_t)((j ^ g) << 4);
         const int* list = a.w.lists + (int64_t)e * a.w.tcap;
         const __half* xsrc = kMode == 2 ? a.w.act : a.w.x16;
         const unsigned char* xg0 = sgen + P.xe + g * 64 + 16 * t;
         float* red0 = reinterpret_cast<float*>(sgen + P.red);
-        // this thread's fixed share of the B-entry staging: quarter q of
-        // column c of block j of every (kEW / 8)-th group from grp0
-        const int sq = threadIdx.x & 3, sc_ = (threadIdx.x >> 2) & 7, sj = (threadIdx.x >> 5) & 7;
-        const int sgrp0 = threadIdx.x >> 8;
         bool ok = true;
         int slot = 0;
         uint32_t phase = 0;
@@ -376,118 +394,149 @@ __global__ void __launch_bounds__(kEThreads, 1) k_expert_gemv(const __grid_const
                 meta_mul[threadIdx.x] = kMode == 2 ? a.w.weights[sl] : a.w.xmul[row];
             }
             consumers_sync();
-            {  // B entries: (group, block j, column c) <- x[token of c][block] or zeros
+            // B entries: quarter q of (group, block j, column c) <- x[token of c][block] or zeros
+            for (int i = threadIdx.x; i < ngrp * 256; i += kEW * 32) {
+                const int q = i & 3, c = (i >> 2) & 7, j = (i >> 5) & 7, grp = i >> 8;
                 bool live;
                 int tok;
-                if (n == 1) { live = sj == sc_; tok = 0; }
-                else if (n == 2) { live = (sj & 3) == (sc_ >> 1); tok = sc_ & 1; }
-                else { live = (sj & 1) == (sc_ >> 2); tok = sc_ & 3; }
-                live = live && tok < n;
-                const uint4* src = reinterpret_cast<const uint4*>(xsrc + (int64_t)(live ? meta_row[tok] : 0) * a.K) +
-                                   sj * 4 + sq;
-                uint4* dst = reinterpret_cast<uint4*>(sgen + P.xe) + (threadIdx.x & 255);
-                for (int grp = sgrp0; grp < ngrp; grp += kEW / 8) {
-                    const bool in = live && grp * 8 + sj < nblk;
-                    dst[grp * 256] = in ? __ldg(src + grp * 32) : make_uint4(0u, 0u, 0u, 0u);
-                }
+                if (n == 1) { live = j == c; tok = 0; }
+                else if (n == 2) { live = (j & 3) == (c >> 1); tok = c & 1; }
+                else { live = (j & 1) == (c >> 2); tok = c & 3; }
+                live = live && tok < n && grp * 8 + j < nblk;
+                uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                if (live)
+                    v = __ldg(reinterpret_cast<const uint4*>(xsrc + (int64_t)meta_row[tok] * a.K) + (grp * 8 + j) * 4 + q);
+                reinterpret_cast<uint4*>(sgen + P.xe)[i] = v;
             }
             consumers_sync();
-          for (int r = 0; r < R; ++r) {
-            const int tile = tile0 + r * tb + tl;
-            const bool valid = tile < ntiles;
-            float* red = red0 + (r & 1) * (kEW * 2 * 8 * kEPass);  // double-buffered by round
-            float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-            for (int s = 0; s < per; ++s) {
-                if (ok) {
-                    ok = try_parity(fullb + slot * 8, phase) || wait_parity(fullb + slot * 8, phase, status);
-                    if (!ok) *abort_flag = 1;
-                }
-                ok = __all_sync(0xffffffffu, ok) && !*abort_flag;
-                const int grp = g0 + s;
-                if (ok && valid && grp < g1) {
-                    if (grp < nfull) {
-                        const unsigned char* A = sgen + P.ring + slot * kStageW + warp * kGrp;
-                        const unsigned char* Sc = sgen + P.sc + slot * kStageS + warp * kGrpSc;
-                        const unsigned char* xg = xg0 + grp * 4096;
-                        if (n == 1) group_mma<1, true>(A, Sc, 8, rA, rB, xg, t, acc);
-                        else if (n == 2) group_mma<2, true>(A, Sc, 8, rA, rB, xg, t, acc);
-                        else group_mma<4, true>(A, Sc, 8, rA, rB, xg, t, acc);
-                    } else {
-                        const unsigned char* A = sgen + P.ring + slot * kStageW + sp * tb * kGrp + tl * 256 * wlast;
-                        const unsigned char* Sc = sgen + P.sc + slot * kStageS + sp * tb * kGrpSc + tl * 16 * wlast;
-                        const unsigned char* xg = xg0 + grp * 4096;
-                        if (n == 1) group_mma<1, false>(A, Sc, wlast, rA, rB, xg, t, acc);
-                        else if (n == 2) group_mma<2, false>(A, Sc, wlast, rA, rB, xg, t, acc);
-                        else group_mma<4, false>(A, Sc, wlast, rA, rB, xg, t, acc);
+            for (int r = 0; r < R; ++r) {
+                float* red = red0 + (r & 1) * (kCT * 2 * 8 * kEPass);  // double-buffered by round
+                float acc[kNT][2][2];
+#pragma unroll
+                for (int ti = 0; ti < kNT; ++ti) acc[ti][0][0] = acc[ti][0][1] = acc[ti][1][0] = acc[ti][1][1] = 0.f;
+                const bool any = tile0 + r * tb + wl * kNT < ntiles;  // the warp's first tile exists
+                // the bias pair each emitting lane adds, loaded now so its latency
+                // hides behind the stage loop (gate_up: rows 2f, 2f + 1 of feature
+                // f = tile * 8 + g; down: rows tile * 16 + g, + 8)
+                float bias0[kNT], bias1[kNT];
+                {
+                    const uint16_t* bias =
+                        reinterpret_cast<const uint16_t*>(a.base + (int64_t)le * a.stride + a.off_bias);
+#pragma unroll
+                    for (int ti = 0; ti < kNT; ++ti) {
+                        const int tile = tile0 + r * tb + wl * kNT + ti;
+                        bias0[ti] = bias1[ti] = 0.f;
+                        if (sp == 0 && tile < ntiles) {
+                            const int i0 = kMode == 2 ? tile * 16 + g : 2 * (tile * 8 + g);
+                            const int i1 = kMode == 2 ? i0 + 8 : i0 + 1;
+                            bias0[ti] = bf16_bits_to_f32(__ldg(bias + i0));
+                            bias1[ti] = bf16_bits_to_f32(__ldg(bias + i1));
+                        }
                     }
                 }
-                __syncwarp();
-                if (leader) arrive(emptyb + slot * 8);  // this warp is done with the stage
-                if (++slot == kEStages) { slot = 0; phase ^= 1; }
-            }
-            if (valid) {  // (a K-split warp left without groups contributes zeros)
-                // columns -> (row, token): sum the block slots held by the quad
-                float v[2][2];
+                for (int s = 0; s < per; ++s) {
+                    if (ok) {
+                        ok = try_parity(fullb + slot * 8, phase) || wait_parity(fullb + slot * 8, phase, status);
+                        if (!ok) *abort_flag = 1;
+                    }
+                    ok = __all_sync(0xffffffffu, ok) && !*abort_flag;
+                    const int grp = g0 + s;
+                    if (ok && any && grp < g1) {
+                        const unsigned char* xg = xg0 + grp * 4096;
+                        const unsigned char* W = sgen + P.ring + slot * kStageW + sp * tb * kGrp;
+                        const unsigned char* S = sgen + P.sc + slot * kStageS + sp * tb * kGrpSc;
+                        if (grp < nfull) {
+                            const unsigned char* A = W + wl * kNT * kGrp;
+                            const unsigned char* Sc = S + wl * kNT * kGrpSc;
+                            if (n == 1) group_mma<1, true>(A, kGrp, Sc, kGrpSc, 8, g, t, off, xg, acc);
+                            else if (n == 2) group_mma<2, true>(A, kGrp, Sc, kGrpSc, 8, g, t, off, xg, acc);
+                            else group_mma<4, true>(A, kGrp, Sc, kGrpSc, 8, g, t, off, xg, acc);
+                        } else {
+                            const unsigned char* A = W + wl * kNT * 256 * wlast;
+                            const unsigned char* Sc = S + wl * kNT * 16 * wlast;
+                            const int as = 256 * wlast, ss = 16 * wlast;
+                            if (n == 1) group_mma<1, false>(A, as, Sc, ss, wlast, g, t, off, xg, acc);
+                            else if (n == 2) group_mma<2, false>(A, as, Sc, ss, wlast, g, t, off, xg, acc);
+                            else group_mma<4, false>(A, as, Sc, ss, wlast, g, t, off, xg, acc);
+                        }
+                    }
+                    __syncwarp();
+                    if (leader) arrive(emptyb + slot * 8);  // this warp is done with the stage
+                    if (++slot == kEStages) { slot = 0; phase ^= 1; }
+                }
 #pragma unroll
-                for (int r = 0; r < 2; ++r) {
-                    if (n == 1) {
-                        float x = acc[r][0];
-                        x += __shfl_xor_sync(0xffffffffu, x, 1);
-                        x += __shfl_xor_sync(0xffffffffu, x, 2);
-                        v[r][0] = x;
-                        v[r][1] = 0.f;
-                    } else if (n == 2) {
+                for (int ti = 0; ti < kNT; ++ti) {
+                    const int tl = wl * kNT + ti;          // tile within the split
+                    if (tile0 + r * tb + tl >= ntiles) continue;
+                    // columns -> (row, token): sum the block slots held by the quad
+                    float v[2][2];
 #pragma unroll
-                        for (int c = 0; c < 2; ++c) {
-                            float x = acc[r][c];
+                    for (int rr = 0; rr < 2; ++rr) {
+                        if (n == 1) {
+                            float x = acc[ti][rr][0];
                             x += __shfl_xor_sync(0xffffffffu, x, 1);
                             x += __shfl_xor_sync(0xffffffffu, x, 2);
-                            v[r][c] = x;
-                        }
-                    } else {
+                            v[rr][0] = x;
+                            v[rr][1] = 0.f;
+                        } else if (n == 2) {
 #pragma unroll
-                        for (int c = 0; c < 2; ++c) v[r][c] = acc[r][c] + __shfl_xor_sync(0xffffffffu, acc[r][c], 2);
+                            for (int c = 0; c < 2; ++c) {
+                                float x = acc[ti][rr][c];
+                                x += __shfl_xor_sync(0xffffffffu, x, 1);
+                                x += __shfl_xor_sync(0xffffffffu, x, 2);
+                                v[rr][c] = x;
+                            }
+                        } else {
+#pragma unroll
+                            for (int c = 0; c < 2; ++c)
+                                v[rr][c] = acc[ti][rr][c] + __shfl_xor_sync(0xffffffffu, acc[ti][rr][c], 2);
+                        }
+                    }
+                    // red[tile slot][r][g][token] = tile row 8r + g
+                    float* rw = red + (sp * tb + tl) * (2 * 8 * kEPass);
+                    const int tk = n <= 2 ? 0 : 2 * t;
+                    if ((n <= 2 && t == 0) || (n > 2 && t < 2)) {
+                        rw[0 * 8 * kEPass + g * kEPass + tk] = v[0][0];
+                        rw[1 * 8 * kEPass + g * kEPass + tk] = v[1][0];
+                        rw[0 * 8 * kEPass + g * kEPass + tk + 1] = v[0][1];
+                        rw[1 * 8 * kEPass + g * kEPass + tk + 1] = v[1][1];
                     }
                 }
-                // red[warp][r][g][token]; gate_up rows in (gate, up) order
-                float* rw = red + warp * (2 * 8 * kEPass);
-                const bool swap = kMode != 2 && g >= 4;
-                const float r00 = swap ? v[1][0] : v[0][0], r01 = swap ? v[1][1] : v[0][1];
-                const float r10 = swap ? v[0][0] : v[1][0], r11 = swap ? v[0][1] : v[1][1];
-                const int tk = n <= 2 ? 0 : 2 * t;
-                if ((n <= 2 && t == 0) || (n > 2 && t < 2)) {
-                    rw[0 * 8 * kEPass + g * kEPass + tk] = r00;
-                    rw[1 * 8 * kEPass + g * kEPass + tk] = r10;
-                    rw[0 * 8 * kEPass + g * kEPass + tk + 1] = r01;
-                    rw[1 * 8 * kEPass + g * kEPass + tk + 1] = r11;
+                // a tile with K-split partials waits for all of them; a warp that
+                // owns its tiles outright only for its own lanes
+                if (ks > 1) consumers_sync();
+                else __syncwarp();
+                // split-0 warps emit their tiles: lane (g, t) -> token t
+                if (sp == 0 && t < n && ok) {
+                    const int sl = meta_slot[t];
+                    const float mul = meta_mul[t];
+                    // gate_up: feature g = tile rows 2g (gate), 2g + 1 (up); down: rows g, g + 8
+                    const int q0 = kMode == 2 ? g : 2 * g, q1 = kMode == 2 ? g + 8 : 2 * g + 1;
+#pragma unroll
+                    for (int ti = 0; ti < kNT; ++ti) {
+                        const int tl = wl * kNT + ti;
+                        const int tile = tile0 + r * tb + tl;
+                        if (tile >= ntiles) continue;
+                        float y0 = 0.f, y1 = 0.f;
+                        for (int q = 0; q < ks; ++q) {
+                            const float* rw = red + (q * tb + tl) * (2 * 8 * kEPass);
+                            y0 += rw[(q0 >> 3) * 8 * kEPass + (q0 & 7) * kEPass + t];
+                            y1 += rw[(q1 >> 3) * 8 * kEPass + (q1 & 7) * kEPass + t];
+                        }
+                        if (kMode != 2) {
+                            const int f = tile * 8 + g;
+                            const float gate = y0 * mul + bias0[ti];
+                            const float up = y1 * mul + bias1[ti];
+                            a.w.act[(int64_t)sl * a.F + f] = __float2half_rn(activate<kMode>(gate, up, a.limit, a.alpha));
+                        } else {
+                            const int r0 = tile * 16 + g;
+                            float* y = a.w.ybuf + (int64_t)sl * a.H;
+                            y[r0] = (y0 + bias0[ti]) * mul;
+                            y[r0 + 8] = (y1 + bias1[ti]) * mul;
+                        }
+                    }
                 }
             }
-            consumers_sync();
-            // split-0 warps emit: lane (g, t) -> token t (the splits of a tile
-            // are warps tl, tl + tb, ...)
-            if (valid && sp == 0 && t < n && ok) {
-                float y0 = 0.f, y1 = 0.f;
-                for (int q = 0; q < ks; ++q) {
-                    const float* rw = red + (warp + q * tb) * (2 * 8 * kEPass);
-                    y0 += rw[0 * 8 * kEPass + g * kEPass + t];
-                    y1 += rw[1 * 8 * kEPass + g * kEPass + t];
-                }
-                const int sl = meta_slot[t];
-                const float mul = meta_mul[t];
-                const uint16_t* bias = reinterpret_cast<const uint16_t*>(a.base + (int64_t)le * a.stride + a.off_bias);
-                if (kMode != 2) {
-                    const int f = tile * 8 + g;
-                    const float gate = y0 * mul + bf16_bits_to_f32(bias[2 * f]);
-                    const float up = y1 * mul + bf16_bits_to_f32(bias[2 * f + 1]);
-                    a.w.act[(int64_t)sl * a.F + f] = __float2half_rn(activate<kMode>(gate, up, a.limit, a.alpha));
-                } else {
-                    const int r0 = tile * 16 + g;
-                    float* y = a.w.ybuf + (int64_t)sl * a.H;
-                    y[r0] = (y0 + bf16_bits_to_f32(bias[r0])) * mul;
-                    y[r0 + 8] = (y1 + bf16_bits_to_f32(bias[r0 + 8])) * mul;
-                }
-            }
-          }
         }
     }
     __syncthreads();
@@ -500,7 +549,7 @@ __global__ void __launch_bounds__(kEThreads, 1) k_expert_gemv(const __grid_const
 // about one and a half waves of CTAs (one per SM).
 int pick_split(int experts, int ntiles) {
     int ks = 1;
-    while (ks < 8 && (int64_t)experts * ((ntiles * ks + kEW - 1) / kEW) < 222) ks *= 2;
+    while (ks < 4 && (int64_t)experts * ((ntiles * ks + kCT - 1) / kCT) < 222) ks *= 2;
     return ks;
 }
 
@@ -543,7 +592,7 @@ int launch_expert_gemv(const LayerView& L, const MoeDims& d, const MoeWork& w, i
     const int e_local = (d.E - d.shard_rank + d.shard_count - 1) / d.shard_count;
     const int maxa = std::min(d.E, T * d.k);
     a.ksplit = pick_split(maxa, ntiles);
-    const int tb = kEW / a.ksplit;
+    const int tb = kCT / a.ksplit;
     // Several rounds of tiles per CTA amortise its set-up and token staging;
     // keep at least ~4 waves of CTAs.
     a.rounds = 1;
@@ -570,7 +619,7 @@ int launch_expert_gemv(const LayerView& L, const MoeDims& d, const MoeWork& w, i
     {
         const cuuint64_t gd[5] = {128, 16, nf, (cuuint64_t)ntiles, (cuuint64_t)e_local};
         const cuuint64_t gs[4] = {128, 2048, tile_pk, es};
-        const cuuint32_t box[5] = {128, 16, 1, (cuuint32_t)tb, 1};
+        const cuuint32_t box[5] = {128, 16, 1, (cuuint32_t)kBoxT, 1};
         good = good && enc(&maps.w_full, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, const_cast<uint8_t*>(pk), gd, gs, box,
                            ones, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
@@ -578,7 +627,7 @@ int launch_expert_gemv(const LayerView& L, const MoeDims& d, const MoeWork& w, i
     {
         const cuuint64_t gd[4] = {(cuuint64_t)16 * wn, 16, (cuuint64_t)ntiles, (cuuint64_t)e_local};
         const cuuint64_t gs[3] = {(cuuint64_t)16 * wn, tile_pk, es};
-        const cuuint32_t box[4] = {(cuuint32_t)(16 * wn), 16, (cuuint32_t)tb, 1};
+        const cuuint32_t box[4] = {(cuuint32_t)(16 * wn), 16, (cuuint32_t)kBoxT, 1};
         good = good && enc(&maps.w_narrow, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4,
                            const_cast<uint8_t*>(pk + (wlast < 8 ? (int64_t)nfull * 2048 : 0)), gd, gs, box, ones,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,

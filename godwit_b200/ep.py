@@ -98,54 +98,87 @@ def shard_of(expert: int, world: int) -> int:
 
 
 class AllToAllEP:
-    def __init__(self, ops, layers: int, top_k: int, group=None):
+    """Token-sliced expert parallelism with fixed-capacity exchanges.
+
+    Every rank sends each peer a block of exactly C rows (C = capacity per
+    peer), so both all-to-alls have equal splits known before the layer runs
+    and nothing waits on the host between layers: a (token, slot) row goes to
+    position `pos` of its owner's block, where pos counts the earlier slots
+    bound for the same owner (computed on the device); unused rows carry
+    expert id -1 and are skipped by the owner's grouping.  Each row carries
+    its expert id and routing weight in four trailing bf16 columns, so rows
+    and metadata travel in one exchange.
+
+    C defaults to the exact bound max_r(T_r) * k (no row can be dropped).
+    With `capacity_factor` f, C = ceil(max_r(T_r) * k / world * f) + 4 and
+    forward() checks once, at its end, that no block overflowed (raising
+    RuntimeError if one did: rows are never dropped silently)."""
+
+    def __init__(self, ops, layers: int, top_k: int, group=None, capacity_factor: float | None = None):
         self.ops = ops
         self.layers = layers
         self.k = top_k
         self.group = group
+        self.capacity_factor = capacity_factor
+        self.capacity = None
+        self.overflow = None
 
-    def _a2a(self, out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits) -> None:
-        if dist.is_initialized() and dist.get_world_size(self.group) > 1:
-            dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+    def _world(self):
+        return dist.get_world_size(self.group) if dist.is_initialized() else 1
+
+    def _a2a(self, out: torch.Tensor, inp: torch.Tensor) -> None:
+        if self._world() > 1:
+            dist.all_to_all_single(out, inp, group=self.group)
         else:
             out.copy_(inp)
 
+    def set_capacity(self, tokens_max: int) -> None:
+        world = self._world()
+        full = max(1, tokens_max * self.k)
+        if self.capacity_factor is None:
+            self.capacity = full
+        else:
+            self.capacity = min(full, int(-(-full * self.capacity_factor // world)) + 4)
+
     def layer_partial(self, layer: int, x: torch.Tensor) -> torch.Tensor:
         """This rank's tokens x [T, H] -> [T, H] fp32 weighted expert sum of layer `layer`."""
-        world = dist.get_world_size(self.group) if dist.is_initialized() else 1
+        world = self._world()
         T, H = x.shape
-        k = self.k
+        k, C = self.k, self.capacity
+        dev = x.device
         if T > 0:
             experts, weights = self.ops.route(layer, x)
         else:  # a rank without tokens still takes part in every exchange
-            experts = torch.empty((0, k), dtype=torch.int32, device=x.device)
-            weights = torch.empty((0, k), dtype=torch.float32, device=x.device)
+            experts = torch.empty((0, k), dtype=torch.int32, device=dev)
+            weights = torch.empty((0, k), dtype=torch.float32, device=dev)
         flat_e = experts.reshape(-1).to(torch.int64)
         dest = torch.remainder(flat_e, world)
-        order = torch.sort(dest, stable=True).indices                  # slots grouped by owner
-        send_counts = torch.bincount(dest, minlength=world)
-        recv_counts = torch.empty_like(send_counts)
-        self._a2a(recv_counts, send_counts, None, None)
-        s_split, r_split = send_counts.tolist(), recv_counts.tolist()
-        R = sum(r_split)
-        send_rows = x.index_select(0, torch.div(order, k, rounding_mode="floor"))
-        # expert id and routing weight of each sent row, one int32 pair
-        meta = torch.stack([flat_e.index_select(0, order).to(torch.int32),
-                            weights.reshape(-1).index_select(0, order).contiguous().view(torch.int32)], 1)
-        rows = torch.empty((R, H), dtype=x.dtype, device=x.device)
-        rmeta = torch.empty((R, 2), dtype=torch.int32, device=x.device)
-        self._a2a(rows, send_rows, r_split, s_split)
-        self._a2a(rmeta, meta, r_split, s_split)
-        out = torch.empty((R, H), dtype=torch.float32, device=x.device)
+        # position of each slot in its owner's block: earlier slots bound for the same owner
+        onehot = torch.nn.functional.one_hot(dest, world)
+        pos = (onehot.cumsum(0).gather(1, dest[:, None]).squeeze(1) - 1) if T > 0 else dest
+        if self.overflow is not None and T > 0:
+            self.overflow |= (pos >= C).any()
+        idx = dest * C + torch.clamp(pos, max=C - 1)
+        send = torch.zeros((world * C, H + 4), dtype=x.dtype, device=dev)
+        meta = send[:, H:].view(torch.int32)                           # [world*C, 2]: expert, weight bits
+        meta[:, 0] = -1
+        if T > 0:
+            slot_tok = torch.div(torch.arange(T * k, device=dev), k, rounding_mode="floor")
+            send[idx, :H] = x.index_select(0, slot_tok)
+            packed = torch.stack([experts.reshape(-1), weights.reshape(-1).contiguous().view(torch.int32)], 1)
+            meta[idx] = packed
+        recv = torch.empty_like(send)
+        self._a2a(recv, send)
+        rows = recv[:, :H].contiguous()
+        rmeta = recv[:, H:].view(torch.int32)
+        out = torch.zeros((world * C, H), dtype=torch.float32, device=dev)
         self.ops.apply_rows(layer, rows, rmeta[:, 0].contiguous(), rmeta[:, 1].contiguous().view(torch.float32),
                             out)
-        back = torch.empty((T * k, H), dtype=torch.float32, device=x.device)
-        self._a2a(back, out, s_split, r_split)
-        y = torch.empty_like(back)
-        y.index_copy_(0, order, back)
-        y = y.view(T, k, H)
+        back = torch.empty_like(out)
+        self._a2a(back, out)
         if T == 0:
-            return torch.empty((0, H), dtype=torch.float32, device=x.device)
+            return torch.empty((0, H), dtype=torch.float32, device=dev)
+        y = back.index_select(0, idx).view(T, k, H)
         partial = y[:, 0].clone()
         for j in range(1, k):                                          # slot order, as the combine
             partial += y[:, j]
@@ -154,9 +187,19 @@ class AllToAllEP:
     def forward(self, x: torch.Tensor, stream: torch.Tensor, x_work: torch.Tensor) -> torch.Tensor:
         """x [T, H] (this rank's tokens, compute dtype) -> stream [T, H] fp32:
         stream = x; for l: stream += moe_l(round(stream))."""
+        if self.capacity is None:  # one exchange of the token counts, then fixed shapes
+            t = torch.tensor([x.shape[0]], dtype=torch.int64, device=x.device)
+            if self._world() > 1:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+            self.set_capacity(int(t.item()))
+        if self.capacity_factor is not None:
+            self.overflow = torch.zeros((), dtype=torch.bool, device=x.device)
         self.ops.widen(x, stream)
         x_work.copy_(x)
         for layer in range(self.layers):
             partial = self.layer_partial(layer, x_work)
             self.ops.residual(stream, partial, x_work)
+        if self.overflow is not None and bool(self.overflow):
+            raise RuntimeError(f"an all-to-all block overflowed its capacity of {self.capacity} rows; "
+                               "raise capacity_factor (or leave it unset for the exact bound)")
         return stream

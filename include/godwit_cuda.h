@@ -246,7 +246,8 @@ GW_API gw_status gw_moe_stack_forward_async(gw_ctx* ctx, gw_bank* bank,
 /* Applies a given routing [T, k] (device arrays) to x_dev: out_dev (=, or +=
  * when `accumulate` != 0) sum_k w * expert(x).  Expert ids this shard does
  * not own, or outside [0, E), contribute nothing — the per-rank half of
- * expert parallelism. */
+ * expert parallelism, whose rows carry one expert each: the expert path
+ * (gw_set_tensor_core_min_tokens) is chosen as for T slots, not T * k. */
 GW_API gw_status gw_moe_apply_async(gw_ctx* ctx, gw_bank* bank, int32_t layer,
                              const void* x_dev, int32_t x_dtype, int32_t T,
                              const int32_t* experts_dev, const float* weights_dev,

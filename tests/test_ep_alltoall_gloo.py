@@ -36,8 +36,10 @@ class ToyOps:
         return top.indices.to(torch.int32), torch.softmax(top.values, dim=1).to(torch.float32)
 
     def apply_rows(self, layer, rows, experts, weights, out):
-        assert bool(((experts.to(torch.int64) % self.world) == self.rank).all()), "row sent to a non-owner"
-        out.copy_(weights[:, None] * torch.tanh(rows.float() * (experts[:, None].float() + 1 + layer)))
+        live = experts >= 0  # rows with expert id -1 pad the fixed-capacity blocks
+        assert bool(((experts[live].to(torch.int64) % self.world) == self.rank).all()), "row sent to a non-owner"
+        y = weights[:, None] * torch.tanh(rows.float() * (experts[:, None].float() + 1 + layer))
+        out.copy_(torch.where(live[:, None], y, torch.zeros_like(y)))
 
 
 def make_x():
@@ -45,20 +47,25 @@ def make_x():
     return torch.randn(T_TOTAL, H, generator=g).to(torch.bfloat16)
 
 
-def run(rank, world, total=T_TOTAL):
+def run(rank, world, total=T_TOTAL, capacity_factor=None):
     from godwit_b200.ep import AllToAllEP
     per = -(-total // world)
     x = make_x()[:total][rank * per:min(total, (rank + 1) * per)].contiguous()
     stream = torch.empty(x.shape[0], H)
     x_work = torch.empty_like(x)
-    return AllToAllEP(ToyOps(rank, world), LAYERS, K).forward(x, stream, x_work).numpy()
+    ep = AllToAllEP(ToyOps(rank, world), LAYERS, K, capacity_factor=capacity_factor)
+    return ep.forward(x, stream, x_work).numpy()
 
 
-def _worker(rank, world, port, out_dir, total=T_TOTAL):
+def _worker(rank, world, port, out_dir, total=T_TOTAL, capacity_factor=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        np.save(os.path.join(out_dir, f"r{rank}.npy"), run(rank, world, total))
+        try:
+            res = run(rank, world, total, capacity_factor)
+        except RuntimeError as e:
+            res = np.array([str(e)])
+        np.save(os.path.join(out_dir, f"r{rank}.npy"), res)
     finally:
         dist.destroy_process_group()
 
@@ -104,3 +111,18 @@ def test_one_rank_matches_direct_sum():
         stream += acc
         xw = stream.to(torch.bfloat16)
     assert np.array_equal(run(0, 1), stream.numpy())
+
+
+def test_bounded_capacity_matches_and_overflow_is_reported(tmp_path):
+    """capacity_factor 2 (blocks of ceil(T k / world * 2) + 4 rows) gives the
+    same result; a factor too small to hold the rows raises instead of
+    dropping any."""
+    ref = run(0, 1)
+    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path), T_TOTAL, 2.0), nprocs=2, join=True)
+    got = np.concatenate([np.load(tmp_path / f"r{r}.npy") for r in range(2)])
+    assert np.array_equal(got, ref)
+    # 13 tokens x 3 slots over 2 ranks, blocks of ceil(21 * 0.01 / 2) + 4 = 5 rows:
+    # some owner receives more than 5 of a sender's 21 slots
+    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path), T_TOTAL, 0.01), nprocs=2, join=True)
+    msgs = [np.load(tmp_path / f"r{r}.npy") for r in range(2)]
+    assert any(m.dtype.kind == "U" and "overflowed" in str(m[0]) for m in msgs)
