@@ -49,11 +49,13 @@ WORKLOADS = {
     "qwen3-decode32": ("qwen3-30b-a3b", 32, "Qwen3-30B-A3B-shaped MoE decode, 48 layers, batch 32"),
     "oss120-prefill": ("gpt-oss-120b", 2048, "GPT-OSS-120B-shaped MoE prefill layer, 2048 tokens, 4x hot-expert skew on 8 experts"),
     "gemv": (None, 1, "MXFP4 GEMV 2880x2880 (GPT-OSS down_proj shape), batched over copies"),
+    "int8-head": (None, 1, "int8 affine GEMV 201088x2880 (GPT-OSS output head), one token"),
 }
 DEFAULT_WORKLOAD = "oss120-decode64"
 # timed steps when --steps is not given: about a second of work each
 DEFAULT_STEPS = {"oss120-decode64": 60, "oss120-decode1": 600, "oss20-decode1": 1000,
-                 "qwen3-decode1": 600, "qwen3-decode32": 200, "oss120-prefill": 150, "gemv": 2000}
+                 "qwen3-decode1": 600, "qwen3-decode32": 200, "oss120-prefill": 150, "gemv": 2000,
+                 "int8-head": 400}
 SEED = 0
 
 
@@ -239,7 +241,9 @@ def run_reference(args, workload):
     if ref is not None:
         ref.calibrate(4.0)
     for i in range(args.warmup + args.steps):
-        if ref is None:
+        if workload == "int8-head":
+            v, sample = cpu_int8_sample(threads, budget_s=4.0)
+        elif ref is None:
             v, sample = cpu_gemv_sample(threads, budget_s=4.0)
         else:
             dt = ref.run()
@@ -265,6 +269,8 @@ def run_reference(args, workload):
 def metric_unit(workload):
     if workload == "gemv":
         return "MXFP4 expert GEMV HBM GB/s", "GB/s"
+    if workload == "int8-head":
+        return "int8 affine head GEMV HBM GB/s", "GB/s"
     kind = "prefill" if "prefill" in workload else "decode"
     return f"MoE {kind} tokens/s (" + WORKLOADS[workload][2] + ")", "tokens/s"
 
@@ -291,6 +297,8 @@ def main():
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args, args.workload)
+    if args.workload == "int8-head":
+        return run_int8_head(args)
     if args.workload == "gemv":
         return run_gemv(args)
     return run_decode(args)
@@ -495,7 +503,7 @@ def run_decode(args):
                     "hbm_frac": (achieved / peak) if achieved else None}
         roofline["frac"] = roofline["achieved"] / tpeak
     else:
-        roofline = {"bound": "hbm", "kernel": "k_gateup + k_down (expert MXFP4 GEMVs)",
+        roofline = {"bound": "hbm", "kernel": "k_expert_gemv gate_up + down (expert MXFP4 GEMVs)",
                     "achieved": achieved, "peak": peak, "unit": "GB/s",
                     "frac": (achieved / peak) if achieved else None,
                     "peak_kind": peak_kind, "traffic": None}
@@ -549,6 +557,8 @@ def run_decode(args):
             # config 0 (the metric's GEMV half), measured in the same run
             line["gemv_config0"] = measure_gemv(ctx, cur, local, 1500, 3, 1,
                                                 cpu_baseline=not args.no_cpu_baseline)
+            line["int8_head"] = measure_int8_head(ctx, cur, local, 200, 3,
+                                                  cpu_baseline=not args.no_cpu_baseline)
         print(json.dumps(line), flush=True)
     bank.close()
     ctx.close()
@@ -657,6 +667,126 @@ def measure_gemv(ctx, cur, local: int, steps: int, warmup: int, world: int = 1,
     del packed, scales, bias, x, y
     torch.cuda.empty_cache()
     return out
+
+
+HEAD_ROWS, HEAD_COLS = 201088, 2880  # GPT-OSS output head (vocabulary x hidden)
+
+
+def cpu_int8_sample(threads: int, budget_s: float = 8.0):
+    """The oracle port of int8_affine_gemv on a bounded slice of the head's
+    rows, grown until it takes about `budget_s`; GB/s of weights streamed."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    rng = np.random.default_rng(SEED)
+    rows = 2048
+    while True:
+        codes = rng.integers(0, 256, (rows, HEAD_COLS), dtype=np.uint8)
+        meta = rng.integers(0x3800, 0x3900, (rows, HEAD_COLS // 64, 2), dtype=np.uint16)
+        x = rng.standard_normal((1, HEAD_COLS)).astype(np.float16).astype(np.float32)
+        t0 = time.perf_counter()
+        O.int8_gemv(codes, meta, x, threads=threads)
+        dt = time.perf_counter() - t0
+        if dt * 4 > budget_s or rows >= HEAD_ROWS:
+            break
+        rows = min(HEAD_ROWS, rows * 4)
+    nbytes = rows * HEAD_COLS + rows * (HEAD_COLS // 64) * 4
+    return nbytes / dt / 1e9, f"{rows} of the head's {HEAD_ROWS} rows, one token, {dt:.2f} s on {threads} threads"
+
+
+def measure_int8_head(ctx, cur, local: int, steps: int, warmup: int, cpu_baseline: bool = True) -> dict:
+    """The trunk's largest int8 projection: the GPT-OSS output head (201088 x
+    2880 int8 codes + bf16 scale/zero per 64, 0.62 GB > L2) for one token,
+    int8_affine_gemv (router.metal:65-98).  Timed like config 0: warm-up, then
+    the median of GEMV_ROUNDS rounds of `steps` launches."""
+    import numpy as np
+    import torch
+
+    from godwit_b200 import device as D
+
+    rows, cols = HEAD_ROWS, HEAD_COLS
+    g = torch.Generator(device="cuda").manual_seed(SEED)
+    codes = torch.randint(0, 256, (rows, cols), dtype=torch.uint8, device="cuda", generator=g)
+    # bf16 scales ~1.5e-4 and zero points ~ -0.02 (a +-0.02 weight range)
+    sc = torch.empty(rows, cols // 64, device="cuda").uniform_(1e-4, 2e-4, generator=g)
+    zr = -sc * 127.5
+    meta = torch.stack([sc.to(torch.bfloat16), zr.to(torch.bfloat16)], -1).contiguous().view(torch.int16)
+    x_host = torch.randn(1, cols, generator=torch.Generator().manual_seed(SEED)).half().pin_memory()
+    x = x_host.to("cuda")
+    y = torch.empty(1, rows, dtype=torch.float32, device="cuda")
+    y_host = torch.empty(1, rows, dtype=torch.float32).pin_memory()
+    alg = rows * cols + rows * (cols // 64) * 4 + cols * 2 + rows * 4
+
+    def step():
+        D.int8_affine_gemv(ctx, codes, meta, None, x, y)
+
+    for _ in range(max(warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    launches0 = ctx.launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    rounds = []
+    for _ in range(GEMV_ROUNDS):
+        ev0.record(cur)
+        for _ in range(steps):
+            step()
+        ev1.record(cur)
+        torch.cuda.synchronize()
+        rounds.append(ev0.elapsed_time(ev1) / steps)
+    launches = ctx.launch_count() - launches0
+    ms = statistics.median(rounds)
+    ev0.record(cur)
+    for _ in range(steps):
+        x.copy_(x_host, non_blocking=True)
+        step()
+        y_host.copy_(y, non_blocking=True)
+    ev1.record(cur)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    e2e_ms = ev0.elapsed_time(ev1) / steps
+    peak, peak_kind = peaks()
+    gbs = alg / (ms / 1e3) / 1e9
+    out = {
+        "metric": "int8 affine head GEMV HBM GB/s", "value": gbs, "unit": "GB/s", "n_gpus": 1,
+        "steps": steps, "warmup": warmup, "ms_per_step": ms, "rounds": GEMV_ROUNDS,
+        "round_ms": [round(r, 4) for r in rounds], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8 affine (bf16 scale/zero per 64) x f16, fp32 accumulate",
+        "data": "synthetic",
+        "config": {"workload": "int8-head", "rows": rows, "cols": cols, "tokens": 1,
+                   "l2": f"{alg / 1e9:.2f} GB of weights per launch > L2",
+                   "protocol": f"warm-up, then median of {GEMV_ROUNDS} rounds of {steps} launches"},
+        "e2e": {"value": alg / (e2e_ms / 1e3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": cols * 2,
+                "d2h_bytes_per_step": rows * 4},
+        "gpu_launches": launches,
+        # one kernel per step: the round timing is the kernel's own duration
+        "roofline": {"bound": "hbm", "kernel": "k_int8_gemv", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                     "frac": gbs / peak, "peak_kind": peak_kind, "alg_bytes_per_launch": alg, "traffic": None},
+        "clocks": clocks,
+    }
+    if cpu_baseline:
+        threads = os.cpu_count() or 1
+        v, sample = cpu_int8_sample(threads)
+        out["cpu_baseline"] = {"value": v, "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample}
+    del codes, meta, sc, zr, x, y
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_int8_head(args):
+    from godwit_b200 import device as D
+    from godwit_b200.runtime import Context
+
+    world, rank, local = _dist_setup(args)
+    ctx = Context(local)
+    cur = D.bind_stream(ctx)
+    line = measure_int8_head(ctx, cur, local, args.steps, args.warmup, cpu_baseline=not args.no_cpu_baseline)
+    if rank == 0:
+        line["n_gpus"] = world
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    return 0
 
 
 def run_gemv(args):

@@ -23,6 +23,7 @@ GW_E_UNSUPPORTED = -6
 
 GW_DTYPE_F16 = 0
 GW_DTYPE_BF16 = 1
+GW_DTYPE_F32 = 2  # int8 projection outputs only
 GW_ACT_GPTOSS_CLAMPED = 0
 GW_ACT_SILU = 1
 
@@ -83,6 +84,8 @@ SIGNATURES = {
     "gw_expert_apply_batch": (ST, [P, P, I32, P, I32, I32, P, P, P]),
     "gw_moe_forward": (ST, [P, P, I32, P, I32, I32, P, P, P, P, P]),
     "gw_mxfp4_gemv": (ST, [P, P, P, P, P, I32, P, I32, I32]),
+    "gw_int8_affine_gemv": (ST, [P, P, P, P, P, I32, I32, I32, P, I32]),
+    "gw_int8_affine_gemv_async": (ST, [P, P, P, P, P, I32, I32, I32, P, I32]),
     "gw_mxfp4_dequant": (ST, [P, P, P, I32, I32, P]),
     "gw_mxfp4_gemv_batched_async": (ST, [P, I32, P, I64, P, I64, P, I64, P, I64, I32, P, I64,
                                          I32, I32]),

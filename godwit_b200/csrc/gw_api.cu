@@ -170,7 +170,8 @@ gw_status ensure_work(gw_ctx* c, const gw_bank* b, int T) {
     const size_t o_weights = take((size_t)tcap * kc * 4);
     const size_t o_counts = take((size_t)Ec * 4);
     const size_t o_active = take((size_t)Ec * 4);
-    const size_t o_nactive = take(4);
+    const size_t o_nactive = take(8);  // nactive, nextra
+    const size_t o_extra = take(((size_t)tcap * kc / gw::kGemvPass + 1) * 4);
     const size_t o_lists = take((size_t)Ec * tcap * 4);
     const size_t o_act = take((size_t)tcap * kc * Fc * 2);
     const size_t o_ybuf = take((size_t)tcap * kc * Hc * 4);
@@ -180,12 +181,14 @@ gw_status ensure_work(gw_ctx* c, const gw_bank* b, int T) {
     const size_t o_aq = take((size_t)tcap * kc * Fc);
     const size_t o_asf = take((size_t)tcap * kc * ((Fc + 127) / 128) * 4);
     const size_t o_done = take((size_t)(tcap / 8 + 1) * 4);
+    const size_t o_sched = take(8);
     cudaError_t e = c->work.ensure(off);
     if (e != cudaSuccess) return cuda_fail(e, "workspace allocation");
     char* base = static_cast<char*>(c->work.p);
     GW_CUDA(cudaMemsetAsync(base + o_done, 0, (size_t)(tcap / 8 + 1) * 4, c->cur));
-    GW_CUDA(cudaMemsetAsync(base + o_nactive, 0, 4, c->cur));
+    GW_CUDA(cudaMemsetAsync(base + o_nactive, 0, 8, c->cur));
     GW_CUDA(cudaMemsetAsync(base + o_counts, 0, (size_t)Ec * 4, c->cur));
+    GW_CUDA(cudaMemsetAsync(base + o_sched, 0, 8, c->cur));
     gw::MoeWork& w = c->w;
     w.tcap = tcap;
     w.xr = base + o_xr;
@@ -197,6 +200,8 @@ gw_status ensure_work(gw_ctx* c, const gw_bank* b, int T) {
     w.counts = reinterpret_cast<int32_t*>(base + o_counts);
     w.active = reinterpret_cast<int32_t*>(base + o_active);
     w.nactive = reinterpret_cast<int32_t*>(base + o_nactive);
+    w.nextra = w.nactive + 1;
+    w.extra = reinterpret_cast<int32_t*>(base + o_extra);
     w.lists = reinterpret_cast<int32_t*>(base + o_lists);
     w.act = reinterpret_cast<__half*>(base + o_act);
     w.ybuf = reinterpret_cast<float*>(base + o_ybuf);
@@ -206,6 +211,7 @@ gw_status ensure_work(gw_ctx* c, const gw_bank* b, int T) {
     w.aq = reinterpret_cast<uint8_t*>(base + o_aq);
     w.asf = reinterpret_cast<uint32_t*>(base + o_asf);
     w.done = reinterpret_cast<unsigned*>(base + o_done);
+    w.sched = reinterpret_cast<unsigned*>(base + o_sched);
     w.status = c->status;
     w.mma_min_avg = c->mma_min_avg;
     w.block_scaled = c->block_scaled;
@@ -373,7 +379,8 @@ gw_status gw_init(int32_t device, gw_ctx** out) {
     if (prop.major != 10)
         return fail(GW_E_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a",
                     device, prop.major, prop.minor);
-    if (gw::configure_kernels() != 0 || gw::configure_grouped() != 0 || gw::configure_expert_gemv() != 0)
+    if (gw::configure_kernels() != 0 || gw::configure_grouped() != 0 || gw::configure_expert_gemv() != 0 ||
+        gw::configure_int8() != 0)
         return cuda_fail(cudaGetLastError(), "kernel attributes");
     gw_ctx* c = new gw_ctx();
     c->device = device;
@@ -1025,7 +1032,64 @@ gw_status gw_mxfp4_gemv_batched_async(gw_ctx* c, int32_t count_m, const uint8_t*
                        x, x_stride, x_dtype, y, y_stride, rows, cols);
 }
 
+namespace {
+gw_status check_int8(const void* codes, const void* meta, const void* x, const void* y, int T, int rows,
+                     int cols, int y_dtype) {
+    if (!codes || !meta || !x || !y) return fail(GW_E_ARG, "null argument");
+    if (T <= 0 || rows <= 0 || cols <= 0 || cols % 64)
+        return fail(GW_E_ARG, "need T > 0, rows > 0 and cols a positive multiple of 64 (got T=%d, %d x %d)",
+                    T, rows, cols);
+    if (cols > gw::kMaxInt8Cols) return fail(GW_E_ARG, "cols %d exceeds %d", cols, gw::kMaxInt8Cols);
+    if (y_dtype != GW_DTYPE_F32 && y_dtype != GW_DTYPE_F16)
+        return fail(GW_E_ARG, "y_dtype must be GW_DTYPE_F32 or GW_DTYPE_F16 (got %d)", y_dtype);
+    return GW_OK;
+}
+}  // namespace
+
+gw_status gw_int8_affine_gemv_async(gw_ctx* c, const uint8_t* codes, const uint16_t* meta,
+                                    const uint16_t* bias, const uint16_t* x, int32_t T, int32_t rows,
+                                    int32_t cols, void* y, int32_t y_dtype) {
+    if (!c) return fail(GW_E_ARG, "null context");
+    gw_status st = check_int8(codes, meta, x, y, T, rows, cols, y_dtype);
+    if (st) return st;
+    if ((st = check_align16(codes, "codes_dev")) || (st = check_align16(x, "x_dev"))) return st;
+    if (reinterpret_cast<uintptr_t>(meta) % 4) return fail(GW_E_ARG, "meta_dev must be 4-byte aligned");
+    CtxLock lk(c);
+    if ((st = set_device(c))) return st;
+    return count(c, gw::launch_int8_gemv(codes, meta, bias, reinterpret_cast<const __half*>(x), T, rows, cols,
+                                         y, y_dtype == GW_DTYPE_F16, c->cur));
+}
+
 // ---- synchronous host-pointer API ------------------------------------------
+
+gw_status gw_int8_affine_gemv(gw_ctx* c, const uint8_t* codes, const uint16_t* meta, const uint16_t* bias,
+                              const uint16_t* x, int32_t T, int32_t rows, int32_t cols, void* y,
+                              int32_t y_dtype) {
+    if (!c) return fail(GW_E_ARG, "null context");
+    gw_status st = check_int8(codes, meta, x, y, T, rows, cols, y_dtype);
+    if (st) return st;
+    CtxLock lk(c);
+    if ((st = set_device(c))) return st;
+    Stage sg(c);
+    const size_t nc = (size_t)rows * cols, nm = (size_t)rows * (cols / 64) * 4, nx = (size_t)T * cols * 2;
+    const size_t ny = (size_t)T * rows * (y_dtype == GW_DTYPE_F16 ? 2 : 4);
+    const size_t oc = sg.add(nc), om = sg.add(nm), ob = sg.add(bias ? (size_t)rows * 2 : 0), ox = sg.add(nx),
+                 oy = sg.add(ny);
+    cudaError_t e = sg.alloc();
+    if (e != cudaSuccess) return cuda_fail(e, "staging allocation");
+    GW_CUDA(cudaMemcpyAsync(sg.at<uint8_t>(oc), codes, nc, cudaMemcpyHostToDevice, c->cur));
+    GW_CUDA(cudaMemcpyAsync(sg.at<uint8_t>(om), meta, nm, cudaMemcpyHostToDevice, c->cur));
+    if (bias) GW_CUDA(cudaMemcpyAsync(sg.at<uint8_t>(ob), bias, (size_t)rows * 2, cudaMemcpyHostToDevice, c->cur));
+    GW_CUDA(cudaMemcpyAsync(sg.at<uint8_t>(ox), x, nx, cudaMemcpyHostToDevice, c->cur));
+    if ((st = count(c, gw::launch_int8_gemv(sg.at<uint8_t>(oc), sg.at<uint16_t>(om),
+                                            bias ? sg.at<uint16_t>(ob) : nullptr, sg.at<__half>(ox), T, rows,
+                                            cols, sg.at<void>(oy), y_dtype == GW_DTYPE_F16, c->cur))))
+        return st;
+    GW_CUDA(cudaMemcpyAsync(y, sg.at<uint8_t>(oy), ny, cudaMemcpyDeviceToHost, c->cur));
+    GW_CUDA(cudaStreamSynchronize(c->cur));
+    return GW_OK;
+}
+
 
 
 gw_status gw_mxfp4_gemv(gw_ctx* c, const uint8_t* packed, const uint8_t* scales,
@@ -1103,7 +1167,7 @@ gw_status gw_router_logits(gw_ctx* c, gw_bank* b, int32_t layer, const void* x, 
                                          c->cur))))
         return st;
     GW_CUDA(cudaMemsetAsync(c->w.counts, 0, (size_t)d.E * 4, c->cur));
-    GW_CUDA(cudaMemsetAsync(c->w.nactive, 0, 4, c->cur));
+    GW_CUDA(cudaMemsetAsync(c->w.nactive, 0, 8, c->cur));  // and nextra
     GW_CUDA(cudaMemcpyAsync(logits, c->w.logits, (size_t)T * d.E * 4, cudaMemcpyDeviceToHost, c->cur));
     GW_CUDA(cudaStreamSynchronize(c->cur));
     return GW_OK;
@@ -1127,7 +1191,7 @@ gw_status gw_route_async(gw_ctx* c, gw_bank* b, int32_t layer, const void* x_dev
     // the router also grouped the slots for the expert kernels: leave the
     // counts at zero for the next layer call, as the combine would
     GW_CUDA(cudaMemsetAsync(c->w.counts, 0, (size_t)d.E * 4, c->cur));
-    GW_CUDA(cudaMemsetAsync(c->w.nactive, 0, 4, c->cur));
+    GW_CUDA(cudaMemsetAsync(c->w.nactive, 0, 8, c->cur));  // and nextra
     const size_t nk = (size_t)T * d.k;
     GW_CUDA(cudaMemcpyAsync(experts_dev, c->w.experts, nk * 4, cudaMemcpyDeviceToDevice, c->cur));
     GW_CUDA(cudaMemcpyAsync(weights_dev, c->w.weights, nk * 4, cudaMemcpyDeviceToDevice, c->cur));
@@ -1154,7 +1218,7 @@ gw_status gw_route(gw_ctx* c, gw_bank* b, int32_t layer, const void* x, int32_t 
                                          c->cur))))
         return st;
     GW_CUDA(cudaMemsetAsync(c->w.counts, 0, (size_t)d.E * 4, c->cur));
-    GW_CUDA(cudaMemsetAsync(c->w.nactive, 0, 4, c->cur));
+    GW_CUDA(cudaMemsetAsync(c->w.nactive, 0, 8, c->cur));  // and nextra
     const size_t nk = (size_t)T * d.k;
     GW_CUDA(cudaMemcpyAsync(experts_out, c->w.experts, nk * 4, cudaMemcpyDeviceToHost, c->cur));
     GW_CUDA(cudaMemcpyAsync(weights_out, c->w.weights, nk * 4, cudaMemcpyDeviceToHost, c->cur));
@@ -1315,11 +1379,13 @@ extern "C" GW_API gw_status gw_moe_forward_noalloc_async(gw_ctx* c, gw_bank* b, 
     const size_t o_weights = take((size_t)T * k * 4);
     const size_t o_counts = take((size_t)E * 4);
     const size_t o_active = take((size_t)E * 4);
-    const size_t o_nactive = take(4);
+    const size_t o_nactive = take(8);  // nactive, nextra
+    const size_t o_extra = take(((size_t)T * k / gw::kGemvPass + 1) * 4);
     const size_t o_lists = take((size_t)E * T * 4);
     const size_t o_act = take((size_t)T * k * F * 2);
     const size_t o_ybuf = take((size_t)T * k * H * 4);
     const size_t o_done = take((size_t)(T / 8 + 1) * 4);
+    const size_t o_sched = take(8);
     if (off > kNoAllocScratchBytes)
         return fail(GW_E_ARG,
                     "T=%d needs %zu bytes of layer scratch; the no-allocation path holds %zu "
@@ -1341,16 +1407,20 @@ extern "C" GW_API gw_status gw_moe_forward_noalloc_async(gw_ctx* c, gw_bank* b, 
     w.counts = reinterpret_cast<int32_t*>(base + o_counts);
     w.active = reinterpret_cast<int32_t*>(base + o_active);
     w.nactive = reinterpret_cast<int32_t*>(base + o_nactive);
+    w.nextra = w.nactive + 1;
+    w.extra = reinterpret_cast<int32_t*>(base + o_extra);
     w.lists = reinterpret_cast<int32_t*>(base + o_lists);
     w.act = reinterpret_cast<__half*>(base + o_act);
     w.ybuf = reinterpret_cast<float*>(base + o_ybuf);
     w.done = reinterpret_cast<unsigned*>(base + o_done);
+    w.sched = reinterpret_cast<unsigned*>(base + o_sched);
     w.status = c->status;
     // The array keeps whatever the previous call left: clear the expert counts,
     // the active-expert count and the router completion counters.
     GW_CUDA(cudaMemsetAsync(base + o_counts, 0, (size_t)E * 4, c->cur));
-    GW_CUDA(cudaMemsetAsync(base + o_nactive, 0, 4, c->cur));
+    GW_CUDA(cudaMemsetAsync(base + o_nactive, 0, 8, c->cur));
     GW_CUDA(cudaMemsetAsync(base + o_done, 0, (size_t)(T / 8 + 1) * 4, c->cur));
+    GW_CUDA(cudaMemsetAsync(base + o_sched, 0, 8, c->cur));
     const gw::MoeDims d = dims_of(b);
     const gw::LayerView L = layer_of(b, layer);
     if ((st = count(c, gw::launch_router(L, d, x_dev, x_dtype, T, w, c->cur)))) return st;

@@ -59,7 +59,7 @@ constexpr int kCT = kEW * kNT;               // tiles per stage (per round)
 constexpr int kBoxT = 6;                     // tiles per TMA box of weights (divides kCT / 4)
 constexpr int kEThreads = (kEW + 1) * 32;    // + the producer warp
 constexpr int kEStages = 3;                  // stages in flight per CTA
-constexpr int kEPass = 4;                    // tokens per pass over the weights
+constexpr int kEPass = kGemvPass;            // tokens per pass over the weights
 constexpr int kGrp = 2048;                   // one tile's full group: 16 rows x 128 bytes
 constexpr int kGrpSc = 128;                  // its scale bytes
 constexpr int kStageW = kCT * kGrp;          // 48 KB of weights per stage
@@ -75,7 +75,6 @@ struct ExpertGemvArgs {
     int64_t off_bias;
     int M, K;              // matrix rows, columns
     int ksplit;            // K-splits (tiles per split = kCT / ksplit)
-    int rounds;            // tile rounds per CTA: round r covers kCT / ksplit tiles
     int k, shard_count;
     int F, H;
     float limit, alpha;
@@ -103,7 +102,7 @@ __host__ __device__ inline SmemPlan smem_plan(int K) {
     p.sc = p.ring + kEStages * kStageW;
     p.xe = p.sc + kEStages * kStageS;
     p.red = p.xe + ngrp * 8 * 8 * 64;
-    p.bars = p.red + 2 * kCT * 2 * 8 * kEPass * 4;
+    p.bars = p.red + kCT * 2 * 8 * kEPass * 4;
     p.total = p.bars + 2 * kEStages * 8 + 16 + 1024;  // + abort flag, alignment slack
     return p;
 }
@@ -226,7 +225,7 @@ __device__ __forceinline__ void group_mma(const unsigned char* A, int astep, con
                     acc[ti][1][0] = fmaf(d0[ti][2] + d1[ti][2], scale(ti, g + 8, 2 * t), acc[ti][1][0]);
                     acc[ti][1][0] = fmaf(d0[ti][3] + d1[ti][3], scale(ti, g + 8, 2 * t + 1), acc[ti][1][0]);
                 } else {  // columns 2t, 2t + 1 share one block
-                    const int bi = jb + (kTok == 2 ? t : (t >> 1));
+                    const int bi = jb + (kTok == 2 ? t : kTok == 4 ? (t >> 1) : 0);
                     const float fa = scale(ti, g, bi), fb = scale(ti, g + 8, bi);
                     acc[ti][0][0] = fmaf(d0[ti][0] + d1[ti][0], fa, acc[ti][0][0]);
                     acc[ti][0][1] = fmaf(d0[ti][1] + d1[ti][1], fa, acc[ti][0][1]);
@@ -251,6 +250,17 @@ __device__ __forceinline__ void arrive(uint32_t bar) {
 }
 // the kEW consumer warps only
 __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kEW * 32) : "memory"); }
+// the same barrier, returning whether any consumer thread passed true
+__device__ __forceinline__ bool consumers_sync_or(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.or.pred p, 1, %2, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "n"(kEW * 32)
+        : "memory");
+    return r != 0;
+}
 
 __device__ __forceinline__ void tma_4d(uint32_t dst, const CUtensorMap* map, int c1, int c2, int c3, uint32_t bar) {
     asm volatile(
@@ -269,22 +279,25 @@ __device__ __forceinline__ void tma_3d(uint32_t dst, const CUtensorMap* map, int
 
 // kMode 0 / 1: gate_up with the clamped GLU / SiLU epilogue (f16 activations
 // per slot); 2: down x routing weight (fp32 per slot).
-// grid (min(E, T*k), ceil(tiles / (rounds * kCT / ksplit))), kEThreads threads.
+//
+// Persistent: `gridDim.x` CTAs (at most one per SM) share the layer's work
+// items — item i = (active expert i / ny, tile round i % ny), a round being
+// kCT / ksplit tiles over the whole K range — through the self-resetting
+// counter pair a.w.sched (next item, CTAs finished).  The producer warp takes
+// the next item as soon as it has issued the last stage of the current one,
+// so the weight stream of an SM runs on across items while the consumers
+// finish one item's epilogue and stage the next item's tokens.  Each stage
+// carries its item id in shared memory; item -1 ends the consumers' loop.
 template <int kMode>
 __global__ void __launch_bounds__(kEThreads, 1) k_expert_gemv(const __grid_constant__ GemvMaps maps,
                                                               ExpertGemvArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    const int ai = blockIdx.x;
-    if (ai >= *a.w.nactive) return;
-    // a wait of this launch (or an earlier one since the last gw_sync) ran
-    // out: the results are already invalid, so do no more work
-    if (a.w.status && (*(volatile unsigned*)a.w.status & kStatusGemv)) return;
-    const int e = a.w.active[ai];
     const SmemPlan P = smem_plan(a.K);
     const uint32_t sbase = (saddr(smem_raw) + 1023u) & ~1023u;
     unsigned char* sgen = smem_raw + (sbase - saddr(smem_raw));
     __shared__ int meta_row[kEPass], meta_slot[kEPass];
     __shared__ float meta_mul[kEPass];
+    __shared__ int stage_item[kEStages];
 
     // the warp index through a shuffle: the compiler then knows every value
     // derived from it is warp-uniform
@@ -293,18 +306,9 @@ __global__ void __launch_bounds__(kEThreads, 1) k_expert_gemv(const __grid_const
     const int nblk = a.K >> 5, nfull = nblk >> 3, ngrp = (nblk + 7) >> 3;
     const int wlast = nblk - 8 * (ngrp - 1);
     const int ntiles = a.M >> 4;
-    const int ks = a.ksplit, tb = kCT / ks;  // tiles per split and round
-    const int per = (ngrp + ks - 1) / ks;           // stages per pass
-    const int cnt = min(a.w.counts[e], a.w.tcap);
-    const int npass = (cnt + kEPass - 1) / kEPass;
-    const int R = a.rounds;
-    const int total = per * R * npass;
-    const int le = e / a.shard_count;
-    const int tile0 = blockIdx.y * tb * R;
-    // Within a stage, split sp owns the region a full box would fill (tb
-    // tiles x 2 KB of weights, tb x 128 B of scales) whether its group is full
-    // or narrow: a stage can mix the two, and every TMA destination starts on a
-    // 128-byte boundary.
+    const int ks = a.ksplit, tb = kCT / ks;  // tiles per split and item
+    const int per = (ngrp + ks - 1) / ks;    // stages per pass
+    const int ny = (ntiles + tb - 1) / tb;   // items per expert
     unsigned* status = a.w.status;
     const uint32_t fullb = sbase + P.bars, emptyb = fullb + kEStages * 8;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(sgen + P.bars + 2 * kEStages * 8);
@@ -318,54 +322,83 @@ __global__ void __launch_bounds__(kEThreads, 1) k_expert_gemv(const __grid_const
     __syncthreads();
 
     if (warp == kEW) {
-        // ---- producer: stage i = (pass, round r, step s) in that nesting;
-        // split sp's group sp * per + s of tiles tile0 + r * tb ...
+        // ---- producer: stages of an item = steps s; split sp's group
+        // sp * per + s of the item's tiles
         if (elect_one()) {
-            int slot = 0, s = 0, r = 0;
+            // a wait of this launch (or an earlier one since the last gw_sync)
+            // ran out: the results are already invalid, so take no work
+            const bool dead = status && (*(volatile unsigned*)status & kStatusGemv);
+            const int na = *a.w.nactive;
+            const int nitems = dead ? 0 : (na + *a.w.nextra) * ny;
+            int slot = 0;
             uint32_t phase = 0;
+            long long it = 0;  // stages issued
             bool ok = true;
-            for (int i = 0; i < total; ++i) {
-                if (i >= kEStages && ok) {
+            auto acquire = [&]() {  // the next ring slot is free (bounded wait)
+                if (it >= kEStages && ok) {
                     ok = wait_parity(emptyb + slot * 8, phase ^ 1, status);
                     if (!ok) *abort_flag = 1;
                 }
                 if (ok && *abort_flag) ok = false;
-                if (!ok) break;
-                uint32_t bytes = 0;
-                for (int sp = 0; sp < ks; ++sp) {
-                    const int grp = sp * per + s;
-                    if (grp >= min(ngrp, (sp + 1) * per)) continue;
-                    bytes += grp < nfull ? (uint32_t)tb * (kGrp + kGrpSc) : (uint32_t)tb * 17u * 16u * wlast;
-                }
-                const uint32_t bar = fullb + slot * 8;
-                arrive_tx(bar, bytes);
-                for (int sp = 0; sp < ks; ++sp) {
-                    const int grp = sp * per + s;
-                    if (grp >= min(ngrp, (sp + 1) * per)) continue;
-                    const uint32_t wdst = sbase + P.ring + slot * kStageW;
-                    const uint32_t sdst = sbase + P.sc + slot * kStageS;
-                    const int tt = tile0 + r * tb;
-                    if (grp < nfull) {
-                        for (int b = 0; b < tb; b += kBoxT)
-                            tma_5d(wdst + (sp * tb + b) * kGrp, &maps.w_full, grp, tt + b, le, bar);
-                        tma_4d(sdst + sp * tb * kGrpSc, &maps.s_full, grp, tt, le, bar);
-                    } else {
-                        for (int b = 0; b < tb; b += kBoxT)
-                            tma_4d(wdst + sp * tb * kGrp + b * 256 * wlast, &maps.w_narrow, 0, tt + b, le, bar);
-                        tma_3d(sdst + sp * tb * kGrpSc, &maps.s_narrow, tt, le, bar);
+                return ok;
+            };
+            // the first item is the CTA's own; later ones come from the counter,
+            // requested while the current item's first stage is in flight
+            int item = blockIdx.x;
+            while (item < nitems) {
+                const int q = item / ny;
+                const int e = q < na ? a.w.active[q] : (a.w.extra[q - na] & 0xFFFF);
+                const int le = e / a.shard_count;
+                const int tt = (item % ny) * tb;
+                int next = nitems;
+                for (int i = 0, s = 0; i < per; ++i) {
+                    if (!acquire()) break;
+                    uint32_t bytes = 0;
+                    for (int sp = 0; sp < ks; ++sp) {
+                        const int grp = sp * per + s;
+                        if (grp >= min(ngrp, (sp + 1) * per)) continue;
+                        bytes += grp < nfull ? (uint32_t)tb * (kGrp + kGrpSc) : (uint32_t)tb * 17u * 16u * wlast;
                     }
+                    stage_item[slot] = item;
+                    const uint32_t bar = fullb + slot * 8;
+                    arrive_tx(bar, bytes);
+                    for (int sp = 0; sp < ks; ++sp) {
+                        const int grp = sp * per + s;
+                        if (grp >= min(ngrp, (sp + 1) * per)) continue;
+                        const uint32_t wdst = sbase + P.ring + slot * kStageW;
+                        const uint32_t sdst = sbase + P.sc + slot * kStageS;
+                        if (grp < nfull) {
+                            for (int b = 0; b < tb; b += kBoxT)
+                                tma_5d(wdst + (sp * tb + b) * kGrp, &maps.w_full, grp, tt + b, le, bar);
+                            tma_4d(sdst + sp * tb * kGrpSc, &maps.s_full, grp, tt, le, bar);
+                        } else {
+                            for (int b = 0; b < tb; b += kBoxT)
+                                tma_4d(wdst + sp * tb * kGrp + b * 256 * wlast, &maps.w_narrow, 0, tt + b, le, bar);
+                            tma_3d(sdst + sp * tb * kGrpSc, &maps.s_narrow, tt, le, bar);
+                        }
+                    }
+                    if (i == 0) next = (int)gridDim.x + (int)atomicAdd(&a.w.sched[0], 1u);
+                    if (++s == per) s = 0;
+                    ++it;
+                    if (++slot == kEStages) { slot = 0; phase ^= 1; }
                 }
-                if (++s == per) {
-                    s = 0;
-                    if (++r == R) r = 0;
-                }
-                if (++slot == kEStages) { slot = 0; phase ^= 1; }
+                if (!ok) break;
+                item = next;
+            }
+            // end of work: a stage without copies whose item id is -1
+            if (acquire()) {
+                stage_item[slot] = -1;
+                arrive(fullb + slot * 8);
+            } else {
+                // after a wait ran out: let the copies still in flight land
+                for (long long j = it - kEStages > 0 ? it - kEStages : 0; j < it; ++j)
+                    (void)wait_parity(fullb + (j % kEStages) * 8, (uint32_t)((j / kEStages) & 1), nullptr);
             }
         }
         __syncwarp();
     } else {
-        // ---- consumers: warp = (split sp, position wl); its kNT tiles of a
-        // round are tiles wl * kNT .. + kNT - 1 of the split's tb
+        // ---- consumers: warp = (split sp, position wl); its kNT tiles of an
+        // item are tiles wl * kNT .. + kNT - 1 of the split's tb
         const int wps = kEW / ks;  // consumer warps per split
         const int sp = warp / wps, wl = warp % wps;
         const int g0 = min(ngrp, sp * per), g1 = min(ngrp, g0 + per);
@@ -376,72 +409,90 @@ __global__ void __launch_bounds__(kEThreads, 1) k_expert_gemv(const __grid_const
         uint32_t off[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) off[j] = (uint32_t)((j ^ g) << 4);
-        const int* list = a.w.lists + (int64_t)e * a.w.tcap;
         const __half* xsrc = kMode == 2 ? a.w.act : a.w.x16;
         const unsigned char* xg0 = sgen + P.xe + g * 64 + 16 * t;
-        float* red0 = reinterpret_cast<float*>(sgen + P.red);
+        float* red = reinterpret_cast<float*>(sgen + P.red);
         bool ok = true;
         int slot = 0;
         uint32_t phase = 0;
-        for (int p = 0; p < npass; ++p) {
-            const int c0 = p * kEPass, n = min(kEPass, cnt - c0);
-            consumers_sync();  // the previous pass's staged x, results and metadata are consumed
-            if (threadIdx.x < n) {
-                const int sl = list[c0 + threadIdx.x];
-                const int row = kMode == 2 ? sl : sl / a.k;
-                meta_slot[threadIdx.x] = sl;
-                meta_row[threadIdx.x] = row;
-                meta_mul[threadIdx.x] = kMode == 2 ? a.w.weights[sl] : a.w.xmul[row];
+        auto wait_full = [&]() {  // this warp's bounded wait on the current stage
+            if (ok) {
+                ok = try_parity(fullb + slot * 8, phase) || wait_parity(fullb + slot * 8, phase, status);
+                if (!ok) *abort_flag = 1;
             }
-            consumers_sync();
-            // B entries: quarter q of (group, block j, column c) <- x[token of c][block] or zeros
-            for (int i = threadIdx.x; i < ngrp * 256; i += kEW * 32) {
-                const int q = i & 3, c = (i >> 2) & 7, j = (i >> 5) & 7, grp = i >> 8;
-                bool live;
-                int tok;
-                if (n == 1) { live = j == c; tok = 0; }
-                else if (n == 2) { live = (j & 3) == (c >> 1); tok = c & 1; }
-                else { live = (j & 1) == (c >> 2); tok = c & 3; }
-                live = live && tok < n && grp * 8 + j < nblk;
-                uint4 v = make_uint4(0u, 0u, 0u, 0u);
-                if (live)
-                    v = __ldg(reinterpret_cast<const uint4*>(xsrc + (int64_t)meta_row[tok] * a.K) + (grp * 8 + j) * 4 + q);
-                reinterpret_cast<uint4*>(sgen + P.xe)[i] = v;
+            ok = __all_sync(0xffffffffu, ok) && !*abort_flag;
+            return ok;
+        };
+        // Every consumer warp runs the same sequence of consumer barriers: the
+        // decisions to stop (end of work, or a wait that ran out anywhere in
+        // the CTA) are taken at a barrier with an OR over all consumers.
+        const int na = *a.w.nactive;
+        for (;;) {
+            // (also: the previous item's staged x, results and metadata are consumed)
+            const bool here = wait_full();
+            if (consumers_sync_or(!here)) break;
+            const int item = stage_item[slot];
+            if (item < 0) break;
+            // item -> (expert, pass of up to kEPass of its tokens, tile round)
+            const int q = item / ny;
+            const int ex = q < na ? 0 : a.w.extra[q - na];
+            const int e = q < na ? a.w.active[q] : (ex & 0xFFFF);
+            const int c0 = (ex >> 16) * kEPass;
+            const int n = min(kEPass, min(a.w.counts[e], a.w.tcap) - c0);
+            const int* list = a.w.lists + (int64_t)e * a.w.tcap;
+            const int le = e / a.shard_count;
+            const int tile0 = (item % ny) * tb;
+            const bool any = tile0 + wl * kNT < ntiles;  // the warp's first tile exists
+            // the bias pair each emitting lane adds (gate_up: rows 2f, 2f + 1 of
+            // feature f = tile * 8 + g; down: rows tile * 16 + g, + 8), loaded
+            // now so its latency hides behind the stage loop
+            float bias0[kNT], bias1[kNT];
+            {
+                const uint16_t* bias =
+                    reinterpret_cast<const uint16_t*>(a.base + (int64_t)le * a.stride + a.off_bias);
+#pragma unroll
+                for (int ti = 0; ti < kNT; ++ti) {
+                    const int tile = tile0 + wl * kNT + ti;
+                    bias0[ti] = bias1[ti] = 0.f;
+                    if (sp == 0 && tile < ntiles) {
+                        const int i0 = kMode == 2 ? tile * 16 + g : 2 * (tile * 8 + g);
+                        const int i1 = kMode == 2 ? i0 + 8 : i0 + 1;
+                        bias0[ti] = bf16_bits_to_f32(__ldg(bias + i0));
+                        bias1[ti] = bf16_bits_to_f32(__ldg(bias + i1));
+                    }
+                }
             }
-            consumers_sync();
-            for (int r = 0; r < R; ++r) {
-                float* red = red0 + (r & 1) * (kCT * 2 * 8 * kEPass);  // double-buffered by round
+            {
+                if (threadIdx.x < n) {
+                    const int sl = list[c0 + threadIdx.x];
+                    const int row = kMode == 2 ? sl : sl / a.k;
+                    meta_slot[threadIdx.x] = sl;
+                    meta_row[threadIdx.x] = row;
+                    meta_mul[threadIdx.x] = kMode == 2 ? a.w.weights[sl] : a.w.xmul[row];
+                }
+                consumers_sync();
+                // B entries: quarter q of (group, block j, column c) <- x[token of c][block] or zeros
+                for (int i = threadIdx.x; i < ngrp * 256; i += kEW * 32) {
+                    const int q = i & 3, c = (i >> 2) & 7, j = (i >> 5) & 7, grp = i >> 8;
+                    bool live;
+                    int tok;
+                    if (n == 1) { live = j == c; tok = 0; }
+                    else if (n == 2) { live = (j & 3) == (c >> 1); tok = c & 1; }
+                    else if (n <= 4) { live = (j & 1) == (c >> 2); tok = c & 3; }
+                    else { live = true; tok = c; }
+                    live = live && tok < n && grp * 8 + j < nblk;
+                    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                    if (live)
+                        v = __ldg(reinterpret_cast<const uint4*>(xsrc + (int64_t)meta_row[tok] * a.K) + (grp * 8 + j) * 4 + q);
+                    reinterpret_cast<uint4*>(sgen + P.xe)[i] = v;
+                }
+                consumers_sync();
                 float acc[kNT][2][2];
 #pragma unroll
                 for (int ti = 0; ti < kNT; ++ti) acc[ti][0][0] = acc[ti][0][1] = acc[ti][1][0] = acc[ti][1][1] = 0.f;
-                const bool any = tile0 + r * tb + wl * kNT < ntiles;  // the warp's first tile exists
-                // the bias pair each emitting lane adds, loaded now so its latency
-                // hides behind the stage loop (gate_up: rows 2f, 2f + 1 of feature
-                // f = tile * 8 + g; down: rows tile * 16 + g, + 8)
-                float bias0[kNT], bias1[kNT];
-                {
-                    const uint16_t* bias =
-                        reinterpret_cast<const uint16_t*>(a.base + (int64_t)le * a.stride + a.off_bias);
-#pragma unroll
-                    for (int ti = 0; ti < kNT; ++ti) {
-                        const int tile = tile0 + r * tb + wl * kNT + ti;
-                        bias0[ti] = bias1[ti] = 0.f;
-                        if (sp == 0 && tile < ntiles) {
-                            const int i0 = kMode == 2 ? tile * 16 + g : 2 * (tile * 8 + g);
-                            const int i1 = kMode == 2 ? i0 + 8 : i0 + 1;
-                            bias0[ti] = bf16_bits_to_f32(__ldg(bias + i0));
-                            bias1[ti] = bf16_bits_to_f32(__ldg(bias + i1));
-                        }
-                    }
-                }
                 for (int s = 0; s < per; ++s) {
-                    if (ok) {
-                        ok = try_parity(fullb + slot * 8, phase) || wait_parity(fullb + slot * 8, phase, status);
-                        if (!ok) *abort_flag = 1;
-                    }
-                    ok = __all_sync(0xffffffffu, ok) && !*abort_flag;
                     const int grp = g0 + s;
-                    if (ok && any && grp < g1) {
+                    if (wait_full() && any && grp < g1) {
                         const unsigned char* xg = xg0 + grp * 4096;
                         const unsigned char* W = sgen + P.ring + slot * kStageW + sp * tb * kGrp;
                         const unsigned char* S = sgen + P.sc + slot * kStageS + sp * tb * kGrpSc;
@@ -450,14 +501,16 @@ __global__ void __launch_bounds__(kEThreads, 1) k_expert_gemv(const __grid_const
                             const unsigned char* Sc = S + wl * kNT * kGrpSc;
                             if (n == 1) group_mma<1, true>(A, kGrp, Sc, kGrpSc, 8, g, t, off, xg, acc);
                             else if (n == 2) group_mma<2, true>(A, kGrp, Sc, kGrpSc, 8, g, t, off, xg, acc);
-                            else group_mma<4, true>(A, kGrp, Sc, kGrpSc, 8, g, t, off, xg, acc);
+                            else if (n <= 4) group_mma<4, true>(A, kGrp, Sc, kGrpSc, 8, g, t, off, xg, acc);
+                            else group_mma<8, true>(A, kGrp, Sc, kGrpSc, 8, g, t, off, xg, acc);
                         } else {
                             const unsigned char* A = W + wl * kNT * 256 * wlast;
                             const unsigned char* Sc = S + wl * kNT * 16 * wlast;
                             const int as = 256 * wlast, ss = 16 * wlast;
                             if (n == 1) group_mma<1, false>(A, as, Sc, ss, wlast, g, t, off, xg, acc);
                             else if (n == 2) group_mma<2, false>(A, as, Sc, ss, wlast, g, t, off, xg, acc);
-                            else group_mma<4, false>(A, as, Sc, ss, wlast, g, t, off, xg, acc);
+                            else if (n <= 4) group_mma<4, false>(A, as, Sc, ss, wlast, g, t, off, xg, acc);
+                            else group_mma<8, false>(A, as, Sc, ss, wlast, g, t, off, xg, acc);
                         }
                     }
                     __syncwarp();
@@ -467,7 +520,7 @@ __global__ void __launch_bounds__(kEThreads, 1) k_expert_gemv(const __grid_const
 #pragma unroll
                 for (int ti = 0; ti < kNT; ++ti) {
                     const int tl = wl * kNT + ti;          // tile within the split
-                    if (tile0 + r * tb + tl >= ntiles) continue;
+                    if (tile0 + tl >= ntiles) continue;
                     // columns -> (row, token): sum the block slots held by the quad
                     float v[2][2];
 #pragma unroll
@@ -486,16 +539,19 @@ __global__ void __launch_bounds__(kEThreads, 1) k_expert_gemv(const __grid_const
                                 x += __shfl_xor_sync(0xffffffffu, x, 2);
                                 v[rr][c] = x;
                             }
-                        } else {
+                        } else if (n <= 4) {
 #pragma unroll
                             for (int c = 0; c < 2; ++c)
                                 v[rr][c] = acc[ti][rr][c] + __shfl_xor_sync(0xffffffffu, acc[ti][rr][c], 2);
+                        } else {
+                            v[rr][0] = acc[ti][rr][0];
+                            v[rr][1] = acc[ti][rr][1];
                         }
                     }
                     // red[tile slot][r][g][token] = tile row 8r + g
                     float* rw = red + (sp * tb + tl) * (2 * 8 * kEPass);
                     const int tk = n <= 2 ? 0 : 2 * t;
-                    if ((n <= 2 && t == 0) || (n > 2 && t < 2)) {
+                    if ((n <= 2 && t == 0) || (n > 2 && n <= 4 && t < 2) || n > 4) {
                         rw[0 * 8 * kEPass + g * kEPass + tk] = v[0][0];
                         rw[1 * 8 * kEPass + g * kEPass + tk] = v[1][0];
                         rw[0 * 8 * kEPass + g * kEPass + tk + 1] = v[0][1];
@@ -506,33 +562,38 @@ __global__ void __launch_bounds__(kEThreads, 1) k_expert_gemv(const __grid_const
                 // owns its tiles outright only for its own lanes
                 if (ks > 1) consumers_sync();
                 else __syncwarp();
-                // split-0 warps emit their tiles: lane (g, t) -> token t
-                if (sp == 0 && t < n && ok) {
-                    const int sl = meta_slot[t];
-                    const float mul = meta_mul[t];
+                // split-0 warps emit their tiles: lane (g, t) -> tokens t, t + 4
+                if (sp == 0 && ok) {
                     // gate_up: feature g = tile rows 2g (gate), 2g + 1 (up); down: rows g, g + 8
                     const int q0 = kMode == 2 ? g : 2 * g, q1 = kMode == 2 ? g + 8 : 2 * g + 1;
 #pragma unroll
-                    for (int ti = 0; ti < kNT; ++ti) {
-                        const int tl = wl * kNT + ti;
-                        const int tile = tile0 + r * tb + tl;
-                        if (tile >= ntiles) continue;
-                        float y0 = 0.f, y1 = 0.f;
-                        for (int q = 0; q < ks; ++q) {
-                            const float* rw = red + (q * tb + tl) * (2 * 8 * kEPass);
-                            y0 += rw[(q0 >> 3) * 8 * kEPass + (q0 & 7) * kEPass + t];
-                            y1 += rw[(q1 >> 3) * 8 * kEPass + (q1 & 7) * kEPass + t];
-                        }
-                        if (kMode != 2) {
-                            const int f = tile * 8 + g;
-                            const float gate = y0 * mul + bias0[ti];
-                            const float up = y1 * mul + bias1[ti];
-                            a.w.act[(int64_t)sl * a.F + f] = __float2half_rn(activate<kMode>(gate, up, a.limit, a.alpha));
-                        } else {
-                            const int r0 = tile * 16 + g;
-                            float* y = a.w.ybuf + (int64_t)sl * a.H;
-                            y[r0] = (y0 + bias0[ti]) * mul;
-                            y[r0 + 8] = (y1 + bias1[ti]) * mul;
+                    for (int half = 0; half < 2; ++half) {
+                        const int tok = t + 4 * half;
+                        if (tok >= n) break;
+                        const int sl = meta_slot[tok];
+                        const float mul = meta_mul[tok];
+#pragma unroll
+                        for (int ti = 0; ti < kNT; ++ti) {
+                            const int tl = wl * kNT + ti;
+                            const int tile = tile0 + tl;
+                            if (tile >= ntiles) continue;
+                            float y0 = 0.f, y1 = 0.f;
+                            for (int q = 0; q < ks; ++q) {
+                                const float* rw = red + (q * tb + tl) * (2 * 8 * kEPass);
+                                y0 += rw[(q0 >> 3) * 8 * kEPass + (q0 & 7) * kEPass + tok];
+                                y1 += rw[(q1 >> 3) * 8 * kEPass + (q1 & 7) * kEPass + tok];
+                            }
+                            if (kMode != 2) {
+                                const int f = tile * 8 + g;
+                                const float gate = y0 * mul + bias0[ti];
+                                const float up = y1 * mul + bias1[ti];
+                                a.w.act[(int64_t)sl * a.F + f] = __float2half_rn(activate<kMode>(gate, up, a.limit, a.alpha));
+                            } else {
+                                const int r0 = tile * 16 + g;
+                                float* y = a.w.ybuf + (int64_t)sl * a.H;
+                                y[r0] = (y0 + bias0[ti]) * mul;
+                                y[r0 + 8] = (y1 + bias1[ti]) * mul;
+                            }
                         }
                     }
                 }
@@ -540,9 +601,15 @@ __global__ void __launch_bounds__(kEThreads, 1) k_expert_gemv(const __grid_const
         }
     }
     __syncthreads();
-    // after a wait ran out: let the copies still in flight land before exit
-    if (warp == kEW && *abort_flag && elect_one())
-        for (int j = 0; j < kEStages; ++j) (void)wait_parity(fullb + j * 8, 0, nullptr), (void)wait_parity(fullb + j * 8, 1, nullptr);
+    // the last CTA to finish resets the work counters for the next launch
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(&a.w.sched[1], 1u) == gridDim.x - 1) {
+            a.w.sched[0] = 0;
+            a.w.sched[1] = 0;
+            __threadfence();
+        }
+    }
 }
 
 // Smallest K-split (1, 2, 4 or 8 warps per tile) that gives the launch
@@ -593,11 +660,6 @@ int launch_expert_gemv(const LayerView& L, const MoeDims& d, const MoeWork& w, i
     const int maxa = std::min(d.E, T * d.k);
     a.ksplit = pick_split(maxa, ntiles);
     const int tb = kCT / a.ksplit;
-    // Several rounds of tiles per CTA amortise its set-up and token staging;
-    // keep at least ~4 waves of CTAs.
-    a.rounds = 1;
-    while (a.rounds < 8 && (int64_t)maxa * ((ntiles + tb * a.rounds * 2 - 1) / (tb * a.rounds * 2)) >= 4 * 148)
-        a.rounds *= 2;
     // TMA views of the bank (uint8 elements; a tile is 16 * nblk * 16 bytes
     // of blocks and 16 * nblk bytes of scales; experts one stride apart):
     //   w_full   (128 B, 16 rows, full groups, tiles, experts), box (128, 16, 1, tb, 1), 128-byte swizzle
@@ -651,7 +713,14 @@ int launch_expert_gemv(const LayerView& L, const MoeDims& d, const MoeWork& w, i
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
     }
     if (!good) return -1;
-    const dim3 grid(maxa, (ntiles + tb * a.rounds - 1) / (tb * a.rounds));
+    // persistent: one CTA per SM, or one per work item when there are fewer
+    static int sms[16] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 16) return -1;
+    if (!sms[dev] && cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return -1;
+    const int items = (maxa + T * d.k / kEPass) * ((ntiles + tb - 1) / tb);
+    const dim3 grid(std::min(items, sms[dev]));
     const int smem = smem_plan(a.K).total;
     if (which == 1) k_expert_gemv<2><<<grid, kEThreads, smem, s>>>(maps, a);
     else if (d.act == 0) k_expert_gemv<0><<<grid, kEThreads, smem, s>>>(maps, a);

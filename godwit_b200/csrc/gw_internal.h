@@ -12,7 +12,8 @@ constexpr int kMaxTopK = 16;
 constexpr int kMaxExperts = 256;
 constexpr int kTokTile = 8;       // tokens per router CTA
 constexpr int kRouterMmaMinTokens = 128;  // bf16 batches from here on use k_router_mma
-constexpr int kGemvWarps = 4;     // warps per k_gemv CTA (one 16-row tile each)
+constexpr int kGemvWarps = 4;
+constexpr int kGemvPass = 8;      // tokens per pass of the expert GEMV over an expert's weights     // warps per k_gemv CTA (one 16-row tile each)
 
 // Element types of activation inputs.  F32 is internal: the residual stream
 // that the stack forward rounds to the configured input type.
@@ -47,6 +48,9 @@ struct MoeWork {
     int32_t* counts;   // [E]          tokens routed to each expert
     int32_t* active;   // [E]          experts with at least one token (any order)
     int32_t* nactive;  // [1]
+    int32_t* nextra;   // [1]          entries of `extra` (the word after *nactive)
+    int32_t* extra;    // [tcap*k/kGemvPass+1] expert | pass << 16 for each further
+                       //              kGemvPass-token pass an expert's tokens need
     int32_t* lists;    // [E][tcap]    slot ids (t*k + j) per expert
     __half* act;       // [tcap*k][F]  activated gate_up output (f16, as the reference); slot
                        //              order on the GEMV path, expert order on the tensor-core path
@@ -58,6 +62,7 @@ struct MoeWork {
     float* ybuf;       // [tcap*k][H]  routing-weighted down output per slot
     unsigned* done;    // [tcap/8+1]   router completion counter per token chunk (self-resetting)
     unsigned* status;  // [1]          sticky error bits set by bounded waits (nullptr: none)
+    unsigned* sched;   // [2]          expert GEMV work counter and finished-CTA count (self-resetting)
     int mma_min_avg;   // tensor-core expert path when T*k >= mma_min_avg * E (0: never)
     int block_scaled;  // tensor-core path as block-scaled MXFP4 x MXFP8 MMAs (activations quantised)
 };
@@ -108,6 +113,12 @@ int launch_expert_gemv(const LayerView& L, const MoeDims& d, const MoeWork& w, i
                        cudaStream_t s);
 bool expert_gemv_supported(const MoeDims& d);
 int configure_expert_gemv();
+// Trunk int8 affine GEMV (gw_int8.cu): y[T][rows] (fp32, or f16 when y_f16)
+// = dequant(codes, meta) . x[t] (+ bf16 bias); cols % 64 == 0.
+constexpr int kMaxInt8Cols = 16384;
+int launch_int8_gemv(const uint8_t* codes, const uint16_t* meta, const uint16_t* bias, const __half* x,
+                     int T, int rows, int cols, void* y, int y_f16, cudaStream_t s);
+int configure_int8();
 // Row-exponent table entries of a row-major scale matrix.
 int launch_rowexp(const uint8_t* scales, int rows, int cols, uint8_t* out, cudaStream_t s);
 int configure_kernels();

@@ -120,6 +120,9 @@ __device__ __forceinline__ void group_slot(const MoeDims& d, const MoeWork& w, i
     if (pos == 0) {
         const int a = atomicAdd(w.nactive, 1);
         w.active[a] = e;
+    } else if (pos % kGemvPass == 0) {  // the expert's tokens need one more GEMV pass
+        const int a = atomicAdd(w.nextra, 1);
+        w.extra[a] = e | ((pos / kGemvPass) << 16);
     }
     w.lists[(int64_t)e * w.tcap + pos] = slot;
 }
@@ -420,7 +423,7 @@ __global__ void __launch_bounds__(128) k_router_mma(LayerView L, MoeDims d, cons
 __global__ void __launch_bounds__(256) k_group(MoeDims d, const int32_t* __restrict__ experts_in,
                                                const float* __restrict__ weights_in, int T, MoeWork w) {
     for (int i = threadIdx.x; i < d.E; i += blockDim.x) w.counts[i] = 0;
-    if (threadIdx.x == 0) *w.nactive = 0;
+    if (threadIdx.x == 0) *w.nactive = *w.nextra = 0;
     __syncthreads();
     const int n = T * d.k;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -442,7 +445,7 @@ __global__ void k_combine(MoeDims d, MoeWork w, float* __restrict__ out, int acc
     // next router launch
     if (blockIdx.x == 0 && blockIdx.y == 0) {
         for (int i = threadIdx.x; i < d.E; i += blockDim.x) w.counts[i] = 0;
-        if (threadIdx.x == 0) *w.nactive = 0;
+        if (threadIdx.x == 0) *w.nactive = *w.nextra = 0;
     }
     if (h4 * 4 >= d.H) return;
     float4 s = make_float4(0.f, 0.f, 0.f, 0.f);

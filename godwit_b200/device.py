@@ -56,6 +56,21 @@ def gemv_batched(ctx: Context, packed: torch.Tensor, scales: torch.Tensor, bias:
          dtype_code(x), _p(y), y.stride(0), rows, cols)
 
 
+def int8_affine_gemv(ctx: Context, codes: torch.Tensor, meta: torch.Tensor, bias: torch.Tensor | None,
+                     x: torch.Tensor, y: torch.Tensor) -> None:
+    """codes [rows, cols] u8, meta [rows, cols/64, 2] bf16 bits (any 16-bit
+    storage), bias [rows] bf16 bits or None, x [T, cols] f16 -> y [T, rows]
+    (float32: int8_affine_gemv; float16: int8_affine_gemv_bias_batched)."""
+    rows, cols = codes.shape
+    if x.dtype != torch.float16:
+        raise _abi.GodwitCUDAError(_abi.GW_E_ARG, f"x must be float16 (got {x.dtype})")
+    code = {torch.float32: _abi.GW_DTYPE_F32, torch.float16: GW_DTYPE_F16}.get(y.dtype)
+    if code is None:
+        raise _abi.GodwitCUDAError(_abi.GW_E_ARG, f"y must be float32 or float16 (got {y.dtype})")
+    call("gw_int8_affine_gemv_async", ctx.handle, _p(codes), _p(meta), _p(bias), _p(x), x.shape[0], rows,
+         cols, _p(y), code)
+
+
 def moe_forward(ctx: Context, bank: ExpertBank, layer: int, x: torch.Tensor, out: torch.Tensor,
                 experts: torch.Tensor | None = None, weights: torch.Tensor | None = None) -> None:
     T = x.shape[0]

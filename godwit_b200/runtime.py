@@ -121,6 +121,26 @@ class Context:
              _dtype_code(dtype), _ptr(y), rows, cols)
         return y
 
+    def int8_affine_gemv(self, codes: np.ndarray, meta: np.ndarray, x: np.ndarray, *,
+                         bias: np.ndarray | None = None, out: str = "f32") -> np.ndarray:
+        """The trunk's int8 projection (int8_affine_gemv, router.metal:65-98, when
+        out="f32"; int8_affine_gemv_bias_batched, :107-141, when out="f16").
+        codes [rows, cols] uint8, meta [rows, cols/64, 2] bf16 bits (scale, zero),
+        x [T, cols] (or [cols]) f16 values, bias [rows] bf16 bits -> y [T, rows]."""
+        codes = np.ascontiguousarray(codes, dtype=np.uint8)
+        meta = np.ascontiguousarray(meta, dtype=np.uint16)
+        rows, cols = codes.shape
+        xb = np.atleast_2d(_bits16(x, "f16"))
+        if xb.shape[1] != cols:
+            raise GodwitCUDAError(_abi.GW_E_ARG, f"x has {xb.shape[1]} columns, W has {cols}")
+        T = xb.shape[0]
+        bb = None if bias is None else np.ascontiguousarray(bias, dtype=np.uint16)
+        code = {"f32": _abi.GW_DTYPE_F32, "f16": _abi.GW_DTYPE_F16}[out]
+        y = np.empty((T, rows), dtype=np.float32 if out == "f32" else np.float16)
+        call("gw_int8_affine_gemv", self.handle, _ptr(codes), _ptr(meta), _ptr(bb), _ptr(xb), T, rows,
+             cols, _ptr(y), code)
+        return y
+
     def mxfp4_dequant(self, packed: np.ndarray, scales: np.ndarray) -> np.ndarray:
         packed = np.ascontiguousarray(packed, dtype=np.uint8)
         scales = np.ascontiguousarray(scales, dtype=np.uint8)

@@ -19,6 +19,11 @@
  *                                           Sources/Godwit/Runtime/ModelReader.swift:73-76
  *   - mxfp4_gemv (benchmark GEMV)           Sources/Godwit/Metal/Quant/dequant_gemv.metal:37-67
  *   - MXFP4.decode (bit-exact dequant)      Sources/Godwit/Quant/MXFP4.swift:37-92
+ *   - int8_affine_gemv / int8_affine_gemv_bias_batched (the trunk's int8
+ *     projections: output head, attention q/k/v/o)
+ *                                           Sources/Godwit/Metal/MoE/router.metal:65-141,
+ *                                           Sources/Godwit/Runtime/ModelRunner.swift:165-190,
+ *                                           Sources/Godwit/Runtime/Attention.swift:218-240
  *
  * Conventions:
  *   - Synchronous calls (no `_async` suffix) take HOST pointers, copy inputs to
@@ -66,6 +71,9 @@ typedef int32_t gw_status;
  * configs feed bfloat16.  Both are accepted everywhere `x_dtype` appears. */
 #define GW_DTYPE_F16   0
 #define GW_DTYPE_BF16  1
+/* Output element type of the int8 projections (y_dtype): fp32 as
+ * int8_affine_gemv writes, or f16 as int8_affine_gemv_bias_batched does. */
+#define GW_DTYPE_F32   2
 
 /* Expert activation, mirroring FeedForwardActivation
  * (Sources/Godwit/Model/ArchitectureSpec.swift:15-39). */
@@ -215,7 +223,27 @@ GW_API gw_status gw_mxfp4_gemv(gw_ctx* ctx, const uint8_t* packed, const uint8_t
 GW_API gw_status gw_mxfp4_dequant(gw_ctx* ctx, const uint8_t* packed, const uint8_t* scales,
                            int32_t rows, int32_t cols, float* w_out);
 
+/* int8 affine projection on host arrays (Install/Int8Affine.swift format):
+ * codes [rows][cols] uint8, meta [rows][cols/64][2] bf16 (scale, zero) pairs
+ * — the two regions of an installed trunk tensor, codes first
+ * (InstallLayout.swift:151-157) — bias [rows] bf16 or NULL, x [T][cols] f16;
+ * y [T][rows] = sum over groups of scale*(codes.x) + zero*sum(x), + bias,
+ * written as fp32 (y_dtype GW_DTYPE_F32, the head's int8_affine_gemv,
+ * router.metal:65-98) or rounded to f16 (GW_DTYPE_F16,
+ * int8_affine_gemv_bias_batched, router.metal:107-141).  cols % 64 == 0,
+ * cols <= 16384. */
+GW_API gw_status gw_int8_affine_gemv(gw_ctx* ctx, const uint8_t* codes, const uint16_t* meta,
+                                     const uint16_t* bias_or_null, const uint16_t* x_f16, int32_t T,
+                                     int32_t rows, int32_t cols, void* y, int32_t y_dtype);
+
 /* ---- stream-ordered device-pointer API ---------------------------------- */
+
+/* gw_int8_affine_gemv on device memory, ordered on the context's stream.
+ * codes_dev and x_dev must be 16-byte aligned, meta_dev 4-byte aligned. */
+GW_API gw_status gw_int8_affine_gemv_async(gw_ctx* ctx, const uint8_t* codes_dev,
+                                           const uint16_t* meta_dev, const uint16_t* bias_dev_or_null,
+                                           const uint16_t* x_dev, int32_t T, int32_t rows,
+                                           int32_t cols, void* y_dev, int32_t y_dtype);
 
 /* Batched GEMV over `count` independent matrices (device pointers, strides
  * in elements of each array's type).  x_stride may be 0 to share one x. */

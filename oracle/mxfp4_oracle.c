@@ -418,3 +418,125 @@ GWO_API void gwo_dequant64_mt(const uint8_t* packed, const uint8_t* scales, int6
     for (int t = 0; t < started; ++t)
         if (tid[t]) pthread_join(tid[t], NULL);
 }
+
+/* ---- int8 affine trunk projections --------------------------------------
+ * Int8Affine (Sources/Godwit/Install/Int8Affine.swift) quantises the trunk
+ * (output head, attention projections) to one uint8 code per weight with a
+ * bf16 (scale, zero) pair per group of 64 columns: codes [rows][cols], then
+ * the pairs [rows][cols/64][2] (Install/Installer.swift:315-345,
+ * InstallLayout.swift:151-157).  The GEMVs are router.metal:65-141. */
+
+/* BFloat16.fromFloat — Install/Int8Affine.swift:89-96: round to nearest even,
+ * NaN kept a NaN. */
+GWO_API uint16_t gwo_bf16_from_f32(float v) {
+    uint32_t bits;
+    memcpy(&bits, &v, 4);
+    if ((bits & 0x7FFFFFFFu) > 0x7F800000u) return (uint16_t)((bits >> 16) | 0x0040u);
+    const uint32_t rounding = ((bits >> 16) & 1u) + 0x7FFFu;
+    return (uint16_t)((bits + rounding) >> 16);
+}
+
+/* Int8Affine.quantize(row:) — Install/Int8Affine.swift:31-58.  Per group of
+ * 64: low/high by a sequential scan, scale = max((high-low)/255,
+ * FLT_MIN), zero = low, code = clamp(round((v-low)/scale), 0, 255) with
+ * Swift's .rounded() (half away from zero: roundf).  Returns 0, or -1 when n
+ * is not a multiple of 64 (the reference's precondition). */
+GWO_API int gwo_int8_quantize_row(const float* row, int64_t n, uint8_t* codes, float* scale,
+                                  float* zero) {
+    if (n % 64) return -1;
+    for (int64_t g = 0; g < n / 64; ++g) {
+        const float* v = row + g * 64;
+        float low = v[0], high = v[0];
+        for (int i = 1; i < 64; ++i) {
+            low = fminf(low, v[i]);
+            high = fmaxf(high, v[i]);
+        }
+        float s = (high - low) / 255.0f;
+        if (!(s >= 1.17549435e-38f)) s = 1.17549435e-38f;  /* max(_, .leastNormalMagnitude) */
+        scale[g] = s;
+        zero[g] = low;
+        for (int i = 0; i < 64; ++i) {
+            float level = roundf((v[i] - low) / s);
+            level = level < 0.0f ? 0.0f : (level > 255.0f ? 255.0f : level);
+            codes[g * 64 + i] = (uint8_t)level;
+        }
+    }
+    return 0;
+}
+
+/* Int8Affine.dequantize — Install/Int8Affine.swift:61-73, with the bf16 pair
+ * layout the device reads (ModelRunner.embed, Runtime/ModelRunner.swift:131-157):
+ * w = code * scale + zero in fp32. */
+GWO_API void gwo_int8_dequant(const uint8_t* codes, const uint16_t* meta, int64_t rows,
+                              int64_t cols, float* out) {
+    const int64_t ng = cols / 64;
+    for (int64_t r = 0; r < rows; ++r)
+        for (int64_t g = 0; g < ng; ++g) {
+            const float s = bf16_to_f32(meta[(r * ng + g) * 2]);
+            const float z = bf16_to_f32(meta[(r * ng + g) * 2 + 1]);
+            for (int i = 0; i < 64; ++i) {
+                const int64_t c = r * cols + g * 64 + i;
+                out[c] = (float)codes[c] * s + z;
+            }
+        }
+}
+
+/* int8_affine_gemv / int8_affine_gemv_bias_batched — Metal/MoE/router.metal:65-141:
+ * per row and group, dot = sum q*x and xsum = sum x in fp32 over the 64
+ * columns, acc += scale*dot + zero*xsum; y = acc (+ bias).  The Metal
+ * kernel spreads the groups over 32 lanes and sums the lanes at the end;
+ * this restatement walks the groups in order.  x holds the f16 values
+ * [T][cols]; y [T][rows] fp32 (the batched kernel's f16 rounding is the
+ * caller's).  Rows split over `threads` POSIX threads. */
+typedef struct {
+    const uint8_t* codes; const uint16_t* meta; const uint16_t* bias; const float* x;
+    int64_t T, rows, cols, r0, r1; float* y;
+} i8_job;
+
+static void* i8_worker(void* p) {
+    const i8_job* j = (const i8_job*)p;
+    const int64_t ng = j->cols / 64;
+    for (int64_t r = j->r0; r < j->r1; ++r) {
+        const uint8_t* w = j->codes + r * j->cols;
+        const uint16_t* m = j->meta + r * ng * 2;
+        for (int64_t t = 0; t < j->T; ++t) {
+            const float* xt = j->x + t * j->cols;
+            float acc = 0.0f;
+            for (int64_t g = 0; g < ng; ++g) {
+                const float scale = bf16_to_f32(m[g * 2]), zero = bf16_to_f32(m[g * 2 + 1]);
+                float dot = 0.0f, xsum = 0.0f;
+                for (int i = 0; i < 64; ++i) {
+                    const float xi = xt[g * 64 + i];
+                    dot += (float)w[g * 64 + i] * xi;
+                    xsum += xi;
+                }
+                acc += scale * dot + zero * xsum;
+            }
+            j->y[t * j->rows + r] = acc + (j->bias ? bf16_to_f32(j->bias[r]) : 0.0f);
+        }
+    }
+    return NULL;
+}
+
+GWO_API void gwo_int8_gemv_mt(const uint8_t* codes, const uint16_t* meta, const uint16_t* bias,
+                              const float* x, int64_t T, int64_t rows, int64_t cols, float* y,
+                              int threads) {
+    if (threads < 1) threads = 1;
+    if (threads > 256) threads = 256;
+    pthread_t tid[256];
+    i8_job jobs[256];
+    const int64_t per = (rows + threads - 1) / threads;
+    int started = 0;
+    for (int t = 0; t < threads; ++t) {
+        const int64_t r0 = t * per, r1 = (t + 1) * per < rows ? (t + 1) * per : rows;
+        if (r0 >= r1) break;
+        jobs[t] = (i8_job){codes, meta, bias, x, T, rows, cols, r0, r1, y};
+        if (threads == 1 || pthread_create(&tid[t], NULL, i8_worker, &jobs[t]) != 0) {
+            i8_worker(&jobs[t]);
+            tid[t] = 0;
+        }
+        started = t + 1;
+    }
+    for (int t = 0; t < started; ++t)
+        if (tid[t]) pthread_join(tid[t], NULL);
+}

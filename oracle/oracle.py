@@ -55,6 +55,12 @@ def lib() -> C.CDLL:
         L.gwo_moe_layer_mt.argtypes = [P, I64, P, I64, I64, I64, C.c_int, C.c_int, F, F, P, P,
                                        P, I64, P, P, P, C.c_int]
         L.gwo_dequant64_mt.argtypes = [P, P, I64, I64, P, C.c_int]
+        L.gwo_bf16_from_f32.restype = C.c_uint16
+        L.gwo_bf16_from_f32.argtypes = [F]
+        L.gwo_int8_quantize_row.restype = C.c_int
+        L.gwo_int8_quantize_row.argtypes = [P, I64, P, P, P]
+        L.gwo_int8_dequant.argtypes = [P, P, I64, I64, P]
+        L.gwo_int8_gemv_mt.argtypes = [P, P, P, P, I64, I64, I64, P, C.c_int]
         _lib = L
     return _lib
 
@@ -366,6 +372,77 @@ def moe_block64(spec, strides: np.ndarray, stream: np.ndarray, normed: np.ndarra
     normed f16 input and the routing: stream + moe_layer64(normed)."""
     return np.asarray(stream, dtype=np.float64) + moe_layer64(spec, strides, normed.astype(np.float64),
                                                               experts, weights)
+
+
+# ---- int8 affine trunk projections (Install/Int8Affine.swift, router.metal:65-141)
+
+def bf16_from_f32(v: float) -> int:
+    """BFloat16.fromFloat (Int8Affine.swift:89-96)."""
+    return int(lib().gwo_bf16_from_f32(float(v)))
+
+
+def int8_quantize_row(row):
+    """Int8Affine.quantize(row:) -> (codes uint8 [n], scale fp32 [n/64], zero fp32 [n/64])."""
+    row = _f32(row)
+    n = row.size
+    codes = np.empty(n, np.uint8)
+    scale = np.empty(n // 64, np.float32)
+    zero = np.empty(n // 64, np.float32)
+    if lib().gwo_int8_quantize_row(_p(row), n, _p(codes), _p(scale), _p(zero)) != 0:
+        raise ValueError(f"row width {n} is not a multiple of 64")
+    return codes, scale, zero
+
+
+def int8_quantize(w):
+    """A [rows, cols] fp32 matrix -> (codes uint8 [rows, cols], meta uint16 bf16 bits
+    [rows, cols/64, 2]) in the installer's trunk layout (Installer.swift:315-345)."""
+    w = _f32(w)
+    rows, cols = w.shape
+    codes = np.empty((rows, cols), np.uint8)
+    meta = np.empty((rows, cols // 64, 2), np.uint16)
+    for r in range(rows):
+        c, s, z = int8_quantize_row(w[r])
+        codes[r] = c
+        meta[r, :, 0] = [bf16_from_f32(v) for v in s]
+        meta[r, :, 1] = [bf16_from_f32(v) for v in z]
+    return codes, meta
+
+
+def int8_dequant(codes, meta) -> np.ndarray:
+    codes = np.ascontiguousarray(codes, np.uint8)
+    meta = np.ascontiguousarray(meta, np.uint16)
+    rows, cols = codes.shape
+    out = np.empty((rows, cols), np.float32)
+    lib().gwo_int8_dequant(_p(codes), _p(meta), rows, cols, _p(out))
+    return out
+
+
+def int8_gemv(codes, meta, x, bias=None, threads: int = 1) -> np.ndarray:
+    """fp32 restatement of int8_affine_gemv(_bias_batched): x [T, cols] (f16
+    values) -> [T, rows] fp32 (before the batched kernel's f16 rounding)."""
+    codes = np.ascontiguousarray(codes, np.uint8)
+    meta = np.ascontiguousarray(meta, np.uint16)
+    rows, cols = codes.shape
+    x = _f32(np.atleast_2d(x))
+    T = x.shape[0]
+    b = None if bias is None else np.ascontiguousarray(bias, np.uint16)
+    y = np.empty((T, rows), np.float32)
+    lib().gwo_int8_gemv_mt(_p(codes), _p(meta), _p(b), _p(x), T, rows, cols, _p(y), threads)
+    return y
+
+
+def int8_gemv64(codes, meta, x, bias=None) -> np.ndarray:
+    """fp64 restatement of the same projection: (code*scale + zero) . x + bias."""
+    codes = np.asarray(codes, np.uint8)
+    rows, cols = codes.shape
+    m = np.asarray(meta, np.uint16).reshape(rows, cols // 64, 2).astype(np.uint32) << 16
+    sc = m[..., 0].view(np.float32).astype(np.float64)
+    zr = m[..., 1].view(np.float32).astype(np.float64)
+    w = codes.reshape(rows, cols // 64, 64).astype(np.float64) * sc[..., None] + zr[..., None]
+    y = np.atleast_2d(np.asarray(x, np.float64)) @ w.reshape(rows, cols).T
+    if bias is not None:
+        y = y + (np.asarray(bias, np.uint16).astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    return y
 
 
 def rel_l2(a, b) -> float:

@@ -50,6 +50,7 @@ def test_one_rank_layer_matches_moe_forward(ctx):
         D.bind_stream(ctx, torch.cuda.current_stream())
         x = torch.from_numpy(hidden().view(np.int16)).cuda().view(torch.bfloat16)
         ep = AllToAllEP(CudaOps(ctx, bank), SPEC.layers, SPEC.top_k)
+        ep.set_capacity(T)  # forward() does this from the ranks' token counts
         got = ep.layer_partial(0, x)
         ref = torch.empty((T, SPEC.hidden), dtype=torch.float32, device="cuda")
         ex = torch.empty((T, SPEC.top_k), dtype=torch.int32, device="cuda")

@@ -197,3 +197,65 @@ def test_qwen3_layout():
         [1_572_864, 98_304, 786_432, 49_152, 3_072, 4_096]
     assert lay.stride == 2_539_520
     assert QWEN3_30B_A3B.expert_weight_bytes == 2_506_752
+
+
+# ---- Int8Affine (Tests/GodwitTests/InstallLayoutTests.swift:82-125) --------
+
+def test_int8_round_trip_within_half_a_step():  # InstallLayoutTests.swift:85-98
+    rng = np.random.default_rng(5)
+    row = rng.uniform(-2, 2, 256).astype(np.float32)
+    codes, scale, zero = O.int8_quantize_row(row)
+    back = codes.reshape(-1, 64).astype(np.float32) * scale[:, None] + zero[:, None]
+    step = np.repeat(scale, 64)
+    assert np.all(np.abs(back.ravel() - row) <= step * 0.51)
+
+
+def test_int8_extremes_exact():  # InstallLayoutTests.swift:100-112
+    row = np.zeros(64, np.float32)
+    row[0], row[63] = -3, 5
+    codes, scale, zero = O.int8_quantize_row(row)
+    back = codes.astype(np.float32) * scale[0] + zero[0]
+    assert abs(back[0] + 3) < 1e-4 and abs(back[63] - 5) < 1e-3
+    assert codes[0] == 0 and codes[63] == 255
+
+
+def test_int8_constant_group_has_positive_scale():  # InstallLayoutTests.swift:114-121
+    row = np.full(64, 1.25, np.float32)
+    codes, scale, zero = O.int8_quantize_row(row)
+    assert scale[0] > 0
+    assert np.all(np.abs(np.zeros(64) * scale[0] + zero[0] - 1.25) < 1e-5)
+
+
+@pytest.mark.parametrize("v", [0.0, 1.0, -1.0, 0.5, 2.0, -0.25, 1024.0])
+def test_bf16_round_trips_representable_values(v):  # InstallLayoutTests.swift:123-127
+    bits = O.bf16_from_f32(v)
+    assert np.array([bits << 16], np.uint32).view(np.float32)[0] == v
+
+
+def test_bf16_rounds_to_nearest_even_and_keeps_nan():  # Int8Affine.swift:89-96
+    assert O.bf16_from_f32(float(np.array([0x3F808000], np.uint32).view(np.float32)[0])) == 0x3F80  # tie -> even
+    assert O.bf16_from_f32(float(np.array([0x3F818000], np.uint32).view(np.float32)[0])) == 0x3F82  # tie -> even
+    assert O.bf16_from_f32(float(np.array([0x3F808001], np.uint32).view(np.float32)[0])) == 0x3F81
+    nan = O.bf16_from_f32(float("nan"))
+    assert (nan & 0x7F80) == 0x7F80 and (nan & 0x7F) != 0
+
+
+def test_int8_quantize_rejects_ragged_rows():  # Int8Affine.swift:32-33 precondition
+    with pytest.raises(ValueError):
+        O.int8_quantize_row(np.zeros(100, np.float32))
+
+
+def test_int8_gemv_restatements_agree():
+    """The fp32 restatement of router.metal:65-141 against the fp64 one, and
+    both against dequantise-then-multiply."""
+    rng = np.random.default_rng(9)
+    w = rng.normal(0, 0.02, (48, 320)).astype(np.float32)
+    codes, meta = O.int8_quantize(w)
+    x = rng.standard_normal((3, 320)).astype(np.float16).astype(np.float32)
+    bias = np.array([O.bf16_from_f32(v) for v in rng.normal(0, 0.02, 48)], np.uint16)
+    y32 = O.int8_gemv(codes, meta, x, bias, threads=2)
+    y64 = O.int8_gemv64(codes, meta, x, bias)
+    assert O.rel_l2(y32, y64) < 1e-6
+    dq = O.int8_dequant(codes, meta).astype(np.float64)
+    b = (bias.astype(np.uint32) << 16).view(np.float32)
+    assert O.rel_l2(x.astype(np.float64) @ dq.T + b, y64) < 1e-6
