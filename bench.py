@@ -425,21 +425,52 @@ def run_decode(args):
     else:
         ep = ReplicatedTokensEP(CudaOps(ctx, bank), spec.layers)
 
-    def step():
+    def step_eager():
         if world == 1:
             D.moe_stack(ctx, bank, x, stream_buf)
         else:
             if sliced:
-                ep.forward(x, stream_buf, x_work)
+                ep.forward(x, stream_buf, x_work, check=False)
             else:
                 ep.forward(x, stream_buf, partial, x_work)
+
+    for _ in range(args.warmup):
+        step_eager()
+    torch.cuda.synchronize()
+    # library kernels one step launches (counted on an eager step: a replayed
+    # graph does not pass through the library's launch counter)
+    l0 = ctx.launch_count()
+    step_eager()
+    torch.cuda.synchronize()
+    launches_per_step = ctx.launch_count() - l0
+    # At N > 1 one step (the library's kernels, the exchange's torch ops and
+    # the NCCL collectives of all layers) is captured once as a CUDA graph and
+    # replayed; one GPU's stack forward already replays its own graph.
+    graph, graph_note = None, None
+    if world > 1:
+        try:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cur):
+                step_eager()
+            graph = g
+            graph.replay()
+            torch.cuda.synchronize()
+        except Exception as e:  # keep measuring, eagerly, and say why
+            graph, graph_note = None, f"graph capture failed, eager steps: {type(e).__name__}: {e}"[:300]
+            torch.cuda.synchronize()
+
+    def step():
+        if graph is not None:
+            graph.replay()
+        else:
+            step_eager()
 
     def step_e2e():
         x.copy_(x_host, non_blocking=True)
         step()
         out_host.copy_(stream_buf, non_blocking=True)
 
-    for _ in range(args.warmup):
+    for _ in range(2):
         step()
     torch.cuda.synchronize()
 
@@ -456,7 +487,7 @@ def run_decode(args):
     ev1.record(cur)
     torch.cuda.synchronize()
     _barrier(world)
-    launches = ctx.launch_count() - launches0
+    launches = ctx.launch_count() - launches0 if graph is None else launches_per_step * args.steps
     ms = _max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
 
     # ---- e2e through the public API with host buffers ----
@@ -473,10 +504,12 @@ def run_decode(args):
     e2e_ms = _max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
 
     # ---- kernel timing of the dominant kernels (expert GEMVs) ----
+    if sliced:
+        ep.raise_if_overflowed()
     ctx.profile_enable(True)
     prof_steps = min(args.steps, 3)
     for _ in range(prof_steps):
-        step()
+        step_eager()
     prof = ctx.profile_read()
     ctx.profile_enable(False)
     expert_ms = prof["gateup_ms"] + prof["down_ms"]
@@ -539,6 +572,8 @@ def run_decode(args):
                                        if world > 1 else "single"),
                        "l2": "weights streamed per step >> 126 MB L2 (no flush needed)",
                        "bank_fill_s": round(fill_s, 2), "bank_bytes": bank.nbytes(),
+                       **({"cuda_graph": graph is not None} if world > 1 else {}),
+                       **({"graph_note": graph_note} if graph_note else {}),
                        **({"skew": skew} if skew else {})},
             "e2e": {"value": T / (e2e_ms / 1e3), "unit": unit, "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": Tr * H * 2, "d2h_bytes_per_step": Tr * H * 4},

@@ -11,8 +11,12 @@
 // f16, down projection times the routing weight — for all of an expert's
 // tokens from one pass over its weights.
 //
+// Two kernels share the work list and the epilogue: k_grouped (exact f16
+// operands, described here) and k_grouped_mx (block-scaled MXFP4 x MXFP8,
+// described above its roles further down).
+//
 // One persistent CTA per SM walks a static list of work items (128-row tile,
-// expert, token chunk of <= 128).  Warp roles:
+// expert, token chunk of <= 128).  Warp roles of k_grouped:
 //   warp 12     weight producer: bulk-copies (cp.async.bulk) each 8-block
 //               group of the tile — in the bank's tiled layout a contiguous
 //               16 x w x 16-byte run per 16-row tile, plus its scale bytes —
@@ -73,27 +77,11 @@ constexpr int kGroupPk = 8 * kTileRun;    // 16 KB of MXFP4 blocks per group
 constexpr int kGroupSc = 8 * 16 * 8;      // 1 KB of scale bytes per group
 constexpr int kRingBytes = kStages * kBSlot;
 constexpr int kGroupOff = kRingBytes;
-// Block-scaled scale words staged for tcgen05.cp, per stage: the tokens' as
-// 32 rows x 16 bytes (row r = tokens r, 32 + r, 64 + r, 96 + r), the weight
-// rows' as 128 rows x 16 bytes (the row's word four times).
-constexpr int kTsfOff = kGroupOff + kGroups * (kGroupPk + kGroupSc);
-constexpr int kTsfSlot = kNMax * 4;
-constexpr int kSfaOff = kTsfOff + kStages * kTsfSlot;
-constexpr int kSfaSlot = kM * 16;
-constexpr int kDynSmem = kSfaOff + kStages * kSfaSlot + 1024;         // + alignment slack
+constexpr int kDynSmem = kGroupOff + kGroups * (kGroupPk + kGroupSc) + 1024;  // + alignment slack
 constexpr int kThreads = 15 * 32;
 constexpr int kTmemCols = 512;            // accumulators 2 x kNMax, then the weight ring
 constexpr int kAColBase = 2 * kNMax;
 static_assert(kAColBase + kStages * kACols <= kTmemCols, "TMEM budget");
-// Block-scaled mode: per stage 128 x 128 e2m1 weights in shared memory (the
-// MMA's unpacked form: 16 values in 8 bytes, then 8 bytes of padding, so a
-// row of 128 values is 128 bytes) and 128 x 128 E4M3 token codes; scale words
-// (four E8M0 bytes = the stage's four blocks) in TMEM after the accumulators.
-constexpr int kMxASlot = kM * 128;        // 16 KB
-constexpr int kMxBSlot = kNMax * 128;     // 16 KB
-constexpr int kMxSfa = 2 * kNMax;         // TMEM columns: weight scales, 4 per stage
-constexpr int kMxSfb = kMxSfa + 4 * kStages;  // token scales, 4 per stage (tokens 32j..32j+31)
-static_assert(kStages * (kMxASlot + kMxBSlot) <= kRingBytes, "block-scaled ring fits the f16 ring");
 
 // Warp roles.
 constexpr int kConvWarps = 8, kEpiWarp0 = 8, kWeightWarp = 12, kTokenWarp = 13, kMmaWarp = 14;
@@ -469,171 +457,8 @@ __device__ __forceinline__ void role_mma(Shared& sh, const GroupedArgs& a, char*
 
 // ---- block-scaled roles (gw_set_block_scaled) ------------------------------
 
-// Unpackers (warps 0-7, in place of the converters): thread c owns weight row
-// r = m0 + (c & 127) and blocks 2h, 2h + 1 of each stage (h = c >> 7).  It
-// copies them from the group ring into the MMA's unpacked e2m1 layout (each
-// 16-value half block = 8 bytes of codes + 8 bytes of zeros, canonical
-// K-major core matrices of 8 rows x 16 bytes); the h = 0 threads stage the
-// row's four block scales (one word) in the stage's scale slot, which the MMA
-// thread copies into TMEM (lane r, column sfa + r / 32) with tcgen05.cp.
-__device__ __forceinline__ void role_unpack(Shared& sh, const GroupedArgs& a, char* smem) {
-    const int c = threadIdx.x;
-    const int r = c & (kM - 1), h = c >> 7, lane = c & 31;
-    const int lr = r & 15, tile = r >> 4;
-    const int nblk = a.K >> 5, ngrp = (nblk + 7) >> 3;
-    unsigned* status = a.w.status;
-    const char* ring = smem + kGroupOff;
-    int g = 0, gq = 0;
-    bool ok = true;
-    for (int it = blockIdx.x; ok && it < sh.nitems; it += gridDim.x) {
-        const Item item = decode(sh, it);
-        const bool valid = item.m0 + r < a.M;
-        for (int grp = 0; ok && grp < ngrp; ++grp, ++gq) {
-            const int w = min(8, nblk - 8 * grp);
-            const int gslot = gq % kGroups;
-            if (!warp_wait(&sh.abort, &sh.gfull[gslot], (gq / kGroups) & 1, status, 2u)) { ok = false; break; }
-            const char* gb = ring + gslot * (kGroupPk + kGroupSc);
-            for (int sub = 0; sub * 4 < w; ++sub, ++g) {
-                const int kb = min(4, w - 4 * sub);
-                const bool mine = 2 * h < kb;
-                const int bl = 4 * sub + 2 * h;
-                uint4 q[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-                uint32_t sfw = 0;
-                if (valid && mine) {
-                    const uint4* src = reinterpret_cast<const uint4*>(gb + tile * kTileRun + (lr * w + bl) * 16);
-                    q[0] = src[0];
-                    q[1] = src[1];
-                }
-                if (valid && h == 0) {  // the row's scale bytes of the stage's blocks
-                    const uint8_t* sb = reinterpret_cast<const uint8_t*>(gb + kGroupPk + tile * 128 + lr * w + 4 * sub);
-                    for (int b = 0; b < kb; ++b) sfw |= (uint32_t)sb[b] << (8 * b);
-                }
-                if (4 * sub + 4 >= w) {  // the group's last stage has been read: free its slot
-                    __syncwarp();
-                    if (lane == 0) bar_arrive(&sh.gempty[gslot]);
-                }
-                const int slot = g % kStages;
-                if (!warp_wait(&sh.abort, &sh.empty[slot], ((g / kStages) & 1) ^ 1, status, 4u)) { ok = false; break; }
-                if (valid && mine) {
-                    char* A = smem + slot * (kMxASlot + kMxBSlot) + (r >> 3) * 1024 + (r & 7) * 16;
-#pragma unroll
-                    for (int b2 = 0; b2 < 2; ++b2) {
-                        const int kc = 2 * (2 * h + b2);  // 16-value chunk index in the 128-value stage
-                        *reinterpret_cast<uint4*>(A + kc * 128) = make_uint4(q[b2].x, q[b2].y, 0u, 0u);
-                        *reinterpret_cast<uint4*>(A + (kc + 1) * 128) = make_uint4(q[b2].z, q[b2].w, 0u, 0u);
-                    }
-                    fence_async_smem();
-                }
-                if (h == 0) {
-                    *reinterpret_cast<uint4*>(smem + kSfaOff + slot * kSfaSlot + r * 16) = make_uint4(sfw, sfw, sfw, sfw);
-                    fence_async_smem();
-                }
-                __syncwarp();
-                if (lane == 0) bar_arrive(&sh.full[slot]);
-            }
-        }
-    }
-}
 
-// Token producer of the block-scaled mode: one TMA (128 rows x 128 E4M3
-// codes, 128B swizzle) per stage, and the stage's token scale words (one per
-// token) into the stage's shared slot for the MMA thread's tcgen05.cp; its
-// one arrival on the stage's full barrier carries the TMA's byte count.
-__device__ __forceinline__ void role_tokens_mx(Shared& sh, const GroupedArgs& a, char* smem,
-                                               const CUtensorMap* map) {
-    const int nblk = a.K >> 5, ngrp = (nblk + 7) >> 3, nst = (a.K + 127) >> 7;
-    const int lane = threadIdx.x & 31;
-    unsigned* status = a.w.status;
-    int g = 0;
-    for (int it = blockIdx.x; it < sh.nitems; it += gridDim.x) {
-        const Item item = decode(sh, it);
-        for (int grp = 0; grp < ngrp; ++grp) {
-            const int w = min(8, nblk - 8 * grp);
-            for (int sub = 0; sub * 4 < w; ++sub, ++g) {
-                const int slot = g % kStages;
-                // token scale words of this stage (loaded before the slot wait: they
-                // only depend on the item)
-                uint32_t tw[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    tw[j] = 32 * j + lane < item.n
-                                ? __ldg(a.bsf + (int64_t)(item.g0 + 32 * j + lane) * nst + 2 * grp + sub)
-                                : 0u;
-                if (!warp_wait(&sh.abort, &sh.empty[slot], ((g / kStages) & 1) ^ 1, status, 8u)) return;
-                *reinterpret_cast<uint4*>(smem + kTsfOff + slot * kTsfSlot + lane * 16) =
-                    make_uint4(tw[0], tw[1], tw[2], tw[3]);
-                fence_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-                    char* B = smem + slot * (kMxASlot + kMxBSlot) + kMxASlot;
-                    bar_arrive_tx(&sh.full[slot], kMxBSlot);
-                    tma_2d(B, map, (8 * grp + 4 * sub) * 32, item.g0, &sh.full[slot]);
-                }
-                __syncwarp();
-            }
-        }
-    }
-}
 
-// MMA issuer of the block-scaled mode: kb MMAs of K = 32 per stage, scale
-// bytes k of the stage's words.
-__device__ __forceinline__ void role_mma_mx(Shared& sh, const GroupedArgs& a, char* smem) {
-    const int nblk = a.K >> 5, ngrp = (nblk + 7) >> 3;
-    const int lane = threadIdx.x & 31;
-    unsigned* status = a.w.status;
-    const uint32_t base = saddr(smem);
-    int g = 0, il = 0;
-    bool ok = true;
-    for (int it = blockIdx.x; ok && it < sh.nitems; it += gridDim.x, ++il) {
-        const Item item = decode(sh, it);
-        const int n = max(16, (item.n + 15) & ~15);
-        // a E2M1 (5), b E4M3 (0), E8M0 scales, N, M = 128, K = 32
-        const uint32_t idesc0 = (5u << 7) | (0u << 10) | (1u << 23) | ((uint32_t)(n >> 3) << 17) |
-                                ((uint32_t)(kM >> 4) << 24);
-        const int b = il & 1;
-        if (!warp_wait(&sh.abort, &sh.tempty[b], ((il >> 1) & 1) ^ 1, status, 16u)) break;
-        tc_after_sync();
-        const uint32_t dtm = sh.tmem + b * kNMax;
-        bool first = true;
-        for (int grp = 0; ok && grp < ngrp; ++grp) {
-            const int w = min(8, nblk - 8 * grp);
-            for (int sub = 0; sub * 4 < w; ++sub, ++g) {
-                const int kb = min(4, w - 4 * sub);
-                const int slot = g % kStages;
-                if (!warp_wait(&sh.abort, &sh.full[slot], (g / kStages) & 1, status, 32u)) { ok = false; break; }
-                tc_after_sync();
-                if (lane == 0) {
-                    const uint32_t A = base + slot * (kMxASlot + kMxBSlot), B = A + kMxASlot;
-                    const uint32_t sfa = sh.tmem + kMxSfa + slot * 4, sfb = sh.tmem + kMxSfb + slot * 4;
-                    tc_cp_128x128b(sfa, smem_desc(base + kSfaOff + slot * kSfaSlot, 128, 128, 0));
-                    tc_cp_32x128b_x4(sfb, smem_desc(base + kTsfOff + slot * kTsfSlot, 128, 128, 0));
-                    for (int k = 0; k < kb; ++k) {
-                        const uint32_t idesc = idesc0 | ((uint32_t)k << 29) | ((uint32_t)k << 4);
-                        tc_mma_mx(dtm, smem_desc(A + k * 256, 128, 1024, 0), smem_desc(B + k * 32, 16, 1024, 2),
-                                  idesc, first ? 0u : 1u, sfa, sfb);
-                        first = false;
-                    }
-                    tc_commit(&sh.empty[slot]);
-                }
-                __syncwarp();
-            }
-        }
-        if (!ok) break;
-        if (lane == 0) tc_commit(&sh.tfull[b]);
-        __syncwarp();
-    }
-    if (lane == 0) {
-        tc_commit(&sh.fin);
-        const long long t0 = clock64();
-        while (!bar_try(&sh.fin, 0)) {
-            if (clock64() - t0 > kWaitCycles) {
-                if (status) atomicOr(status, 64u);
-                break;
-            }
-        }
-    }
-    __syncwarp();
-}
 
 // Epilogue: thread t (0..127) owns TMEM lane t = tile row m0 + t.
 template <int kMode, bool kMX>
@@ -695,15 +520,11 @@ __device__ __forceinline__ void role_epilogue(Shared& sh, const GroupedArgs& a) 
     }
 }
 
-template <int kMode, bool kMX>
-__global__ void __launch_bounds__(kThreads, 1) k_grouped(const __grid_constant__ CUtensorMap bmap,
-                                                         GroupedArgs a) {
-    extern __shared__ unsigned char dyn_raw[];
-    __shared__ Shared sh;
-    char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(dyn_raw) + 1023) & ~uintptr_t(1023));
+// Work list of a launch (every CTA computes the same): the active experts,
+// their token-chunk prefix, and the expert-ordered row offsets.
+__device__ __forceinline__ void plan_items(Shared& sh, const GroupedArgs& a) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int mt = (a.M + kM - 1) / kM;
-
     // active experts and their token chunks
     const int nact = min(*a.w.nactive, a.d.E);
     for (int i = tid; i < nact; i += blockDim.x) {
@@ -716,11 +537,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_grouped(const __grid_constant__
     if (tid == 0) {
         sh.abort = 0;
         sh.nact = nact;
-        for (int i = 0; i < kStages; ++i) { bar_init(&sh.full[i], kConvWarps + 1); bar_init(&sh.empty[i], 1); }
-        for (int i = 0; i < kGroups; ++i) { bar_init(&sh.gfull[i], 1); bar_init(&sh.gempty[i], kConvWarps); }
-        for (int i = 0; i < 2; ++i) { bar_init(&sh.tfull[i], 1); bar_init(&sh.tempty[i], 128); }
-        bar_init(&sh.fin, 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
     if (warp == 0) {  // exclusive prefix over <= 256 chunk counts, 8 per lane
@@ -770,6 +586,227 @@ __global__ void __launch_bounds__(kThreads, 1) k_grouped(const __grid_constant__
     __syncthreads();
     for (int i = tid; i < nact; i += blockDim.x) sh.goff[i] = sh.epre[sh.expert[i]];
     __syncthreads();
+}
+
+// ---- block-scaled mode: weights by TMA straight into the MMA's layout -------
+//
+// k_grouped_mx: the block-scaled grouped GEMM with one stage per 8-block group
+// (K = 256, eight MMAs) and no conversion role.  Per stage:
+//   warp 12 (lane 0)  weights: two TMA boxes of the bank's tiled layout viewed
+//                     as 4-bit elements (CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B),
+//                     128 rows x 128 values each, which the copy unpacks into
+//                     the MMA's e2m1 layout (16 values in 8 bytes + 8 bytes of
+//                     padding) with the 128-byte swizzle; tokens: two boxes of
+//                     128 E4M3 codes x 128 rows; one transaction count.
+//   warp 13           scale words: the tile rows' E8M0 bytes of the group and
+//                     the tokens' words, staged for tcgen05.cp.
+//   warp 14 (lane 0)  tcgen05.cp of both scale sets into TMEM, then eight
+//                     kind::mxf8f6f4.block_scale MMAs (M = 128, K = 32) from
+//                     the 128-byte-swizzled operands, one commit.
+//   warps 8-11        epilogue (as the f16 path's).
+// The last group of a row (w < 8 blocks) is a stage of w MMAs from boxes of
+// a 4-D view whose rows are 16 w bytes apart; the box's values beyond the
+// row read as zeros and are not used.
+constexpr int kS2 = 3;                        // stages in flight
+constexpr int kS2A = kM * 256 / 2 * 2;        // 32 KB: 128 rows x 256 unpacked e2m1 (1 byte / value)
+constexpr int kS2B = kNMax * 256;             // 32 KB: 128 tokens x 256 E4M3 codes
+constexpr int kS2Sa = 2 * kM * 16;            // 4 KB: two 128 x 16-byte scale-word slabs
+constexpr int kS2Sb = 2 * 32 * 16;            // 1 KB: two 32 x 16-byte token-word slabs
+constexpr int kS2Slot = kS2A + kS2B + kS2Sa + kS2Sb;
+constexpr int kS2Smem = kS2 * kS2Slot + 1024;
+constexpr int kS2Sfa = 2 * kNMax;             // TMEM columns: weight scale words, 8 per stage
+constexpr int kS2Sfb = kS2Sfa + 8 * kS2;      // token scale words, 8 per stage
+static_assert(kS2Sfb + 8 * kS2 <= kTmemCols, "TMEM budget");
+static_assert(kS2 <= kStages, "barrier arrays");
+
+struct MxMaps {
+    CUtensorMap b;        // token codes [rows][K], box 128 codes x 32 rows, 128-byte swizzle
+    CUtensorMap wfull;    // 16U4 (256 values, 16 rows, full groups, tiles, experts), box (128, 16, 1, 8, 1)
+    CUtensorMap wnarrow;  // 16U4 (32 w values, 16 rows, tiles, experts) at the last group, box (128, 16, 8, 1)
+};
+
+__device__ __forceinline__ void tma_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                       uint64_t* b) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+        "%4, %5}], [%6];" ::"r"(saddr(dst)),
+        "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(saddr(b))
+        : "memory");
+}
+__device__ __forceinline__ void tma_5d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3, int c4,
+                                       uint64_t* b) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+        "%4, %5, %6}], [%7];" ::"r"(saddr(dst)),
+        "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(saddr(b))
+        : "memory");
+}
+
+// Weight and token copies (lane 0 of warp 12).
+__device__ __forceinline__ void role_copies_mx2(Shared& sh, const GroupedArgs& a, char* smem, const MxMaps* maps) {
+    const int nblk = a.K >> 5, ngrp = (nblk + 7) >> 3, nfull = nblk >> 3;
+    unsigned* status = a.w.status;
+    int g = 0;
+    for (int it = blockIdx.x; it < sh.nitems; it += gridDim.x) {
+        const Item item = decode(sh, it);
+        const int le = item.e / a.d.shard_count;
+        const int tile0 = item.m0 >> 4;
+        for (int grp = 0; grp < ngrp; ++grp, ++g) {
+            const int slot = g % kS2;
+            if (!wait_on(&sh.abort, &sh.empty[slot], ((g / kS2) & 1) ^ 1, status, 1u)) return;
+            const int w = min(8, nblk - 8 * grp);
+            const int nbox = (w + 3) >> 2;          // 128-value boxes
+            const int nrow = (item.n + 31) >> 5;    // 32-token boxes: only the chunk's rows
+            char* A = smem + slot * kS2Slot;
+            char* B = A + kS2A;
+            // packed weight bytes (the transaction counts the global bytes,
+            // 64 per row and box) plus the token codes
+            bar_arrive_tx(&sh.full[slot], (uint32_t)nbox * (kM * 64 + nrow * 32 * 128));
+            for (int x = 0; x < nbox; ++x) {
+                if (grp < nfull) tma_5d(A + x * (kS2A / 2), &maps->wfull, 128 * x, 0, grp, tile0, le, &sh.full[slot]);
+                else tma_4d(A + x * (kS2A / 2), &maps->wnarrow, 128 * x, 0, tile0, le, &sh.full[slot]);
+                for (int y = 0; y < nrow; ++y)
+                    tma_2d(B + x * (kS2B / 2) + y * 32 * 128, &maps->b, grp * 256 + 128 * x, item.g0 + 32 * y,
+                           &sh.full[slot]);
+            }
+        }
+    }
+}
+
+// Scale words (warp 13): lane l stages rows 4l .. 4l + 3 of the tile and the
+// tokens l, 32 + l, 64 + l, 96 + l.
+__device__ __forceinline__ void role_scales_mx2(Shared& sh, const GroupedArgs& a, char* smem) {
+    const int nblk = a.K >> 5, ngrp = (nblk + 7) >> 3, nst = (a.K + 127) >> 7;
+    const int lane = threadIdx.x & 31;
+    unsigned* status = a.w.status;
+    int g = 0;
+    for (int it = blockIdx.x; it < sh.nitems; it += gridDim.x) {
+        const Item item = decode(sh, it);
+        const int64_t le = item.e / a.d.shard_count;
+        const uint8_t* sc = a.L.base + le * a.L.stride + a.L.off[a.sec_scales];
+        for (int grp = 0; grp < ngrp; ++grp, ++g) {
+            const int slot = g % kS2;
+            const int w = min(8, nblk - 8 * grp);
+            // the rows' scale bytes: in the tiled layout tile t's group holds
+            // 16 rows x w bytes from t * 16 * nblk + grp * 128
+            uint32_t rw[4][2];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int r = 4 * lane + q, R = item.m0 + r;
+                rw[q][0] = rw[q][1] = 0u;
+                if (R < a.M) {
+                    const uint8_t* p = sc + (int64_t)(R >> 4) * 16 * nblk + grp * 128 + (R & 15) * w;
+                    if (w == 8) {
+                        const uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
+                        rw[q][0] = v.x;
+                        rw[q][1] = v.y;
+                    } else {
+                        for (int b = 0; b < w; ++b) rw[q][b >> 2] |= (uint32_t)__ldg(p + b) << (8 * (b & 3));
+                    }
+                }
+            }
+            uint32_t tw[2][4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const bool in = 32 * j + lane < item.n;
+                const uint32_t* src = a.bsf + (int64_t)(item.g0 + 32 * j + lane) * nst + 2 * grp;
+                tw[0][j] = in ? __ldg(src) : 0u;
+                tw[1][j] = (in && w > 4) ? __ldg(src + 1) : 0u;
+            }
+            if (!warp_wait(&sh.abort, &sh.empty[slot], ((g / kS2) & 1) ^ 1, status, 8u)) return;
+            char* Sa = smem + slot * kS2Slot + kS2A + kS2B;
+            char* Sb = Sa + kS2Sa;
+#pragma unroll
+            for (int s = 0; s < 2; ++s) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    *reinterpret_cast<uint4*>(Sa + s * kM * 16 + (4 * lane + q) * 16) =
+                        make_uint4(rw[q][s], rw[q][s], rw[q][s], rw[q][s]);
+                *reinterpret_cast<uint4*>(Sb + s * 512 + lane * 16) = make_uint4(tw[s][0], tw[s][1], tw[s][2], tw[s][3]);
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) bar_arrive(&sh.full[slot]);
+        }
+    }
+}
+
+// MMA issuer (warp 14): per stage the scale copies, then w MMAs of K = 32;
+// MMA k reads byte k & 3 of scale column (k >> 2) of the stage.
+__device__ __forceinline__ void role_mma_mx2(Shared& sh, const GroupedArgs& a, char* smem) {
+    const int nblk = a.K >> 5, ngrp = (nblk + 7) >> 3;
+    const int lane = threadIdx.x & 31;
+    unsigned* status = a.w.status;
+    const uint32_t base = saddr(smem);
+    int g = 0, il = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; ok && it < sh.nitems; it += gridDim.x, ++il) {
+        const Item item = decode(sh, it);
+        const int n = max(16, (item.n + 15) & ~15);
+        // a E2M1 (5), b E4M3 (0), E8M0 scales, N, M = 128, K = 32
+        const uint32_t idesc0 = (5u << 7) | (0u << 10) | (1u << 23) | ((uint32_t)(n >> 3) << 17) |
+                                ((uint32_t)(kM >> 4) << 24);
+        const int b = il & 1;
+        if (!warp_wait(&sh.abort, &sh.tempty[b], ((il >> 1) & 1) ^ 1, status, 16u)) break;
+        tc_after_sync();
+        const uint32_t dtm = sh.tmem + b * kNMax;
+        bool first = true;
+        for (int grp = 0; grp < ngrp; ++grp, ++g) {
+            const int w = min(8, nblk - 8 * grp);
+            const int slot = g % kS2;
+            if (!warp_wait(&sh.abort, &sh.full[slot], (g / kS2) & 1, status, 32u)) { ok = false; break; }
+            tc_after_sync();
+            if (lane == 0) {
+                const uint32_t A = base + slot * kS2Slot, B = A + kS2A, Sa = B + kS2B, Sb = Sa + kS2Sa;
+                const uint32_t sfa = sh.tmem + kS2Sfa + slot * 8, sfb = sh.tmem + kS2Sfb + slot * 8;
+                for (int s = 0; s * 4 < w; ++s) {
+                    tc_cp_128x128b(sfa + 4 * s, smem_desc(Sa + s * kM * 16, 128, 128, 0));
+                    tc_cp_32x128b_x4(sfb + 4 * s, smem_desc(Sb + s * 512, 128, 128, 0));
+                }
+                for (int k = 0; k < w; ++k) {
+                    const uint32_t idesc = idesc0 | ((uint32_t)(k & 3) << 29) | ((uint32_t)(k & 3) << 4);
+                    const uint32_t off = (k >> 2) * (kS2A / 2) + (k & 3) * 32;
+                    tc_mma_mx(dtm, smem_desc(A + off, 16, 1024, 2), smem_desc(B + off, 16, 1024, 2), idesc,
+                              first ? 0u : 1u, sfa + 4 * (k >> 2), sfb + 4 * (k >> 2));
+                    first = false;
+                }
+                tc_commit(&sh.empty[slot]);
+            }
+            __syncwarp();
+        }
+        if (!ok) break;
+        if (lane == 0) tc_commit(&sh.tfull[b]);
+        __syncwarp();
+    }
+    if (lane == 0) {
+        tc_commit(&sh.fin);
+        const long long t0 = clock64();
+        while (!bar_try(&sh.fin, 0)) {
+            if (clock64() - t0 > kWaitCycles) {
+                if (status) atomicOr(status, 64u);
+                break;
+            }
+        }
+    }
+    __syncwarp();
+}
+
+template <int kMode>
+__global__ void __launch_bounds__(kThreads, 1) k_grouped(const __grid_constant__ CUtensorMap bmap,
+                                                         GroupedArgs a) {
+    extern __shared__ unsigned char dyn_raw[];
+    __shared__ Shared sh;
+    char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(dyn_raw) + 1023) & ~uintptr_t(1023));
+    const int tid = threadIdx.x, warp = tid >> 5;
+
+    if (tid == 0) {
+        for (int i = 0; i < kStages; ++i) { bar_init(&sh.full[i], kConvWarps + 1); bar_init(&sh.empty[i], 1); }
+        for (int i = 0; i < kGroups; ++i) { bar_init(&sh.gfull[i], 1); bar_init(&sh.gempty[i], kConvWarps); }
+        for (int i = 0; i < 2; ++i) { bar_init(&sh.tfull[i], 1); bar_init(&sh.tempty[i], 128); }
+        bar_init(&sh.fin, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    plan_items(sh, a);
     if (sh.nitems <= (int)blockIdx.x) return;  // no work for this CTA (uniform)
     if (warp == kMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&sh.tmem)),
@@ -780,25 +817,64 @@ __global__ void __launch_bounds__(kThreads, 1) k_grouped(const __grid_constant__
     tc_before_sync();
     __syncthreads();
     tc_after_sync();
-    if (kMX) {
-        if (warp < kConvWarps) role_unpack(sh, a, smem);
-        else if (warp < kWeightWarp) role_epilogue<kMode, true>(sh, a);
-        else if (warp == kWeightWarp) role_weights(sh, a, smem);
-        else if (warp == kTokenWarp) role_tokens_mx(sh, a, smem, &bmap);
-        else role_mma_mx(sh, a, smem);
-    } else {
-        if (warp < kConvWarps) role_convert(sh, a, smem);
-        else if (warp < kWeightWarp) role_epilogue<kMode, false>(sh, a);
-        else if (warp == kWeightWarp) role_weights(sh, a, smem);
-        else if (warp == kTokenWarp) role_tokens(sh, a, smem, &bmap);
-        else role_mma(sh, a, smem);
-    }
+    if (warp < kConvWarps) role_convert(sh, a, smem);
+    else if (warp < kWeightWarp) role_epilogue<kMode, false>(sh, a);
+    else if (warp == kWeightWarp) role_weights(sh, a, smem);
+    else if (warp == kTokenWarp) role_tokens(sh, a, smem, &bmap);
+    else role_mma(sh, a, smem);
 
     tc_before_sync();
     __syncthreads();
     tc_after_sync();
     // A CTA that gave up may still have bulk copies landing in its shared
     // memory: give them time (they complete in microseconds) before exiting.
+    if (*(volatile int*)&sh.abort) {
+        const long long t0 = clock64();
+        while (clock64() - t0 < 2000000) {}
+    }
+    if (warp == kMmaWarp)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(sh.tmem), "r"(kTmemCols)
+                     : "memory");
+}
+
+// The block-scaled grouped GEMM (roles above role_copies_mx2).  Warps 0-7
+// have no role in this mode.
+template <int kMode>
+__global__ void __launch_bounds__(kThreads, 1) k_grouped_mx(const __grid_constant__ MxMaps maps, GroupedArgs a) {
+    extern __shared__ unsigned char dyn_raw[];
+    __shared__ Shared sh;
+    char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(dyn_raw) + 1023) & ~uintptr_t(1023));
+    const int tid = threadIdx.x, warp = tid >> 5;
+    if (tid == 0) {
+        // full: the copies' transaction count plus the scale warp's arrival
+        for (int i = 0; i < kS2; ++i) { bar_init(&sh.full[i], 2); bar_init(&sh.empty[i], 1); }
+        for (int i = 0; i < 2; ++i) { bar_init(&sh.tfull[i], 1); bar_init(&sh.tempty[i], 128); }
+        bar_init(&sh.fin, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    plan_items(sh, a);
+    if (sh.nitems <= (int)blockIdx.x) return;  // no work for this CTA (uniform)
+    if (warp == kMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&sh.tmem)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_before_sync();
+    __syncthreads();
+    tc_after_sync();
+    if (warp >= kEpiWarp0 && warp < kWeightWarp) role_epilogue<kMode, true>(sh, a);
+    else if (warp == kWeightWarp) {
+        if ((tid & 31) == 0) role_copies_mx2(sh, a, smem, &maps);
+        __syncwarp();
+    } else if (warp == kTokenWarp) role_scales_mx2(sh, a, smem);
+    else if (warp == kMmaWarp) role_mma_mx2(sh, a, smem);
+
+    tc_before_sync();
+    __syncthreads();
+    tc_after_sync();
+    // A CTA that gave up may still have copies landing in its shared memory:
+    // give them time (they complete in microseconds) before exiting.
     if (*(volatile int*)&sh.abort) {
         const long long t0 = clock64();
         while (clock64() - t0 < 2000000) {}
@@ -939,13 +1015,59 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 
 
 int configure_grouped() {
-    const void* fns[6] = {(const void*)k_grouped<0, false>, (const void*)k_grouped<1, false>,
-                          (const void*)k_grouped<2, false>, (const void*)k_grouped<0, true>,
-                          (const void*)k_grouped<1, true>,  (const void*)k_grouped<2, true>};
+    const void* fns[3] = {(const void*)k_grouped<0>, (const void*)k_grouped<1>, (const void*)k_grouped<2>};
     for (const void* f : fns)
         if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem) != cudaSuccess) return -1;
+    const void* mx[3] = {(const void*)k_grouped_mx<0>, (const void*)k_grouped_mx<1>, (const void*)k_grouped_mx<2>};
+    for (const void* f : mx)
+        if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kS2Smem) != cudaSuccess) return -1;
     return 0;
 }
+
+namespace {
+// The block-scaled kernel's two 4-bit views of one matrix of the layer's bank
+// (tiled layout: 16-row tiles, 8-block groups of 16 rows x 128 bytes, the
+// last group 16 rows x 16 w bytes; experts one stride apart).
+bool encode_weight_maps(MxMaps& m, const LayerView& L, int sec_packed, int M, int K, int e_local) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return false;
+    const int nblk = K / 32, nfull = nblk / 8, ntiles = M / 16;
+    const int w = nblk - 8 * nfull;  // blocks of the last, narrow group (0: none)
+    const uint8_t* pk = L.base + L.off[sec_packed];
+    const cuuint64_t tile_pk = (cuuint64_t)nblk * 256, es = (cuuint64_t)L.stride;
+    const cuuint32_t ones[5] = {1, 1, 1, 1, 1};
+    {
+        const cuuint64_t gd[5] = {256, 16, (cuuint64_t)(nfull > 0 ? nfull : 1), (cuuint64_t)ntiles, (cuuint64_t)e_local};
+        const cuuint64_t gs[4] = {128, 2048, tile_pk, es};
+        const cuuint32_t box[5] = {128, 16, 1, 8, 1};
+        if (enc(&m.wfull, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 5, const_cast<uint8_t*>(pk), gd, gs, box, ones,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+    }
+    {
+        // the last group's rows are 16 w bytes apart; its 128-value box reads
+        // zeros past the row (or, where the driver wants the box inside the
+        // view, the next row's codes), which the stage's w MMAs never use
+        const int wn = w > 0 ? w : 8;
+        const cuuint64_t gs[3] = {(cuuint64_t)(16 * wn), tile_pk, es};
+        const cuuint32_t box[4] = {128, 16, 8, 1};
+        uint8_t* nb = const_cast<uint8_t*>(pk + (w > 0 ? (int64_t)nfull * 2048 : 0));
+        bool ok = false;
+        for (cuuint64_t d0 : {(cuuint64_t)(32 * wn), (cuuint64_t)128}) {
+            const cuuint64_t gd[4] = {d0, 16, (cuuint64_t)ntiles, (cuuint64_t)e_local};
+            if (enc(&m.wnarrow, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 4, nb, gd, gs, box, ones,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
+                ok = true;
+                break;
+            }
+        }
+        if (!ok) return false;
+    }
+    return true;
+}
+}  // namespace
 
 bool grouped_supported(const MoeDims& d, const MoeWork& w) {
     // an even number of 32-column blocks per row (stages of 4 or 2 blocks);
@@ -1008,13 +1130,21 @@ int launch_grouped(const LayerView& L, const MoeDims& d, const MoeWork& w, int w
     }
     const dim3 grid(sms), block(kThreads);
     if (mx) {
-        if (a.mode == 0) k_grouped<0, true><<<grid, block, kDynSmem, s>>>(map, a);
-        else if (a.mode == 1) k_grouped<1, true><<<grid, block, kDynSmem, s>>>(map, a);
-        else k_grouped<2, true><<<grid, block, kDynSmem, s>>>(map, a);
+        MxMaps maps;
+        const cuuint32_t box32[2] = {128, 32};
+        if (enc(&maps.b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(bsrc), gdim, gstride, box32, estride,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return -1;
+        const int e_local = (d.E - d.shard_rank + d.shard_count - 1) / d.shard_count;
+        if (!encode_weight_maps(maps, L, a.sec_packed, a.M, a.K, e_local)) return -1;
+        if (a.mode == 0) k_grouped_mx<0><<<grid, block, kS2Smem, s>>>(maps, a);
+        else if (a.mode == 1) k_grouped_mx<1><<<grid, block, kS2Smem, s>>>(maps, a);
+        else k_grouped_mx<2><<<grid, block, kS2Smem, s>>>(maps, a);
     } else {
-        if (a.mode == 0) k_grouped<0, false><<<grid, block, kDynSmem, s>>>(map, a);
-        else if (a.mode == 1) k_grouped<1, false><<<grid, block, kDynSmem, s>>>(map, a);
-        else k_grouped<2, false><<<grid, block, kDynSmem, s>>>(map, a);
+        if (a.mode == 0) k_grouped<0><<<grid, block, kDynSmem, s>>>(map, a);
+        else if (a.mode == 1) k_grouped<1><<<grid, block, kDynSmem, s>>>(map, a);
+        else k_grouped<2><<<grid, block, kDynSmem, s>>>(map, a);
     }
     return cudaGetLastError() == cudaSuccess ? launched + 1 : -1;
 }

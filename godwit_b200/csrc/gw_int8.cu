@@ -32,7 +32,7 @@ namespace gw {
 namespace {
 
 constexpr int kI8Warps = 8;           // warps per CTA
-constexpr int kI8Unroll = 4;          // groups in flight per warp
+constexpr int kI8Unroll = 8;          // groups in flight per warp
 constexpr int kI8MaxTok = 32;         // tokens per pass (kNB = 4)
 
 struct Int8Args {
@@ -85,7 +85,7 @@ __device__ __forceinline__ float bf16f(uint16_t v) { return __uint_as_float((uin
 // grid: ceil(tiles / (kI8Warps / ksplit)) CTAs of kI8Warps warps; warp w works
 // on tile blockIdx.x * (kI8Warps / ksplit) + w / ksplit, split w % ksplit.
 template <int kNB>
-__global__ void __launch_bounds__(kI8Warps * 32, kNB == 1 ? 3 : kNB == 2 ? 2 : 1) k_int8_gemv(Int8Args a) {
+__global__ void __launch_bounds__(kI8Warps * 32, kNB == 1 ? 2 : 1) k_int8_gemv(Int8Args a) {
     extern __shared__ float i8_smem[];
     const int ng = a.cols >> 6;
     const int tc = min(a.T, 8 * kNB);           // tokens per pass
@@ -273,7 +273,7 @@ int launch_int8_gemv(const uint8_t* codes, const uint16_t* meta, const uint16_t*
     const int tiles = (rows + 15) / 16;
     // K-split: the fewest warps per tile that still put ~16 warps on every SM
     while (a.ksplit < kI8Warps && (int64_t)tiles * a.ksplit < (int64_t)sms[dev] * 16 &&
-           cols / 64 >= 2 * a.ksplit * kI8Unroll)
+           cols / 64 >= 8 * a.ksplit)
         a.ksplit *= 2;
     const int tpc = kI8Warps / a.ksplit;
     const dim3 grid((tiles + tpc - 1) / tpc);

@@ -137,6 +137,8 @@ __device__ __forceinline__ void prep_block(const void* x, int x_dtype, int H, in
     else x16[i] = __float2half_rn(bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(x)[i]) * pow2f(p));
 }
 
+constexpr int kRouterSegs = (kMaxGemvCols + 255) / 256;  // 256-value hidden segments (banks cap H)
+
 // k_router: grid (E, ceil(T/8)), kRouterWarps warps (16 for a single token
 // chunk, where the grid is only E CTAs; 4 otherwise — both measured best on
 // B200); CTA (e, y) scores expert e against the chunk's (up to) 8 tokens,
@@ -154,56 +156,68 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router(LayerView L, MoeDi
     const int t0 = blockIdx.y * kTokTile;
     const int t1 = min(T, t0 + kTokTile);
     const uint4* wrow = reinterpret_cast<const uint4*>(L.router_w + (int64_t)e * d.H);
+    // The hidden dimension is cut into fixed segments of 32 8-value chunks (one
+    // chunk per lane), each summed by one warp's tree; warp w takes segments
+    // w, w + kRouterWarps, ... and the segment sums meet in segment order, so
+    // a token's logits come out bit-identical whatever the warp count (and
+    // so whatever the batch it is routed in).
     const int nchunk = d.H >> 3;
-    const int per = (nchunk + kRouterWarps - 1) / kRouterWarps;
-    const int c0 = warp * per, c1 = min(nchunk, c0 + per);
-    float acc[kTokTile], mx[kTokTile];
+    const int nseg = (nchunk + 31) >> 5;
+    __shared__ float racc[kRouterSegs][kTokTile], rmx[kRouterWarps][kTokTile];
+    __shared__ int shift[kTokTile];
+    float mx[kTokTile];
 #pragma unroll
-    for (int q = 0; q < kTokTile; ++q) acc[q] = mx[q] = 0.f;
-    for (int c = c0 + lane; c < c1; c += 32) {
-        const uint4 wv = __ldg(wrow + c);
-        const uint32_t wr[4] = {wv.x, wv.y, wv.z, wv.w};
+    for (int q = 0; q < kTokTile; ++q) mx[q] = 0.f;
+    for (int sg = warp; sg < nseg; sg += kRouterWarps) {
+        const int c = sg * 32 + lane;
+        float acc[kTokTile];
 #pragma unroll
-        for (int q = 0; q < kTokTile; ++q) {
-            if (t0 + q >= t1) break;
-            const uint4 xv = __ldg(reinterpret_cast<const uint4*>(
-                                       static_cast<const char*>(xr) + (int64_t)(t0 + q) * d.H * 2) + c);
-            const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
+        for (int q = 0; q < kTokTile; ++q) acc[q] = 0.f;
+        if (c < nchunk) {
+            const uint4 wv = __ldg(wrow + c);
+            const uint32_t wr[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                float x0, x1;
-                if (x_dtype == kBF16) {
-                    x0 = __uint_as_float(xx[u] << 16);
-                    x1 = __uint_as_float(xx[u] & 0xffff0000u);
-                } else {
-                    const __half2 h = *reinterpret_cast<const __half2*>(&xx[u]);
-                    x0 = __low2float(h);
-                    x1 = __high2float(h);
+            for (int q = 0; q < kTokTile; ++q) {
+                if (t0 + q >= t1) break;
+                const uint4 xv = __ldg(reinterpret_cast<const uint4*>(
+                                           static_cast<const char*>(xr) + (int64_t)(t0 + q) * d.H * 2) + c);
+                const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    float x0, x1;
+                    if (x_dtype == kBF16) {
+                        x0 = __uint_as_float(xx[u] << 16);
+                        x1 = __uint_as_float(xx[u] & 0xffff0000u);
+                    } else {
+                        const __half2 h = *reinterpret_cast<const __half2*>(&xx[u]);
+                        x0 = __low2float(h);
+                        x1 = __high2float(h);
+                    }
+                    mx[q] = fmaxf(mx[q], fmaxf(fabsf(x0), fabsf(x1)));
+                    acc[q] = fmaf(__uint_as_float(wr[u] << 16), x0, acc[q]);
+                    acc[q] = fmaf(__uint_as_float(wr[u] & 0xffff0000u), x1, acc[q]);
                 }
-                mx[q] = fmaxf(mx[q], fmaxf(fabsf(x0), fabsf(x1)));
-                acc[q] = fmaf(__uint_as_float(wr[u] << 16), x0, acc[q]);
-                acc[q] = fmaf(__uint_as_float(wr[u] & 0xffff0000u), x1, acc[q]);
             }
         }
+#pragma unroll
+        for (int q = 0; q < kTokTile; ++q) {
+            const float v = warp_sum(acc[q]);
+            if (lane == 0) racc[sg][q] = v;
+        }
     }
-    __shared__ float racc[kRouterWarps][kTokTile], rmx[kRouterWarps][kTokTile];
-    __shared__ int shift[kTokTile];
 #pragma unroll
     for (int q = 0; q < kTokTile; ++q) {
-        const float v = warp_sum(acc[q]);
         const float m = warp_max(mx[q]);
-        if (lane == 0) { racc[warp][q] = v; rmx[warp][q] = m; }
+        if (lane == 0) rmx[warp][q] = m;
     }
     __syncthreads();
     if (warp == 0 && lane < kTokTile && t0 + lane < t1) {
         const int q = lane;
         const float bias = L.router_b ? bf16_bits_to_f32(L.router_b[e]) : 0.f;
         float v = racc[0][q], m = rmx[0][q];
+        for (int j = 1; j < nseg; ++j) v += racc[j][q];
 #pragma unroll
-        for (int j = 1; j < kRouterWarps; ++j) {
-            v += racc[j][q];
-            m = fmaxf(m, rmx[j][q]);
-        }
+        for (int j = 1; j < kRouterWarps; ++j) m = fmaxf(m, rmx[j][q]);
         w.logits[(int64_t)(t0 + q) * d.E + e] = v + bias;
         const int p = x_dtype == kBF16 ? row_exponent_shift(m) : 0;
         shift[q] = p;

@@ -184,22 +184,31 @@ class AllToAllEP:
             partial += y[:, j]
         return partial
 
-    def forward(self, x: torch.Tensor, stream: torch.Tensor, x_work: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, stream: torch.Tensor, x_work: torch.Tensor,
+                check: bool = True) -> torch.Tensor:
         """x [T, H] (this rank's tokens, compute dtype) -> stream [T, H] fp32:
-        stream = x; for l: stream += moe_l(round(stream))."""
+        stream = x; for l: stream += moe_l(round(stream)).  check=False leaves
+        the capacity check to raise_if_overflowed() (a step captured in a CUDA
+        graph cannot read the flag back to the host)."""
         if self.capacity is None:  # one exchange of the token counts, then fixed shapes
             t = torch.tensor([x.shape[0]], dtype=torch.int64, device=x.device)
             if self._world() > 1:
                 dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
             self.set_capacity(int(t.item()))
         if self.capacity_factor is not None:
-            self.overflow = torch.zeros((), dtype=torch.bool, device=x.device)
+            if self.overflow is None:
+                self.overflow = torch.zeros((), dtype=torch.bool, device=x.device)
+            self.overflow.zero_()
         self.ops.widen(x, stream)
         x_work.copy_(x)
         for layer in range(self.layers):
             partial = self.layer_partial(layer, x_work)
             self.ops.residual(stream, partial, x_work)
+        if check:
+            self.raise_if_overflowed()
+        return stream
+
+    def raise_if_overflowed(self) -> None:
         if self.overflow is not None and bool(self.overflow):
             raise RuntimeError(f"an all-to-all block overflowed its capacity of {self.capacity} rows; "
                                "raise capacity_factor (or leave it unset for the exact bound)")
-        return stream

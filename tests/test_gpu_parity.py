@@ -153,6 +153,26 @@ def test_router_matches_oracle(ctx, oss_bank, T, dtype):
     check_topk(ex, ref_ex, ref, spec.top_k)
 
 
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_router_logits_do_not_depend_on_the_batch(ctx, oss_bank, dtype):
+    """A token's logits and routing are bit-identical whether it is routed
+    alone, in a single 8-token chunk or in a larger batch (the router's warp
+    count changes with the batch; its summation order does not), as the
+    reference routes each token on its own (Router.swift:100-104)."""
+    bank, _, _ = oss_bank
+    spec = bank.spec
+    rng = np.random.default_rng(31)
+    xb = synth.make_hidden(rng, 27, spec.hidden, dtype)
+    r = Router(ctx, bank)
+    full = r.logits(xb, 1, dtype)
+    ex_full, wt_full = r.route_batch(xb, 1, dtype)
+    for a, b in [(0, 1), (3, 9), (9, 27)]:
+        part = r.logits(xb[a:b], 1, dtype)
+        assert np.array_equal(part, full[a:b])
+        ex, wt = r.route_batch(xb[a:b], 1, dtype)
+        assert np.array_equal(ex, ex_full[a:b]) and np.array_equal(wt, wt_full[a:b])
+
+
 @pytest.mark.parametrize("E,T", [(32, 128), (128, 300), (128, 2048)])
 def test_batch_router_matches_oracle(ctx, E, T):
     """Large bf16 batches take the tensor-core router (k_router_mma): same
