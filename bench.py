@@ -595,11 +595,17 @@ def run_decode(args):
             line["int8_head"] = measure_int8_head(ctx, cur, local, 200, 3,
                                                   cpu_baseline=not args.no_cpu_baseline)
         print(json.dumps(line), flush=True)
+    if world > 1:
+        # The teardown of a process group whose collectives a CUDA graph
+        # captured has hung here: meet once more and leave without the graph,
+        # library or NCCL teardown (process exit releases the GPU).
+        torch.cuda.synchronize()
+        _barrier(world)
+        sys.stdout.flush()
+        sys.stderr.flush()
+        os._exit(0)
     bank.close()
     ctx.close()
-    if world > 1:
-        import torch.distributed as dist
-        dist.destroy_process_group()
     return 0
 
 

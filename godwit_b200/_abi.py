@@ -85,6 +85,8 @@ SIGNATURES = {
     "gw_moe_forward": (ST, [P, P, I32, P, I32, I32, P, P, P, P, P]),
     "gw_mxfp4_gemv": (ST, [P, P, P, P, P, I32, P, I32, I32]),
     "gw_int8_affine_gemv": (ST, [P, P, P, P, P, I32, I32, I32, P, I32]),
+    "gw_ep_dispatch_async": (ST, [P, P, P, I32, I32, P, P, I32, I32, P, P, P]),
+    "gw_ep_combine_async": (ST, [P, P, P, P, I32, P]),
     "gw_int8_affine_gemv_async": (ST, [P, P, P, P, P, I32, I32, I32, P, I32]),
     "gw_mxfp4_dequant": (ST, [P, P, P, I32, I32, P]),
     "gw_mxfp4_gemv_batched_async": (ST, [P, I32, P, I64, P, I64, P, I64, P, I64, I32, P, I64,

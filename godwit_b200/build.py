@@ -24,7 +24,7 @@ ORACLE_LIB = os.path.join(ORACLE_DIR, "liboracle.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hidden",
               "--expt-relaxed-constexpr"]
-CU_SOURCES = ["gw_kernels.cu", "gw_gemv.cu", "gw_grouped.cu", "gw_int8.cu", "gw_api.cu"]
+CU_SOURCES = ["gw_kernels.cu", "gw_gemv.cu", "gw_grouped.cu", "gw_int8.cu", "gw_ep.cu", "gw_api.cu"]
 HEADERS = ["gw_device.cuh", "gw_internal.h", "gw_async.cuh"]
 
 

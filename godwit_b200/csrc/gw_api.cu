@@ -1060,6 +1060,32 @@ gw_status gw_int8_affine_gemv_async(gw_ctx* c, const uint8_t* codes, const uint1
                                          y, y_dtype == GW_DTYPE_F16, c->cur));
 }
 
+gw_status gw_ep_dispatch_async(gw_ctx* c, gw_bank* b, const void* x, int32_t x_dtype, int32_t T,
+                               const int32_t* experts, const float* weights, int32_t world, int32_t capacity,
+                               void* send, int32_t* idx, int32_t* overflow) {
+    if (!c || !b || !send || !idx || !overflow) return fail(GW_E_ARG, "null argument");
+    gw_status st = check_dtype(x_dtype);
+    if (st) return st;
+    if (T < 0 || (T > 0 && (!x || !experts || !weights))) return fail(GW_E_ARG, "need T >= 0 and its inputs");
+    if (world < 1 || world > gw::kMaxEpWorld || capacity < 1)
+        return fail(GW_E_ARG, "need 1 <= world <= %d and capacity >= 1", gw::kMaxEpWorld);
+    if ((T > 0 && (st = check_align16(x, "x_dev"))) || (st = check_align16(send, "send_dev"))) return st;
+    CtxLock lk(c);
+    if ((st = set_device(c))) return st;
+    return count(c, gw::launch_ep_dispatch(x, T, b->d.hidden, experts, weights, b->d.top_k, world, capacity, send,
+                                           idx, overflow, c->cur));
+}
+
+gw_status gw_ep_combine_async(gw_ctx* c, gw_bank* b, const float* back, const int32_t* idx, int32_t T, float* out) {
+    if (!c || !b) return fail(GW_E_ARG, "null argument");
+    if (T < 0 || (T > 0 && (!back || !idx || !out))) return fail(GW_E_ARG, "need T >= 0 and its buffers");
+    gw_status st;
+    if (T > 0 && ((st = check_align16(back, "back_dev")) || (st = check_align16(out, "out_dev")))) return st;
+    CtxLock lk(c);
+    if ((st = set_device(c))) return st;
+    return count(c, gw::launch_ep_combine(back, idx, T, b->d.top_k, b->d.hidden, out, c->cur));
+}
+
 // ---- synchronous host-pointer API ------------------------------------------
 
 gw_status gw_int8_affine_gemv(gw_ctx* c, const uint8_t* codes, const uint16_t* meta, const uint16_t* bias,

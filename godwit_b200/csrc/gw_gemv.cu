@@ -612,11 +612,14 @@ __global__ void __launch_bounds__(kEThreads, 1) k_expert_gemv(const __grid_const
     }
 }
 
-// Smallest K-split (1, 2, 4 or 8 warps per tile) that gives the launch
-// about one and a half waves of CTAs (one per SM).
-int pick_split(int experts, int ntiles) {
+// K-split (1, 2 or 4 warps per tile): the smallest that gives the launch
+// about one work item per SM (measured best at batch 1: a second round of
+// items on an SM costs more than the split's reduction), keeping at least
+// two 8-block groups per split.
+int pick_split(int experts, int ntiles, int ngrp) {
     int ks = 1;
-    while (ks < 4 && (int64_t)experts * ((ntiles * ks + kCT - 1) / kCT) < 222) ks *= 2;
+    while (ks < 4 && ks * 2 <= std::max(1, ngrp / 2) && (int64_t)experts * ((ntiles * ks + kCT - 1) / kCT) < 118)
+        ks *= 2;
     return ks;
 }
 
@@ -658,7 +661,7 @@ int launch_expert_gemv(const LayerView& L, const MoeDims& d, const MoeWork& w, i
     const int wlast = nblk - 8 * ((nblk + 7) / 8 - 1);
     const int e_local = (d.E - d.shard_rank + d.shard_count - 1) / d.shard_count;
     const int maxa = std::min(d.E, T * d.k);
-    a.ksplit = pick_split(maxa, ntiles);
+    a.ksplit = pick_split(maxa, ntiles, (nblk + 7) / 8);
     const int tb = kCT / a.ksplit;
     // TMA views of the bank (uint8 elements; a tile is 16 * nblk * 16 bytes
     // of blocks and 16 * nblk bytes of scales; experts one stride apart):

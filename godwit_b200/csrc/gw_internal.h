@@ -119,6 +119,12 @@ constexpr int kMaxInt8Cols = 16384;
 int launch_int8_gemv(const uint8_t* codes, const uint16_t* meta, const uint16_t* bias, const __half* x,
                      int T, int rows, int cols, void* y, int y_f16, cudaStream_t s);
 int configure_int8();
+// Token-sliced expert parallelism (gw_ep.cu): pack (token, slot) rows into
+// world blocks of C rows of H + 4 16-bit words; sum returned outputs per token.
+constexpr int kMaxEpWorld = 64;
+int launch_ep_dispatch(const void* x, int T, int H, const int32_t* experts, const float* weights, int k, int world,
+                       int C, void* send, int32_t* idx, int32_t* overflow, cudaStream_t s);
+int launch_ep_combine(const float* back, const int32_t* idx, int T, int k, int H, float* out, cudaStream_t s);
 // Row-exponent table entries of a row-major scale matrix.
 int launch_rowexp(const uint8_t* scales, int rows, int cols, uint8_t* out, cudaStream_t s);
 int configure_kernels();

@@ -56,6 +56,20 @@ class CudaOps:
         self.D.route(self.ctx, self.bank, layer, x, ex, wt)
         return ex, wt
 
+    def dispatch(self, x: torch.Tensor, experts: torch.Tensor, weights: torch.Tensor, world: int, C: int,
+                 send: torch.Tensor, idx: torch.Tensor, overflow: torch.Tensor) -> None:
+        """Packs x's (token, slot) rows into send [world * C, H + 4] (see
+        AllToAllEP) and records each slot's row in idx [T * k] (one kernel
+        for the row plan, one for the copies)."""
+        self.D.call("gw_ep_dispatch_async", self.ctx.handle, self.bank.handle, self.D._p(x), self.D.dtype_code(x),
+                    x.shape[0], self.D._p(experts), self.D._p(weights), world, C, self.D._p(send), self.D._p(idx),
+                    self.D._p(overflow))
+
+    def combine(self, back: torch.Tensor, idx: torch.Tensor, T: int, out: torch.Tensor) -> None:
+        """out[t] = sum over slots j of back[idx[t * k + j]], in slot order."""
+        self.D.call("gw_ep_combine_async", self.ctx.handle, self.bank.handle, self.D._p(back), self.D._p(idx), T,
+                    self.D._p(out))
+
     def apply_rows(self, layer: int, rows: torch.Tensor, experts: torch.Tensor, weights: torch.Tensor,
                    out: torch.Tensor) -> None:
         """out[r] = weights[r] * expert_{experts[r]}(rows[r]) for owned experts: each row
@@ -121,7 +135,8 @@ class AllToAllEP:
         self.group = group
         self.capacity_factor = capacity_factor
         self.capacity = None
-        self.overflow = None
+        self.overflow = None      # bool flag of the torch packing
+        self.overflow_i32 = None  # int32 flag the library's packing kernel sets
 
     def _world(self):
         return dist.get_world_size(self.group) if dist.is_initialized() else 1
@@ -151,6 +166,40 @@ class AllToAllEP:
         else:  # a rank without tokens still takes part in every exchange
             experts = torch.empty((0, k), dtype=torch.int32, device=dev)
             weights = torch.empty((0, k), dtype=torch.float32, device=dev)
+        if hasattr(self.ops, "dispatch"):  # the library's fused pack / combine kernels
+            send = torch.empty((world * C, H + 4), dtype=x.dtype, device=dev)
+            idx = torch.empty((max(T * k, 1),), dtype=torch.int32, device=dev)
+            if self.overflow_i32 is None:
+                self.overflow_i32 = torch.zeros((), dtype=torch.int32, device=dev)
+            self.ops.dispatch(x, experts, weights, world, C, send, idx, self.overflow_i32)
+        else:
+            send, idx = self._dispatch_torch(x, experts, weights, world, C)
+        recv = torch.empty_like(send)
+        self._a2a(recv, send)
+        rows = recv[:, :H].contiguous()
+        rmeta = recv[:, H:].view(torch.int32)
+        out = torch.zeros((world * C, H), dtype=torch.float32, device=dev)
+        self.ops.apply_rows(layer, rows, rmeta[:, 0].contiguous(), rmeta[:, 1].contiguous().view(torch.float32),
+                            out)
+        back = torch.empty_like(out)
+        self._a2a(back, out)
+        partial = torch.empty((T, H), dtype=torch.float32, device=dev)
+        if T == 0:
+            return partial
+        if hasattr(self.ops, "combine"):
+            self.ops.combine(back, idx, T, partial)
+            return partial
+        y = back.index_select(0, idx.to(torch.int64)).view(T, k, H)
+        partial = y[:, 0].clone()
+        for j in range(1, k):                                          # slot order, as the combine
+            partial += y[:, j]
+        return partial
+
+    def _dispatch_torch(self, x, experts, weights, world: int, C: int):
+        """The same packing as the library's gw_ep_dispatch_async, in torch
+        ops (for compute stand-ins without it)."""
+        T, H = x.shape
+        k, dev = self.k, x.device
         flat_e = experts.reshape(-1).to(torch.int64)
         dest = torch.remainder(flat_e, world)
         # position of each slot in its owner's block: earlier slots bound for the same owner
@@ -167,22 +216,7 @@ class AllToAllEP:
             send[idx, :H] = x.index_select(0, slot_tok)
             packed = torch.stack([experts.reshape(-1), weights.reshape(-1).contiguous().view(torch.int32)], 1)
             meta[idx] = packed
-        recv = torch.empty_like(send)
-        self._a2a(recv, send)
-        rows = recv[:, :H].contiguous()
-        rmeta = recv[:, H:].view(torch.int32)
-        out = torch.zeros((world * C, H), dtype=torch.float32, device=dev)
-        self.ops.apply_rows(layer, rows, rmeta[:, 0].contiguous(), rmeta[:, 1].contiguous().view(torch.float32),
-                            out)
-        back = torch.empty_like(out)
-        self._a2a(back, out)
-        if T == 0:
-            return torch.empty((0, H), dtype=torch.float32, device=dev)
-        y = back.index_select(0, idx).view(T, k, H)
-        partial = y[:, 0].clone()
-        for j in range(1, k):                                          # slot order, as the combine
-            partial += y[:, j]
-        return partial
+        return send, idx
 
     def forward(self, x: torch.Tensor, stream: torch.Tensor, x_work: torch.Tensor,
                 check: bool = True) -> torch.Tensor:
@@ -199,16 +233,19 @@ class AllToAllEP:
             if self.overflow is None:
                 self.overflow = torch.zeros((), dtype=torch.bool, device=x.device)
             self.overflow.zero_()
+        if self.overflow_i32 is not None:
+            self.overflow_i32.zero_()
         self.ops.widen(x, stream)
         x_work.copy_(x)
         for layer in range(self.layers):
             partial = self.layer_partial(layer, x_work)
             self.ops.residual(stream, partial, x_work)
-        if check:
+        if check and self.capacity_factor is not None:
             self.raise_if_overflowed()
         return stream
 
     def raise_if_overflowed(self) -> None:
-        if self.overflow is not None and bool(self.overflow):
+        if (self.overflow is not None and bool(self.overflow)) or \
+                (self.overflow_i32 is not None and int(self.overflow_i32) != 0):
             raise RuntimeError(f"an all-to-all block overflowed its capacity of {self.capacity} rows; "
                                "raise capacity_factor (or leave it unset for the exact bound)")

@@ -330,6 +330,28 @@ GW_API gw_status gw_moe_forward_noalloc_async(gw_ctx* ctx, gw_bank* bank, int32_
                                               const void* x_dev, int32_t x_dtype, int32_t T,
                                               float* out_dev, int32_t* experts_dev,
                                               float* weights_dev);
+/* Token-sliced expert parallelism, device side.  No counterpart in the
+ * reference (it runs on one device); used by an engine that shards the
+ * experts over `world` GPUs by index (rank e % world holds expert e).
+ *
+ * gw_ep_dispatch_async packs this rank's T routed tokens for one all-to-all:
+ * send_dev holds world blocks of `capacity` rows, a row being H values of
+ * x_dtype followed by four 16-bit words (the slot's expert id as int32,
+ * -1 for an unused row, and its routing weight as fp32 bits); slot
+ * t * top_k + j goes to row (e % world) * capacity + (the number of earlier
+ * slots bound for the same rank), recorded in idx_dev [T * top_k].  A block
+ * that needs more than `capacity` rows sets *overflow_dev (int32) to 1 (its
+ * extra slots overwrite the block's last row); the caller checks it.
+ * gw_ep_combine_async sums, per token, the returned weighted expert outputs
+ * back_dev [world * capacity][H] fp32 at its slots' rows, in slot order,
+ * into out_dev [T][H].  x_dev, send_dev, back_dev and out_dev 16-byte
+ * aligned (send rows are then 8-byte aligned); world <= 64. */
+GW_API gw_status gw_ep_dispatch_async(gw_ctx* ctx, gw_bank* bank, const void* x_dev, int32_t x_dtype,
+                                      int32_t T, const int32_t* experts_dev, const float* weights_dev,
+                                      int32_t world, int32_t capacity, void* send_dev, int32_t* idx_dev,
+                                      int32_t* overflow_dev);
+GW_API gw_status gw_ep_combine_async(gw_ctx* ctx, gw_bank* bank, const float* back_dev,
+                                     const int32_t* idx_dev, int32_t T, float* out_dev);
 /* Kernel timing recorded with CUDA events on the context's stream around
  * each expert GEMV launch while profiling is enabled. */
 typedef struct gw_profile {

@@ -172,3 +172,32 @@ extension CUDAExpertBank {
         }
     }
 }
+
+/// The trunk's int8 affine projections (Install/Int8Affine.swift format: codes
+/// [rows][cols], then a bf16 (scale, zero) pair per row and 64 columns), in
+/// place of the Metal int8_affine_gemv / int8_affine_gemv_bias_batched
+/// (Sources/Godwit/Metal/MoE/router.metal:65-141) that ModelRunner.project
+/// (Runtime/ModelRunner.swift:165-190) and Attention.encodeProjection
+/// (Runtime/Attention.swift:218-240) dispatch.  The tensors live on the
+/// device (uploaded once, e.g. with cudaMemcpy from the installed trunk.bin
+/// section); the calls are ordered on the context's stream.
+public final class CUDATrunkProjection {
+    let ctx: OpaquePointer?
+    public init(context: OpaquePointer?) { ctx = context }
+
+    /// The output head: one f16 token -> fp32 logits [rows].
+    public func head(codes: UnsafePointer<UInt8>, meta: UnsafePointer<UInt16>,
+                     x: UnsafePointer<UInt16>, rows: Int, cols: Int,
+                     y: UnsafeMutablePointer<Float>) throws {
+        try check(gw_int8_affine_gemv_async(ctx, codes, meta, nil, x, 1, Int32(rows), Int32(cols),
+                                            UnsafeMutableRawPointer(y), GW_DTYPE_F32))
+    }
+
+    /// q/k/v/o: `tokens` f16 rows -> f16 [tokens][rows] with the bf16 bias.
+    public func project(codes: UnsafePointer<UInt8>, meta: UnsafePointer<UInt16>,
+                        bias: UnsafePointer<UInt16>, x: UnsafePointer<UInt16>, tokens: Int,
+                        rows: Int, cols: Int, y: UnsafeMutablePointer<UInt16>) throws {
+        try check(gw_int8_affine_gemv_async(ctx, codes, meta, bias, x, Int32(tokens), Int32(rows),
+                                            Int32(cols), UnsafeMutableRawPointer(y), GW_DTYPE_F16))
+    }
+}

@@ -110,3 +110,54 @@ def test_two_nccl_ranks_match_one_gpu(tmp_path):
     got = np.concatenate([np.load(tmp_path / f"r{r}.npy") for r in range(2)])
     one = _stack(0, 1)
     assert O.rel_l2(got, one) < 1e-5
+
+
+@pytest.mark.parametrize("world,cap", [(1, 48), (3, 24), (3, 4)])
+def test_fused_dispatch_and_combine_match_the_torch_packing(ctx, world, cap):
+    """gw_ep_dispatch_async / gw_ep_combine_async against the same packing in
+    torch ops: identical slot rows, metadata words and per-token sums; a
+    capacity too small for a block raises the overflow flag."""
+    import torch
+    from godwit_b200 import device as D
+    from godwit_b200.ep import AllToAllEP, CudaOps
+    from godwit_b200.runtime import ExpertBank
+
+    bank = ExpertBank(ctx, SPEC, layers=1)
+    try:
+        D.bind_stream(ctx, torch.cuda.current_stream())
+        g = torch.Generator(device="cuda").manual_seed(world * 100 + cap)
+        x = torch.randn((T, SPEC.hidden), device="cuda", generator=g).to(torch.bfloat16)
+        ex = torch.stack([torch.randperm(SPEC.experts, device="cuda", generator=g)[:SPEC.top_k]
+                          for _ in range(T)]).to(torch.int32)
+        wt = torch.rand((T, SPEC.top_k), device="cuda", generator=g)
+        ep = AllToAllEP(None, 1, SPEC.top_k, capacity_factor=1.0)
+        ep.overflow = torch.zeros((), dtype=torch.bool, device="cuda")
+        ref_send, ref_idx = ep._dispatch_torch(x, ex, wt, world, cap)
+        ops = CudaOps(ctx, bank)
+        send = torch.empty_like(ref_send)
+        idx = torch.empty((T * SPEC.top_k,), dtype=torch.int32, device="cuda")
+        flag = torch.zeros((), dtype=torch.int32, device="cuda")
+        ops.dispatch(x, ex, wt, world, cap, send, idx, flag)
+        torch.cuda.synchronize()
+        overflowed = bool(ep.overflow)
+        assert bool(flag) == overflowed
+        H = SPEC.hidden
+        meta = send[:, H:].view(torch.int32)
+        ref_meta = ref_send[:, H:].view(torch.int32)
+        if not overflowed:
+            assert torch.equal(idx.to(torch.int64), ref_idx)
+            assert torch.equal(meta, ref_meta)
+            used = meta[:, 0] >= 0
+            assert torch.equal(send[used, :H], ref_send[used, :H])
+            back = torch.randn((world * cap, H), device="cuda", generator=g)
+            out = torch.empty((T, H), device="cuda")
+            ops.combine(back, idx, T, out)
+            y = back.index_select(0, ref_idx).view(T, SPEC.top_k, H)
+            want = y[:, 0].clone()
+            for j in range(1, SPEC.top_k):
+                want += y[:, j]
+            torch.cuda.synchronize()
+            assert torch.equal(out, want)
+    finally:
+        ctx.set_stream(None)
+        bank.close()
