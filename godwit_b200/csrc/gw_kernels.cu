@@ -148,27 +148,31 @@ constexpr int kRouterSegs = (kMaxGemvCols + 255) / 256;  // 256-value hidden seg
 // its token chunk's counter; the last CTA of a chunk selects the top-k of the
 // chunk's tokens and adds their slots to the expert lists (whose counts the
 // previous combine left at zero).
-template <int kRouterWarps>
+template <int kRouterWarps, int kEpc>
 __global__ void __launch_bounds__(kRouterWarps * 32) k_router(LayerView L, MoeDims d, const void* __restrict__ xr,
                                                 int x_dtype, int T, MoeWork w) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int e = blockIdx.x;
+    const int e0 = blockIdx.x * kEpc;
     const int t0 = blockIdx.y * kTokTile;
     const int t1 = min(T, t0 + kTokTile);
-    const uint4* wrow = reinterpret_cast<const uint4*>(L.router_w + (int64_t)e * d.H);
     // The hidden dimension is cut into fixed segments of 32 8-value chunks (one
-    // chunk per lane), each summed by one warp's tree; warp w takes segments
-    // w, w + kRouterWarps, ... and the segment sums meet in segment order, so
-    // a token's logits come out bit-identical whatever the warp count (and
-    // so whatever the batch it is routed in).
+    // chunk per lane), each summed by one warp's tree; the warps take the
+    // (expert, segment) units of the CTA's kEpc experts in turn and the
+    // segment sums meet in segment order, so a token's logits come out
+    // bit-identical whatever the warp count or the experts per CTA (and so
+    // whatever the batch it is routed in).
     const int nchunk = d.H >> 3;
     const int nseg = (nchunk + 31) >> 5;
-    __shared__ float racc[kRouterSegs][kTokTile], rmx[kRouterWarps][kTokTile];
+    __shared__ float racc[kEpc][kRouterSegs][kTokTile], rmx[kRouterWarps][kTokTile];
     __shared__ int shift[kTokTile];
     float mx[kTokTile];
 #pragma unroll
     for (int q = 0; q < kTokTile; ++q) mx[q] = 0.f;
-    for (int sg = warp; sg < nseg; sg += kRouterWarps) {
+    for (int u = warp; u < kEpc * nseg; u += kRouterWarps) {
+        const int le = u / nseg, sg = u - le * nseg;
+        const int e = e0 + le;
+        if (e >= d.E) break;
+        const uint4* wrow = reinterpret_cast<const uint4*>(L.router_w + (int64_t)e * d.H);
         const int c = sg * 32 + lane;
         float acc[kTokTile];
 #pragma unroll
@@ -183,26 +187,26 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router(LayerView L, MoeDi
                                            static_cast<const char*>(xr) + (int64_t)(t0 + q) * d.H * 2) + c);
                 const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
+                for (int v = 0; v < 4; ++v) {
                     float x0, x1;
                     if (x_dtype == kBF16) {
-                        x0 = __uint_as_float(xx[u] << 16);
-                        x1 = __uint_as_float(xx[u] & 0xffff0000u);
+                        x0 = __uint_as_float(xx[v] << 16);
+                        x1 = __uint_as_float(xx[v] & 0xffff0000u);
                     } else {
-                        const __half2 h = *reinterpret_cast<const __half2*>(&xx[u]);
+                        const __half2 h = *reinterpret_cast<const __half2*>(&xx[v]);
                         x0 = __low2float(h);
                         x1 = __high2float(h);
                     }
                     mx[q] = fmaxf(mx[q], fmaxf(fabsf(x0), fabsf(x1)));
-                    acc[q] = fmaf(__uint_as_float(wr[u] << 16), x0, acc[q]);
-                    acc[q] = fmaf(__uint_as_float(wr[u] & 0xffff0000u), x1, acc[q]);
+                    acc[q] = fmaf(__uint_as_float(wr[v] << 16), x0, acc[q]);
+                    acc[q] = fmaf(__uint_as_float(wr[v] & 0xffff0000u), x1, acc[q]);
                 }
             }
         }
 #pragma unroll
         for (int q = 0; q < kTokTile; ++q) {
             const float v = warp_sum(acc[q]);
-            if (lane == 0) racc[sg][q] = v;
+            if (lane == 0) racc[le][sg][q] = v;
         }
     }
 #pragma unroll
@@ -211,14 +215,21 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router(LayerView L, MoeDi
         if (lane == 0) rmx[warp][q] = m;
     }
     __syncthreads();
+    if ((int)threadIdx.x < kEpc * kTokTile) {
+        const int le = threadIdx.x / kTokTile, q = threadIdx.x % kTokTile;
+        const int e = e0 + le;
+        if (e < d.E && t0 + q < t1) {
+            const float bias = L.router_b ? bf16_bits_to_f32(L.router_b[e]) : 0.f;
+            float v = racc[le][0][q];
+            for (int j = 1; j < nseg; ++j) v += racc[le][j][q];
+            w.logits[(int64_t)(t0 + q) * d.E + e] = v + bias;
+        }
+    }
     if (warp == 0 && lane < kTokTile && t0 + lane < t1) {
         const int q = lane;
-        const float bias = L.router_b ? bf16_bits_to_f32(L.router_b[e]) : 0.f;
-        float v = racc[0][q], m = rmx[0][q];
-        for (int j = 1; j < nseg; ++j) v += racc[j][q];
+        float m = rmx[0][q];
 #pragma unroll
         for (int j = 1; j < kRouterWarps; ++j) m = fmaxf(m, rmx[j][q]);
-        w.logits[(int64_t)(t0 + q) * d.E + e] = v + bias;
         const int p = x_dtype == kBF16 ? row_exponent_shift(m) : 0;
         shift[q] = p;
         if (blockIdx.x == 0) w.xmul[t0 + q] = pow2f(-p);
@@ -637,8 +648,10 @@ int launch_router(const LayerView& L, const MoeDims& d, const void* x, int x_dty
         return ok_or_fail();
     }
     dim3 grid(d.E, (T + kTokTile - 1) / kTokTile);
-    if (T <= kTokTile) k_router<16><<<grid, 16 * 32, 0, s>>>(L, d, x, x_dtype, T, w);
-    else k_router<4><<<grid, 4 * 32, 0, s>>>(L, d, x, x_dtype, T, w);
+    // one expert per CTA (8 experts per CTA, reading each token chunk once,
+    // measured 1.9x slower at batch 64: too few warps in flight)
+    if (T <= kTokTile) k_router<16, 1><<<grid, 16 * 32, 0, s>>>(L, d, x, x_dtype, T, w);
+    else k_router<4, 1><<<grid, 4 * 32, 0, s>>>(L, d, x, x_dtype, T, w);
     return ok_or_fail();
 }
 
