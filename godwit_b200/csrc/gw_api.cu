@@ -313,14 +313,19 @@ gw_status moe_layer_device(gw_ctx* c, gw_bank* b, int layer, const void* x_dev, 
     const int64_t slots = slots_hint >= 0 ? slots_hint : (int64_t)T * d.k;
     const bool mma = w.mma_min_avg > 0 && slots >= (int64_t)w.mma_min_avg * d.E &&
                      gw::grouped_supported(d, w);
+    // A handful of slots (batch 1-2): the small-batch GEMV tiles, whose
+    // launches start streaming sooner than the persistent TMA-fed kernel's.
+    const bool small = !mma && slots <= gw::kSmallBatchSlots;
     if ((st = timed_launch(c, 0, 0, [&] {
-             return mma ? gw::launch_grouped(L, d, w, 0, c->sms, c->cur, x_dev, x_dtype)
-                        : gw::launch_expert_gemv(L, d, w, T, 0, c->cur);
+             return mma     ? gw::launch_grouped(L, d, w, 0, c->sms, c->cur, x_dev, x_dtype)
+                    : small ? gw::launch_gateup(L, d, x_dev, x_dtype, T, w, c->cur)
+                            : gw::launch_expert_gemv(L, d, w, T, 0, c->cur);
          })))
         return st;
     if ((st = timed_launch(c, 1, 0, [&] {
-             return mma ? gw::launch_grouped(L, d, w, 1, c->sms, c->cur)
-                        : gw::launch_expert_gemv(L, d, w, T, 1, c->cur);
+             return mma     ? gw::launch_grouped(L, d, w, 1, c->sms, c->cur)
+                    : small ? gw::launch_down(L, d, T, w, c->cur)
+                            : gw::launch_expert_gemv(L, d, w, T, 1, c->cur);
          })))
         return st;
     if (c->prof && (st = log_nactive(c))) return st;

@@ -290,6 +290,112 @@ __device__ __forceinline__ void mxfp4_tile_diag(const uint8_t* __restrict__ pack
     }
 }
 
+// One 8-block group of mxfp4_tile_diag, for weights already in shared
+// memory (or any generic address): gA / gB point at the group's first block
+// of rows A and B (w blocks per row, the group's width), hA / hB at their
+// scale bytes; base = the group's first block in the row, nblk = the row's
+// blocks (the zero block of xs sits at index nblk).  Accumulates into
+// accA / accB the same per-block partials times scales as one iteration of
+// mxfp4_tile_diag's group loop, with the partials summed over four
+// independent MMA chains; the caller sums the quad at the end (quad_sum_acc).
+template <int kTok, int kSets>
+__device__ __forceinline__ void mxfp4_group_diag(const uint4* gA, const uint4* gB, const uint8_t* hA,
+                                                 const uint8_t* hB, int base, int nblk, const __half* xs,
+                                                 int xs_stride, int ntok, float (&accA)[kTok * kSets],
+                                                 float (&accB)[kTok * kSets]) {
+    static_assert((kTok == 1 && kSets == 1) || kTok == 2, "1 token, or token pairs");
+    const int lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int zero_blk = nblk;
+    uint4 ca[2], cb[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const int j = 4 * r + t;
+        if (base + j < nblk) { ca[r] = gA[j]; cb[r] = gB[j]; }
+        else { ca[r] = make_uint4(0, 0, 0, 0); cb[r] = make_uint4(0, 0, 0, 0); }
+    }
+    auto xsrc = [&](int r, int s) -> const uint4* {
+        const int blk = base + 4 * r + t;
+        int tok = -1;
+        if (kTok == 1) tok = (g == 4 * r + t) ? 0 : -1;
+        else tok = (g >> 1) == t ? 2 * s + (g & 1) : -1;
+        const bool live = tok >= 0 && tok < ntok && blk < nblk;
+        return reinterpret_cast<const uint4*>(live ? xs + tok * xs_stride + blk * kXBlockHalves
+                                                   : xs + zero_blk * kXBlockHalves);
+    };
+    // four independent MMA chains per token set (round r, even / odd word)
+    // so a warp keeps several MMAs in flight; summed before each flush
+    float d[2][kSets][2][4];
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int s = 0; s < kSets; ++s)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) d[r][s][h][0] = d[r][s][h][1] = d[r][s][h][2] = d[r][s][h][3] = 0.f;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const uint4* xp[kSets];
+#pragma unroll
+        for (int s = 0; s < kSets; ++s) xp[s] = xsrc(r, s);
+        const uint32_t wA[4] = {ca[r].x, ca[r].y, ca[r].z, ca[r].w};
+        const uint32_t wB[4] = {cb[r].x, cb[r].y, cb[r].z, cb[r].w};
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            uint32_t a0, a1, a2, a3, q0, q1, q2, q3;
+            e2m1x8_to_f16x8(wA[w], a0, a1, a2, a3);
+            e2m1x8_to_f16x8(wB[w], q0, q1, q2, q3);
+#pragma unroll
+            for (int s = 0; s < kSets; ++s) {
+                const uint4 xv = xp[s][w];
+                float(&dd)[4] = d[r][s][w & 1];
+                mma16816(dd, a0, q0, a1, q1, xv.x, xv.y, dd);
+                mma16816(dd, a2, q2, a3, q3, xv.z, xv.w, dd);
+            }
+        }
+    }
+    if constexpr (kTok == 2) {
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int blk = base + 4 * r + t;
+            const bool ok = blk < nblk;
+            const float fa = ok ? gemv_scale(hA[4 * r + t]) : 0.f;
+            const float fb = ok ? gemv_scale(hB[4 * r + t]) : 0.f;
+#pragma unroll
+            for (int s = 0; s < kSets; ++s) {
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    const int tok = 2 * s + q;
+                    accA[tok] = fmaf(d[r][s][0][q] + d[r][s][1][q], fa, accA[tok]);
+                    accB[tok] = fmaf(d[r][s][0][2 + q] + d[r][s][1][2 + q], fb, accB[tok]);
+                }
+            }
+        }
+    } else {
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const int blk = base + 2 * t + q;
+            const bool ok = blk < nblk;
+            const float fa = ok ? gemv_scale(hA[2 * t + q]) : 0.f;
+            const float fb = ok ? gemv_scale(hB[2 * t + q]) : 0.f;
+            const float sa = (d[0][0][0][q] + d[0][0][1][q]) + (d[1][0][0][q] + d[1][0][1][q]);
+            const float sb = (d[0][0][0][2 + q] + d[0][0][1][2 + q]) + (d[1][0][0][2 + q] + d[1][0][1][2 + q]);
+            accA[0] = fmaf(sa, fa, accA[0]);
+            accB[0] = fmaf(sb, fb, accB[0]);
+        }
+    }
+}
+
+template <int kN>
+__device__ __forceinline__ void quad_sum_acc(float (&accA)[kN], float (&accB)[kN]) {
+#pragma unroll
+    for (int j = 0; j < kN; ++j) {
+        accA[j] += __shfl_xor_sync(0xffffffffu, accA[j], 1);
+        accA[j] += __shfl_xor_sync(0xffffffffu, accA[j], 2);
+        accB[j] += __shfl_xor_sync(0xffffffffu, accB[j], 1);
+        accB[j] += __shfl_xor_sync(0xffffffffu, accB[j], 2);
+    }
+}
+
 // Tiled bank layout of an MXFP4 matrix [rows][cols] (rows % 16 == 0): the
 // 16-row tiles follow one another; inside a tile the 32-column blocks go in
 // groups of 8 (the last group narrower), and each group stores its 16 rows

@@ -12,8 +12,9 @@ constexpr int kMaxTopK = 16;
 constexpr int kMaxExperts = 256;
 constexpr int kTokTile = 8;       // tokens per router CTA
 constexpr int kRouterMmaMinTokens = 128;  // bf16 batches from here on use k_router_mma
-constexpr int kGemvWarps = 4;
-constexpr int kGemvPass = 8;      // tokens per pass of the expert GEMV over an expert's weights     // warps per k_gemv CTA (one 16-row tile each)
+constexpr int kGemvWarps = 4;     // warps per GEMV CTA (k_gemv, k_gateup, k_down: one 16-row tile each)
+constexpr int kChunk = 4;         // tokens per weight pass of a k_gateup / k_down tile
+constexpr int kGemvPass = 8;      // tokens per pass of the expert GEMV over an expert's weights
 
 // Element types of activation inputs.  F32 is internal: the residual stream
 // that the stack forward rounds to the configured input type.
@@ -73,6 +74,15 @@ int launch_router(const LayerView& L, const MoeDims& d, const void* x, int x_dty
                   const MoeWork& w, cudaStream_t s);
 int launch_group(const MoeDims& d, const int32_t* experts_in, const float* weights_in, int T,
                  const MoeWork& w, cudaStream_t s);
+// Small-batch expert GEMVs (gw_kernels.cu): one active expert per CTA row,
+// each warp one 16-row tile loaded by its own lanes with an L2 prefetch of
+// the tile; the GEMV path's choice for layers of at most kSmallBatchSlots
+// (token, slot) pairs, where their low launch latency beats the persistent
+// TMA-fed kernel.
+constexpr int kSmallBatchSlots = 8;
+int launch_gateup(const LayerView& L, const MoeDims& d, const void* x, int x_dtype, int T,
+                  const MoeWork& w, cudaStream_t s);
+int launch_down(const LayerView& L, const MoeDims& d, int T, const MoeWork& w, cudaStream_t s);
 int launch_combine(const MoeDims& d, int T, const MoeWork& w, float* out, int accumulate,
                    void* x_next, int x_dtype, cudaStream_t s);
 int launch_gemv_batched(int count, const uint8_t* packed, int64_t packed_stride,
@@ -99,7 +109,7 @@ int launch_tile_layout(const uint8_t* src, uint8_t* dst, int rows, int cols, int
 constexpr unsigned kStatusProbe = 0x100u;
 int launch_wait_probe(unsigned* status, long long limit, cudaStream_t s);
 int launch_widen(const void* x, int x_dtype, float* stream, int64_t n, cudaStream_t s);
-size_t gemv_smem_bytes(int cols);
+size_t gemv_smem_bytes(int cols, int max_tok);
 // Tensor-core grouped expert GEMM (gw_grouped.cu): which 0 = gate_up + activation,
 // 1 = down + routing weight.  `sms` persistent CTAs.
 int launch_grouped(const LayerView& L, const MoeDims& d, const MoeWork& w, int which, int sms,

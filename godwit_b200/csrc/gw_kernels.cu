@@ -10,6 +10,10 @@
 //                   (Runtime/TransformerLayer.swift:265-285, router.metal:41-60)
 //   k_group         the same grouping for a routing decision supplied by the
 //                   caller (ExpertRunner.applyAssignments' assignment set)
+//   k_gateup        grouped MXFP4 gate_up GEMV + bias + activation epilogue
+//                   (expert.metal:46-102, :380-393), one expert per CTA row
+//   k_down          grouped MXFP4 down GEMV + bias, scaled by the routing weight
+//                   (expert.metal:107-116 folded into the epilogue)
 //   k_combine       per-token sum of its k expert contributions in rank order,
 //                   optionally added to the residual stream, which is then
 //                   rounded into the next layer's input
@@ -459,6 +463,188 @@ __global__ void __launch_bounds__(256) k_group(MoeDims d, const int32_t* __restr
     }
 }
 
+// ---------------------------------------------------------------------------
+// Grouped expert GEMVs.  grid (min(E, T*k), ceil(tiles / tiles_per_cta)),
+// 4 warps: CTA (a, y) takes the a-th active expert; each of its warps owns one
+// 16-row tile and a 1/ksplit share of the K blocks (ksplit = 1, 2 or 4 warps
+// per tile, chosen by the host so that few-expert launches still fill the
+// GPU).  As soon as the expert is known every warp queues its weight tile for
+// L2; the expert's tokens are then walked in pairs staged in shared memory,
+// so the tile streams from HBM once and any further pass (an expert chosen by
+// 3+ tokens) hits L2.
+
+// Block range of split `sp` out of `ksplit` (multiples of the 8-block group).
+__device__ __forceinline__ void split_range(int nblk, int ksplit, int sp, int& b0, int& b1) {
+    const int groups = (nblk + 7) >> 3;
+    const int per = (groups + ksplit - 1) / ksplit;
+    b0 = min(nblk, sp * per * 8);
+    b1 = min(nblk, (sp + 1) * per * 8);
+}
+
+// Runs one token chunk (n = 1..kChunk) of a bank tile (tiled layout: packed /
+// scales point at the tile, rowA / rowB are tile rows) split over `ksplit` warps
+// and calls emit(token, rowA total, rowB total) once per (row pair, token)
+// on the split-0 warp.  Every thread of the CTA must call this (it
+// synchronises when ksplit > 1).  kPrefetch: see mxfp4_tile_diag.
+// L2 prefetch policy of the two expert GEMVs (see mxfp4_tile_diag's
+// kPrefetch): whole K-range up front for gate_up, two groups ahead for down.
+constexpr int kPrefetchGateup = 1, kPrefetchDown = 2;
+template <int kPrefetch, class Emit>
+__device__ __forceinline__ void run_tile(int n, bool valid, const uint8_t* packed,
+                                         const uint8_t* scales, int cols, int rowA, int rowB,
+                                         const __half* xs, int ksplit, Emit&& emit) {
+    __shared__ float red[kGemvWarps][8][2 * kChunk];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int sp = warp % ksplit;
+    int b0, b1;
+    split_range(cols >> 5, ksplit, sp, b0, b1);
+    float a[kChunk], b[kChunk];
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) a[j] = b[j] = 0.f;
+    if (valid) {
+        const int st = diag_stride(cols);
+        if (n == 1) {
+            float a1[1], bb1[1];
+            mxfp4_tile_diag<1, 1, true, false>(packed, scales, cols, rowA, rowB, xs, st, 1, b0, b1, a1, bb1);
+            a[0] = a1[0];
+            b[0] = bb1[0];
+        } else if (n == 2) {
+            float a2[2], bb2[2];
+            mxfp4_tile_diag<2, 1, true, kPrefetch>(packed, scales, cols, rowA, rowB, xs, st, 2, b0, b1, a2, bb2);
+            a[0] = a2[0]; a[1] = a2[1];
+            b[0] = bb2[0]; b[1] = bb2[1];
+        } else {
+            mxfp4_tile_diag<2, 2, true, kPrefetch>(packed, scales, cols, rowA, rowB, xs, st, n, b0, b1, a, b);
+        }
+    }
+    if (ksplit > 1) {
+        if (t == 0) {
+#pragma unroll
+            for (int j = 0; j < kChunk; ++j) {
+                red[warp][g][j] = a[j];
+                red[warp][g][kChunk + j] = b[j];
+            }
+        }
+        __syncthreads();
+        if (sp == 0 && t == 0) {
+            for (int q = 1; q < ksplit; ++q) {
+#pragma unroll
+                for (int j = 0; j < kChunk; ++j) {
+                    a[j] += red[warp + q][g][j];
+                    b[j] += red[warp + q][g][kChunk + j];
+                }
+            }
+        }
+        __syncthreads();
+    }
+    if (valid && sp == 0 && t == 0) {
+#pragma unroll
+        for (int j = 0; j < kChunk; ++j)
+            if (j < n) emit(j, a[j], b[j]);
+    }
+}
+
+template <int kAct>
+__global__ void __launch_bounds__(kGemvWarps * 32, 5) k_gateup(LayerView L, MoeDims d, const void* x,
+                                                              int x_dtype, int T, MoeWork w,
+                                                              int ksplit) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __half* xs = reinterpret_cast<__half*>(smem_raw);
+    __shared__ int rows[kChunk];
+    __shared__ int slots[kChunk];
+    __shared__ float xm[kChunk];
+    const int a = blockIdx.x;
+    if (a >= *w.nactive) return;
+    const int e = w.active[a];
+    const uint8_t* ex = L.base + (int64_t)(e / d.shard_count) * L.stride;
+    const uint8_t* packed = ex + L.off[0];
+    const uint8_t* scales = ex + L.off[1];
+    const uint16_t* bias = reinterpret_cast<const uint16_t*>(ex + L.off[4]);
+    const int H = d.H, F = d.F;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2;
+    const int tile = blockIdx.y * (kGemvWarps / ksplit) + warp / ksplit;
+    const int ntiles = F >> 3;  // 8 output features (16 interleaved rows) per tile
+    const bool valid = tile < ntiles;
+    const int f = tile * 8 + g;
+    const int rowA = valid ? 2 * f : 0, rowB = rowA + 1;
+    zero_block_init(xs, H);
+    const int cnt = min(w.counts[e], w.tcap);
+    const int* list = w.lists + (int64_t)e * w.tcap;
+    float bA = 0.f, bB = 0.f;
+    if (valid) { bA = bf16_bits_to_f32(bias[rowA]); bB = bf16_bits_to_f32(bias[rowB]); }
+
+    for (int c0 = 0; c0 < cnt;) {
+        const int n = min(kChunk, cnt - c0);
+        __syncthreads();
+        if (threadIdx.x < kChunk) {
+            const int s = threadIdx.x < n ? list[c0 + threadIdx.x] : 0;
+            slots[threadIdx.x] = s;
+            rows[threadIdx.x] = s / d.k;
+            xm[threadIdx.x] = threadIdx.x < n ? w.xmul[s / d.k] : 0.f;
+        }
+        __syncthreads();
+        stage_x16(xs, diag_stride(H), w.x16, rows, n, H);
+        __syncthreads();
+        run_tile<kPrefetchGateup>(n, valid, packed + (size_t)tile * 16 * (H >> 1), scales + (size_t)tile * 16 * (H >> 5),
+                 H, 2 * g, 2 * g + 1, xs, ksplit,
+                 [&](int col, float ga, float ub) {
+                     const float v = activate<kAct>(ga * xm[col] + bA, ub * xm[col] + bB, d.limit, d.alpha);
+                     w.act[(int64_t)slots[col] * F + f] = __float2half_rn(v);
+                 });
+        c0 += n;
+    }
+}
+
+__global__ void __launch_bounds__(kGemvWarps * 32, 5) k_down(LayerView L, MoeDims d, int T, MoeWork w,
+                                                            int ksplit) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __half* xs = reinterpret_cast<__half*>(smem_raw);
+    __shared__ int slots[kChunk];
+    __shared__ float wt[kChunk];
+    const int a = blockIdx.x;
+    if (a >= *w.nactive) return;
+    const int e = w.active[a];
+    const uint8_t* ex = L.base + (int64_t)(e / d.shard_count) * L.stride;
+    const uint8_t* packed = ex + L.off[2];
+    const uint8_t* scales = ex + L.off[3];
+    const uint16_t* bias = reinterpret_cast<const uint16_t*>(ex + L.off[5]);
+    const int H = d.H, F = d.F;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2;
+    const int tile = blockIdx.y * (kGemvWarps / ksplit) + warp / ksplit;
+    const int ntiles = H >> 4;
+    const bool valid = tile < ntiles;
+    const int rowA = valid ? tile * 16 + g : 0, rowB = rowA + 8;
+    zero_block_init(xs, F);
+    const int cnt = min(w.counts[e], w.tcap);
+    const int* list = w.lists + (int64_t)e * w.tcap;
+    float bA = 0.f, bB = 0.f;
+    if (valid) { bA = bf16_bits_to_f32(bias[rowA]); bB = bf16_bits_to_f32(bias[rowB]); }
+
+    for (int c0 = 0; c0 < cnt;) {
+        const int n = min(kChunk, cnt - c0);
+        __syncthreads();
+        if (threadIdx.x < kChunk) {
+            const int s = threadIdx.x < n ? list[c0 + threadIdx.x] : 0;
+            slots[threadIdx.x] = s;
+            wt[threadIdx.x] = threadIdx.x < n ? w.weights[s] : 0.f;
+        }
+        __syncthreads();
+        stage_x16(xs, diag_stride(F), w.act, slots, n, F);
+        __syncthreads();
+        run_tile<kPrefetchDown>(n, valid, packed + (size_t)tile * 16 * (F >> 1), scales + (size_t)tile * 16 * (F >> 5),
+                 F, g, g + 8, xs, ksplit,
+                 [&](int col, float ya, float yb) {
+                     float* y = w.ybuf + (int64_t)slots[col] * H;
+                     y[rowA] = (ya + bA) * wt[col];
+                     y[rowB] = (yb + bB) * wt[col];
+                 });
+        c0 += n;
+    }
+}
+
 // k_combine: s = sum over ranks j of ybuf[t*k+j] (skipping slots whose expert
 // this shard does not own); out (=|+=) s; if x_next, x_next = round(out) in
 // x_dtype.  grid (ceil(H/4/256), T).
@@ -628,15 +814,30 @@ __global__ void k_wait_probe(unsigned* status, long long limit) {
 
 inline int ok_or_fail() { return cudaPeekAtLastError() == cudaSuccess ? 1 : -1; }
 
+// Warps per tile: split K when the expert work alone cannot fill the GPU
+// (batch-1 decode runs only top_k experts per layer).
+int pick_ksplit(int tiles_total) {
+    // Measured on B200 at batch 1 (GPT-OSS and Qwen3 shapes): the best split is
+    // the largest that keeps the launch under ~3072 warps (~20 per SM) — more
+    // warps only add partial-sum reductions and per-CTA x staging.
+    int ks = 1;
+    while (ks < kGemvWarps && tiles_total * ks * 2 < 3072) ks *= 2;
+    return ks;
+}
+
 }  // namespace
 
-// Dynamic shared bytes of k_gemv for `cols`-wide inputs (one staged x row).
-size_t gemv_smem_bytes(int cols) {
-    return (size_t)(cols / 32 + 1) * kXBlockHalves * sizeof(__half);
+// Dynamic shared bytes of the expert kernels for `cols`-wide inputs.
+size_t gemv_smem_bytes(int cols, int max_tok) {
+    const size_t diag = (size_t)(cols / 32 + 1) * kXBlockHalves * sizeof(__half);
+    return (size_t)std::min(std::max(max_tok, 1), kChunk) * diag;
 }
 
 int configure_kernels() {
     const int max_smem = 64 * 1024;
+    if (cudaFuncSetAttribute(k_gateup<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem) != cudaSuccess) return -1;
+    if (cudaFuncSetAttribute(k_gateup<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem) != cudaSuccess) return -1;
+    if (cudaFuncSetAttribute(k_down, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem) != cudaSuccess) return -1;
     if (cudaFuncSetAttribute(k_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem) != cudaSuccess) return -1;
     return 0;
 }
@@ -658,6 +859,31 @@ int launch_router(const LayerView& L, const MoeDims& d, const void* x, int x_dty
 int launch_group(const MoeDims& d, const int32_t* experts_in, const float* weights_in, int T,
                  const MoeWork& w, cudaStream_t s) {
     k_group<<<1, 256, 0, s>>>(d, experts_in, weights_in, T, w);
+    return ok_or_fail();
+}
+
+int launch_gateup(const LayerView& L, const MoeDims& d, const void* x, int x_dtype, int T,
+                  const MoeWork& w, cudaStream_t s) {
+    const int maxa = min(d.E, T * d.k);
+    const int tiles = d.F / 8;
+    const int ks = pick_ksplit(tiles * maxa);
+    const int per = kGemvWarps / ks;
+    dim3 grid(maxa, (tiles + per - 1) / per);
+    const size_t sm = gemv_smem_bytes(d.H, T);
+    if (d.act == 0)
+        k_gateup<0><<<grid, kGemvWarps * 32, sm, s>>>(L, d, x, x_dtype, T, w, ks);
+    else
+        k_gateup<1><<<grid, kGemvWarps * 32, sm, s>>>(L, d, x, x_dtype, T, w, ks);
+    return ok_or_fail();
+}
+
+int launch_down(const LayerView& L, const MoeDims& d, int T, const MoeWork& w, cudaStream_t s) {
+    const int maxa = min(d.E, T * d.k);
+    const int tiles = d.H / 16;
+    const int ks = pick_ksplit(tiles * maxa);
+    const int per = kGemvWarps / ks;
+    dim3 grid(maxa, (tiles + per - 1) / per);
+    k_down<<<grid, kGemvWarps * 32, gemv_smem_bytes(d.F, T), s>>>(L, d, T, w, ks);
     return ok_or_fail();
 }
 
@@ -690,7 +916,7 @@ int launch_gemv_batched(int count, const uint8_t* packed, int64_t packed_stride,
     if (cudaPeekAtLastError() != cudaSuccess) return -1;
     const int tiles = (rows + 15) / 16;
     dim3 grid(count, (tiles + kGemvWarps - 1) / kGemvWarps);
-    k_gemv<<<grid, kGemvWarps * 32, gemv_smem_bytes(cols), s>>>(
+    k_gemv<<<grid, kGemvWarps * 32, gemv_smem_bytes(cols, 1), s>>>(
         packed, packed_stride, scales, scale_stride, bias, bias_stride, x16, xmul,
         x_stride == 0 ? 0 : 1, y, y_stride, rows, cols);
     return cudaPeekAtLastError() == cudaSuccess ? 2 : -1;

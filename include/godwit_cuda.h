@@ -321,11 +321,12 @@ GW_API gw_status gw_moe_block_async(gw_ctx* ctx, gw_bank* bank, int32_t layer, f
  * to the device's primary context: after a cudaDeviceReset of that device
  * this entry point must not be called again in the process.  All calls share
  * the array: calls that overlap on the GPU (other streams, other contexts of
- * the same device) race.  The experts always run on the MXFP4 GEMV tiles:
- * the context's expert-path switches (gw_set_tensor_core_min_tokens,
- * gw_set_block_scaled) do not apply here, so its
- * results equal gw_moe_forward_async's whenever that call runs the GEMV
- * tiles too (always at decode sizes under the default policy). */
+ * the same device) race.  The experts always run on the persistent MXFP4
+ * expert GEMV: the context's expert-path switches (gw_set_tensor_core_min_tokens,
+ * gw_set_block_scaled) and the small-batch GEMV tiles do not apply here, so
+ * its results equal gw_moe_forward_async's up to fp32 summation order
+ * whenever that call runs a GEMV path too (always at decode sizes under the
+ * default policy). */
 GW_API gw_status gw_moe_forward_noalloc_async(gw_ctx* ctx, gw_bank* bank, int32_t layer,
                                               const void* x_dev, int32_t x_dtype, int32_t T,
                                               float* out_dev, int32_t* experts_dev,
