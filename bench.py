@@ -332,7 +332,10 @@ def _barrier(world):
         dist.barrier()
 
 
-HOT_EXPERTS = (3, 17, 31, 45, 59, 73, 87, 101)
+# Config 4's hot experts: a contiguous block of ids, which the expert
+# parallelism's round-robin placement (rank e % N) spreads over the ranks at
+# N = 2, 4 and 8.
+HOT_EXPERTS = (8, 9, 10, 11, 12, 13, 14, 15)
 
 
 def skewed_router_bias(spec, x_f32, seed=SEED, target=4.0):

@@ -153,7 +153,7 @@ constexpr int kRouterSegs = (kMaxGemvCols + 255) / 256;  // 256-value hidden seg
 // chunk's tokens and adds their slots to the expert lists (whose counts the
 // previous combine left at zero).
 template <int kRouterWarps, int kEpc>
-__global__ void __launch_bounds__(kRouterWarps * 32) k_router(LayerView L, MoeDims d, const void* __restrict__ xr,
+__global__ void __launch_bounds__(kRouterWarps * 32, kRouterWarps == 4 ? 6 : 1) k_router(LayerView L, MoeDims d, const void* __restrict__ xr,
                                                 int x_dtype, int T, MoeWork w) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int e0 = blockIdx.x * kEpc;
@@ -182,14 +182,19 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router(LayerView L, MoeDi
 #pragma unroll
         for (int q = 0; q < kTokTile; ++q) acc[q] = 0.f;
         if (c < nchunk) {
+            // every load of the segment first (they are independent), then the math
             const uint4 wv = __ldg(wrow + c);
+            uint4 xs[kTokTile];
+#pragma unroll
+            for (int q = 0; q < kTokTile; ++q)
+                xs[q] = t0 + q < t1 ? __ldg(reinterpret_cast<const uint4*>(static_cast<const char*>(xr) +
+                                                                          (int64_t)(t0 + q) * d.H * 2) + c)
+                                    : make_uint4(0u, 0u, 0u, 0u);
             const uint32_t wr[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
             for (int q = 0; q < kTokTile; ++q) {
                 if (t0 + q >= t1) break;
-                const uint4 xv = __ldg(reinterpret_cast<const uint4*>(
-                                           static_cast<const char*>(xr) + (int64_t)(t0 + q) * d.H * 2) + c);
-                const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
+                const uint32_t xx[4] = {xs[q].x, xs[q].y, xs[q].z, xs[q].w};
 #pragma unroll
                 for (int v = 0; v < 4; ++v) {
                     float x0, x1;
