@@ -187,14 +187,16 @@ __device__ __forceinline__ void group_mma(const unsigned char* A, int astep, con
     };
     const unsigned char* rowA = A + (kFull ? g * 128 : g * 16 * w) + 4 * t;
     const int rowB = kFull ? 8 * 128 : 8 * 16 * w;  // row g + 8, relative to row g
-    float d0[kNT][4], d1[kNT][4];
+    // one accumulator per tile: the block's second MMA adds into its first's
+    // result (the pair's partial sums are then one register, not two to add)
+    float d[kNT][4];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         if (!kFull && j % kBlk == 0) {  // a narrow group may end before its window does
 #pragma unroll
             for (int ti = 0; ti < kNT; ++ti)
 #pragma unroll
-                for (int q = 0; q < 4; ++q) d0[ti][q] = d1[ti][q] = 0.f;
+                for (int q = 0; q < 4; ++q) d[ti][q] = 0.f;
         }
         if (kFull || j < wl) {
             const uint4 xv = ld128(xg + j * 512);
@@ -206,13 +208,11 @@ __device__ __forceinline__ void group_mma(const unsigned char* A, int astep, con
                 uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
                 e2m1x8_to_f16x8(wa, a0, a1, a2, a3);
                 e2m1x8_to_f16x8(wb, b0, b1, b2, b3);
-                if (kFull && j % kBlk == 0) {  // the window's first block starts the accumulators
-                    mma_f16_z(d0[ti], a0, b0, a1, b1, xv.x, xv.y);
-                    mma_f16_z(d1[ti], a2, b2, a3, b3, xv.z, xv.w);
-                } else {
-                    mma_f16(d0[ti], a0, b0, a1, b1, xv.x, xv.y);
-                    mma_f16(d1[ti], a2, b2, a3, b3, xv.z, xv.w);
-                }
+                if (kFull && j % kBlk == 0)  // the window's first block starts the accumulator
+                    mma_f16_z(d[ti], a0, b0, a1, b1, xv.x, xv.y);
+                else
+                    mma_f16(d[ti], a0, b0, a1, b1, xv.x, xv.y);
+                mma_f16(d[ti], a2, b2, a3, b3, xv.z, xv.w);
             }
         }
         if (j % kBlk == kBlk - 1) {  // flush the window of blocks [j - kBlk + 1, j]
@@ -220,17 +220,17 @@ __device__ __forceinline__ void group_mma(const unsigned char* A, int astep, con
 #pragma unroll
             for (int ti = 0; ti < kNT; ++ti) {
                 if (kTok == 1) {  // columns 2t, 2t + 1 = blocks 2t, 2t + 1
-                    acc[ti][0][0] = fmaf(d0[ti][0] + d1[ti][0], scale(ti, g, 2 * t), acc[ti][0][0]);
-                    acc[ti][0][0] = fmaf(d0[ti][1] + d1[ti][1], scale(ti, g, 2 * t + 1), acc[ti][0][0]);
-                    acc[ti][1][0] = fmaf(d0[ti][2] + d1[ti][2], scale(ti, g + 8, 2 * t), acc[ti][1][0]);
-                    acc[ti][1][0] = fmaf(d0[ti][3] + d1[ti][3], scale(ti, g + 8, 2 * t + 1), acc[ti][1][0]);
+                    acc[ti][0][0] = fmaf(d[ti][0], scale(ti, g, 2 * t), acc[ti][0][0]);
+                    acc[ti][0][0] = fmaf(d[ti][1], scale(ti, g, 2 * t + 1), acc[ti][0][0]);
+                    acc[ti][1][0] = fmaf(d[ti][2], scale(ti, g + 8, 2 * t), acc[ti][1][0]);
+                    acc[ti][1][0] = fmaf(d[ti][3], scale(ti, g + 8, 2 * t + 1), acc[ti][1][0]);
                 } else {  // columns 2t, 2t + 1 share one block
                     const int bi = jb + (kTok == 2 ? t : kTok == 4 ? (t >> 1) : 0);
                     const float fa = scale(ti, g, bi), fb = scale(ti, g + 8, bi);
-                    acc[ti][0][0] = fmaf(d0[ti][0] + d1[ti][0], fa, acc[ti][0][0]);
-                    acc[ti][0][1] = fmaf(d0[ti][1] + d1[ti][1], fa, acc[ti][0][1]);
-                    acc[ti][1][0] = fmaf(d0[ti][2] + d1[ti][2], fb, acc[ti][1][0]);
-                    acc[ti][1][1] = fmaf(d0[ti][3] + d1[ti][3], fb, acc[ti][1][1]);
+                    acc[ti][0][0] = fmaf(d[ti][0], fa, acc[ti][0][0]);
+                    acc[ti][0][1] = fmaf(d[ti][1], fa, acc[ti][0][1]);
+                    acc[ti][1][0] = fmaf(d[ti][2], fb, acc[ti][1][0]);
+                    acc[ti][1][1] = fmaf(d[ti][3], fb, acc[ti][1][1]);
                 }
             }
         }
