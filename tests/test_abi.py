@@ -69,6 +69,12 @@ def test_null_arguments_rejected_before_any_device_work():
     assert lib.gw_sync(None) == _abi.GW_E_ARG
     assert lib.gw_bank_destroy(None) == _abi.GW_E_ARG
     assert lib.gw_shutdown(None) == _abi.GW_E_ARG
+    assert lib.gw_int8_affine_gemv(None, None, None, None, None, 1, 16, 64, None, _abi.GW_DTYPE_F32) == _abi.GW_E_ARG
+    assert lib.gw_int8_affine_gemv_async(None, None, None, None, None, 1, 16, 64, None,
+                                         _abi.GW_DTYPE_F32) == _abi.GW_E_ARG
+    assert lib.gw_ep_dispatch_async(None, None, None, 0, 1, None, None, 2, 4, None, None, None) == _abi.GW_E_ARG
+    assert lib.gw_ep_combine_async(None, None, None, None, 1, None) == _abi.GW_E_ARG
+    assert lib.gw_moe_forward_noalloc_async(None, None, 0, None, 0, 1, None, None, None) == _abi.GW_E_ARG
 
 
 def test_synthetic_hash_generator_is_deterministic_and_in_range():
