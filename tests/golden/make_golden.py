@@ -12,6 +12,11 @@ expert_reference.py:68-74 (which lives inside its main()) with those
 functions.  Inputs are seeded synthetic MXFP4 experts (codes uniform 0..15,
 scales 118..124, bf16 biases ~N(0, 0.02)) and x ~N(0, 0.5) in float16 as the
 reference's fixture builder draws it.
+
+reference_int8.npz: `int8_affine` of Scripts/analysis/qwen3_quant_quality.py
+(:104-110, the reference's NumPy statement of the trunk's affine int8 scheme)
+applied to seeded float32 weight rows, including a constant group and a
+group holding only two values.
 """
 import importlib.util
 import os
@@ -74,6 +79,20 @@ def main(ref_root):
             out[f"e{i}_{k}"] = v
     np.savez_compressed(os.path.join(HERE, "reference_numpy.npz"), **out)
     print("wrote", os.path.join(HERE, "reference_numpy.npz"))
+    main_int8(ref_root)
+
+
+def main_int8(ref_root):
+    # the module reads tensors over HTTP only from its main(); importing it
+    # defines the functions and touches no network
+    qq = load(os.path.join(ref_root, "Scripts/analysis/qwen3_quant_quality.py"), "qwen3_quant_quality")
+    rng = np.random.default_rng(20240611)
+    w = (rng.standard_normal((24, 256)) * 0.02).astype(np.float32)
+    w[3, 64:128] = 0.0125                      # a constant group
+    w[5, :64] = np.where(np.arange(64) % 2 == 0, -0.5, 0.25).astype(np.float32)  # two values
+    back = qq.int8_affine(w.copy(), group=64).astype(np.float32)
+    np.savez_compressed(os.path.join(HERE, "reference_int8.npz"), w=w, back=back)
+    print("wrote", os.path.join(HERE, "reference_int8.npz"))
 
 
 if __name__ == "__main__":

@@ -50,3 +50,26 @@ def test_expert_apply_matches_reference_numpy():
         assert np.max(np.abs(y - ref)) / np.mean(np.abs(ref)) < 5e-3
         y64 = O.expert64(spec, _stride(spec, i), x)
         assert O.rel_l2(y, y64) < 1e-4
+
+
+def test_int8_quantiser_matches_the_reference_numpy_scheme():
+    """Int8Affine.quantize as restated in the oracle (Install/Int8Affine.swift:31-58),
+    dequantised in float32, against `int8_affine` of the reference's
+    Scripts/analysis/qwen3_quant_quality.py:104-110 on the same rows
+    (tests/golden/reference_int8.npz).  The two statements differ only where
+    a level lands exactly on .5 (Swift rounds half away from zero, NumPy to
+    even) and in the scale a constant group gets (both give back the value)."""
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "reference_int8.npz"))
+    w, back = g["w"], g["back"]
+    ours = np.empty_like(w)
+    ties = np.zeros(w.shape, bool)
+    for r in range(w.shape[0]):
+        codes, scale, zero = O.int8_quantize_row(w[r])
+        s = np.repeat(scale, 64).astype(np.float32)
+        z = np.repeat(zero, 64).astype(np.float32)
+        ours[r] = codes.astype(np.float32) * s + z
+        level = (w[r] - z) / s
+        ties[r] = np.abs(level - np.floor(level) - 0.5) < 1e-6
+    same = ours.view(np.uint32) == back.view(np.uint32)
+    assert np.all(same | ties)
+    assert same.mean() > 0.999
