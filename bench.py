@@ -135,7 +135,7 @@ class CpuReference:
     on the host by the same counter hash as the device bank's, so the sample
     computes the workload's own layer."""
 
-    def __init__(self, spec, threads: int, max_tokens: int = 2048):
+    def __init__(self, spec, threads: int, max_tokens: int = 2048, router_bias=None):
         import numpy as np
 
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -146,7 +146,9 @@ class CpuReference:
         rng = np.random.default_rng(SEED)
         self.x = synth.as_f32(synth.make_hidden(rng, max_tokens, spec.hidden, "bf16"), "bf16")
         self.rw, rb = synth.hash_router(spec, SEED, 0)
-        self.rb = rb if spec.router_bias else None
+        if router_bias is not None:  # the prefill workload's skewed router
+            rb = router_bias
+        self.rb = rb if (spec.router_bias or router_bias is not None) else None
         self.strides = np.zeros((spec.experts, spec.layout().stride), np.uint8)
         self.ready = set()
         self.n = max(1, min(threads, max_tokens))
@@ -237,7 +239,20 @@ def run_reference(args, workload):
     preset, T, desc = WORKLOADS[workload]
     from godwit_b200.layout import PRESETS
     vals = []
-    ref = None if preset is None else CpuReference(PRESETS[preset], threads)
+    skew = None
+    if preset is None:
+        ref = None
+    elif workload == "oss120-prefill":
+        # the same skewed router as the GPU arm's prefill layer (config 4)
+        import numpy as np
+        from godwit_b200 import synth
+        spec = PRESETS[preset].with_(layers=1)
+        x0 = synth.make_hidden(np.random.default_rng(SEED), T, spec.hidden, "bf16")
+        rb, delta, h = skewed_router_bias(spec, synth.as_f32(x0, "bf16"))
+        skew = skew_record(delta, h)
+        ref = CpuReference(spec, threads, router_bias=rb)
+    else:
+        ref = CpuReference(PRESETS[preset], threads)
     if ref is not None:
         ref.calibrate(4.0)
     for i in range(args.warmup + args.steps):
@@ -255,7 +270,7 @@ def run_reference(args, workload):
     line = {"impl": "reference", "metric": metric, "value": value, "unit": unit,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": workload, "description": desc},
+            "config": workload_config(workload, args.gpus, args.ep, None, skew),
             "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port",
                              "sample": sample},
             "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0,
@@ -264,6 +279,38 @@ def run_reference(args, workload):
                     "restatement of its CPU path (oracle/mxfp4_oracle.c) on all host cores"}
     print(json.dumps(line), flush=True)
     return 0
+
+
+def workload_config(workload, world: int = 1, ep: str = "alltoall", layers: int | None = None,
+                    skew: dict | None = None) -> dict:
+    """The `config` object of a workload: the same in both arms of the
+    benchmark (facts of one run, such as fill times, go under "run")."""
+    preset, T, desc = WORKLOADS[workload]
+    if workload == "gemv":
+        return {"workload": "gemv", "rows": 2880, "cols": 2880, "copies": GEMV_COPIES,
+                "l2": f"{GEMV_COPIES} distinct copies = {GEMV_COPIES * GEMV_ALG / 1e9:.2f} GB > 4x L2 per launch"}
+    if workload == "int8-head":
+        alg = HEAD_ROWS * HEAD_COLS + HEAD_ROWS * (HEAD_COLS // 64) * 4 + HEAD_COLS * 2 + HEAD_ROWS * 4
+        return {"workload": "int8-head", "rows": HEAD_ROWS, "cols": HEAD_COLS, "tokens": 1,
+                "l2": f"{alg / 1e9:.2f} GB of weights per launch > L2"}
+    from godwit_b200.layout import PRESETS
+    spec = PRESETS[preset]
+    if workload == "oss120-prefill":
+        spec = spec.with_(layers=1)
+    if layers:
+        spec = spec.with_(layers=layers)
+    per = -(-T // world)
+    sliced = world > 1 and ep == "alltoall"
+    cfg = {"workload": workload,
+           "description": desc if not layers else f"{desc} (profiling run: {spec.layers} layers)",
+           "model_shape": spec.name, "layers": spec.layers, "experts": spec.experts, "top_k": spec.top_k,
+           "hidden": spec.hidden, "intermediate": spec.intermediate, "tokens": T,
+           "parallelism": (f"ep{world} ({'all-to-all, tokens sliced ' + str(per) + ' per rank' if sliced else 'replicated tokens, all-reduce per layer'})"
+                           if world > 1 else "single"),
+           "l2": "weights streamed per step >> 126 MB L2 (no flush needed)"}
+    if skew:
+        cfg["skew"] = skew
+    return cfg
 
 
 def metric_unit(workload):
@@ -338,6 +385,13 @@ def _barrier(world):
 HOT_EXPERTS = (8, 9, 10, 11, 12, 13, 14, 15)
 
 
+def skew_record(delta, h) -> dict:
+    import numpy as np
+    return {"hot_experts": list(HOT_EXPERTS), "delta": round(float(delta), 5),
+            "hot_mean_tokens": float(h[list(HOT_EXPERTS)].mean()),
+            "other_mean_tokens": float(np.delete(h, list(HOT_EXPERTS)).mean())}
+
+
 def skewed_router_bias(spec, x_f32, seed=SEED, target=4.0):
     """Config 4's deliberate skew: the router of layer 0 gets a bias offset
     delta on 8 fixed experts, found by bisection on these tokens so that the
@@ -404,9 +458,7 @@ def run_decode(args):
         rb, delta, h = skewed_router_bias(spec, synth.as_f32(xb, "bf16"))
         rw, _ = synth.hash_router(spec, SEED, 0)
         bank.upload_router(0, rw, rb)
-        skew = {"hot_experts": list(HOT_EXPERTS), "delta": round(float(delta), 5),
-                "hot_mean_tokens": float(h[list(HOT_EXPERTS)].mean()),
-                "other_mean_tokens": float(np.delete(h, list(HOT_EXPERTS)).mean())}
+        skew = skew_record(delta, h)
     # At N > 1 each rank holds a slice of the batch (token-sliced expert
     # parallelism, AllToAllEP: the experts of slot rows are applied by their
     # owner after an all-to-all, outputs return by a second one); with
@@ -567,17 +619,10 @@ def run_decode(args):
             "dtype": ("mxfp4 weights x mxfp8 (e4m3 + e8m0 per 32) activations, fp32 accumulate"
                       if block_scaled else "mxfp4 weights x bf16 activations, fp32 accumulate"),
             "data": "synthetic (seeded random-init bank, hidden ~N(0,1))",
-            "config": {"workload": args.workload, "description": desc if not args.layers else
-                       f"{desc} (profiling run: {spec.layers} layers)", "model_shape": spec.name,
-                       "layers": spec.layers, "experts": spec.experts, "top_k": spec.top_k,
-                       "hidden": spec.hidden, "intermediate": spec.intermediate, "tokens": T,
-                       "parallelism": (f"ep{world} ({'all-to-all, tokens sliced ' + str(per) + ' per rank' if sliced else 'replicated tokens, all-reduce per layer'})"
-                                       if world > 1 else "single"),
-                       "l2": "weights streamed per step >> 126 MB L2 (no flush needed)",
-                       "bank_fill_s": round(fill_s, 2), "bank_bytes": bank.nbytes(),
-                       **({"cuda_graph": graph is not None} if world > 1 else {}),
-                       **({"graph_note": graph_note} if graph_note else {}),
-                       **({"skew": skew} if skew else {})},
+            "config": workload_config(args.workload, world, args.ep, args.layers, skew),
+            "run": {"bank_fill_s": round(fill_s, 2), "bank_bytes": bank.nbytes(),
+                    **({"cuda_graph": graph is not None} if world > 1 else {}),
+                    **({"graph_note": graph_note} if graph_note else {})},
             "e2e": {"value": T / (e2e_ms / 1e3), "unit": unit, "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": Tr * H * 2, "d2h_bytes_per_step": Tr * H * 4},
             "gpu_launches": launches,
@@ -613,6 +658,8 @@ def run_decode(args):
 
 
 GEMV_ROUNDS = 7  # DequantGEMVBenchmark.swift:290-336: one warm-up, then the median of 7 rounds
+GEMV_ALG = 4_429_440  # config 0 bytes per GEMV: packed + scales + x + bias + y
+GEMV_COPIES = 128     # distinct matrices per batched launch (> 4x the 126 MB L2)
 
 
 def measure_gemv(ctx, cur, local: int, steps: int, warmup: int, world: int = 1,
@@ -628,9 +675,9 @@ def measure_gemv(ctx, cur, local: int, steps: int, warmup: int, world: int = 1,
     from godwit_b200 import synth
 
     rows = cols = 2880
-    alg = 4_429_440  # packed + scales + x + bias + y (config 0)
+    alg = GEMV_ALG
     l2 = torch.cuda.get_device_properties(local).L2_cache_size
-    R = max(128, (4 * l2) // alg + 1)
+    R = max(GEMV_COPIES, (4 * l2) // alg + 1)
     rng = np.random.default_rng(SEED)
     p0, s0 = synth.random_mxfp4(rng, rows, cols)
     x0 = synth.make_hidden(rng, 1, cols, "bf16")
@@ -690,9 +737,10 @@ def measure_gemv(ctx, cur, local: int, steps: int, warmup: int, world: int = 1,
         "rounds": GEMV_ROUNDS, "round_ms": [round(r, 4) for r in rounds],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "mxfp4 weights x bf16 x, fp32 accumulate", "data": "synthetic",
-        "config": {"workload": "gemv", "rows": rows, "cols": cols, "copies": R,
-                   "l2": f"{R} distinct copies = {R * alg / 1e9:.2f} GB > 4x L2 per launch",
-                   "protocol": f"warm-up, then median of {GEMV_ROUNDS} rounds of {steps} launches"},
+        "config": workload_config("gemv") if R == GEMV_COPIES else
+                  {"workload": "gemv", "rows": rows, "cols": cols, "copies": R,
+                   "l2": f"{R} distinct copies = {R * alg / 1e9:.2f} GB > 4x L2 per launch"},
+        "run": {"protocol": f"warm-up, then median of {GEMV_ROUNDS} rounds of {steps} launches"},
         "e2e": {"value": R * alg * world / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
                 "h2d_bytes_per_step": R * cols * 2, "d2h_bytes_per_step": R * rows * 4},
         "gpu_launches": launches,
@@ -798,9 +846,8 @@ def measure_int8_head(ctx, cur, local: int, steps: int, warmup: int, cpu_baselin
         "round_ms": [round(r, 4) for r in rounds], "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8 affine (bf16 scale/zero per 64) x f16, fp32 accumulate",
         "data": "synthetic",
-        "config": {"workload": "int8-head", "rows": rows, "cols": cols, "tokens": 1,
-                   "l2": f"{alg / 1e9:.2f} GB of weights per launch > L2",
-                   "protocol": f"warm-up, then median of {GEMV_ROUNDS} rounds of {steps} launches"},
+        "config": workload_config("int8-head"),
+        "run": {"protocol": f"warm-up, then median of {GEMV_ROUNDS} rounds of {steps} launches"},
         "e2e": {"value": alg / (e2e_ms / 1e3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": cols * 2,
                 "d2h_bytes_per_step": rows * 4},
         "gpu_launches": launches,
