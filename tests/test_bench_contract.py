@@ -43,3 +43,16 @@ def test_reference_arm_times_the_int8_head_port():
     assert d["impl"] == "reference" and d["config"]["workload"] == "int8-head"
     assert d["unit"] == "GB/s" and d["value"] > 0
     assert d["metric"] == "int8 affine head GEMV HBM GB/s"
+
+
+def test_both_arms_share_the_workload_config():
+    """The reference arm and the GPU arm describe a workload with the same
+    config object (workload_config), so the two lines compare like for like."""
+    sys.path.insert(0, ROOT)
+    import bench
+    for w in ("oss120-decode64", "oss20-decode1", "qwen3-decode32", "gemv", "int8-head"):
+        a, b = bench.workload_config(w, 1), bench.workload_config(w, 1)
+        assert a == b and a["workload"] == w
+    at2 = bench.workload_config("oss120-decode64", 2)
+    assert at2["parallelism"].startswith("ep2 (all-to-all") and at2["layers"] == 36
+    assert bench.workload_config("gemv")["copies"] == bench.GEMV_COPIES
